@@ -1,0 +1,461 @@
+"""CPU oracle for the SCAO optimizer step -- TEST INFRASTRUCTURE ONLY.
+
+This module restates, in float32 numpy, the reference algorithm of
+whispering3/scao for the optimizer-step hot path.  It exists to check the CUDA
+implementation in ``scao_b200``: only the test-suite, ``__graft_entry__.smoke``
+and the ``cpu_baseline`` / ``--impl reference`` legs of ``bench.py`` may import
+it.  The product path never calls into this file.
+
+Every function cites the reference file:line it follows (paths relative to the
+reference project root).  Its outputs are pinned against golden vectors
+produced by running the reference package itself
+(``tests/golden/make_golden.py`` -> ``tests/golden/*.npz``).
+
+Rounding points that the reference has and that matter for exact parity:
+  * the int8 requant uses true IEEE division x / float32(scale) and
+    round-half-even (``utils.py:187-188``), scale = float64(absmax) / 127;
+  * bf16 / fp16 parameters round after every parameter-dtype op
+    (``optimizer.py:549, 645``) and after ``precondition`` (``preconditioner.py:521``);
+  * the LARS ``p.norm()`` is a parameter-dtype 0-dim tensor (``optimizer.py:373``).
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+F32 = np.float32
+
+
+# ---------------------------------------------------------------------------
+# parameter-dtype emulation
+# ---------------------------------------------------------------------------
+
+def round_bf16(x):
+    """Round float32 values to the nearest bfloat16 (ties to even)."""
+    x = np.ascontiguousarray(x, dtype=F32)
+    b = x.view(np.uint32).astype(np.uint64)
+    nan = np.isnan(x)
+    lsb = (b >> 16) & 1
+    b = (b + 0x7FFF + lsb) & 0xFFFF0000
+    out = b.astype(np.uint32).view(F32).copy()
+    out[nan] = np.nan
+    return out
+
+
+def round_to(x, dtype):
+    """Cast float32 array ``x`` to the parameter dtype and back."""
+    if dtype == "float32":
+        return np.asarray(x, dtype=F32)
+    if dtype == "bfloat16":
+        return round_bf16(x)
+    if dtype == "float16":
+        return np.asarray(x, dtype=F32).astype(np.float16).astype(F32)
+    raise ValueError(dtype)
+
+
+def fma(a, b, c):
+    """float32 a*b + c with one rounding (torch CPU ``add_(x, alpha=)`` and
+    ``addcmul_`` contract to a fused multiply-add)."""
+    r = np.asarray(a, np.float64) * np.asarray(b, np.float64) + np.asarray(c, np.float64)
+    return r.astype(F32)
+
+
+def add_alpha(p, x, alpha, dtype):
+    """``p.add_(x, alpha=alpha)`` in the parameter dtype: torch casts alpha to
+    the tensor dtype first and evaluates with a fused multiply-add."""
+    a = F32(round_to(np.array([alpha], F32), dtype)[0])
+    return round_to(fma(a, x, p), dtype)
+
+
+def norm_f32(x):
+    """Frobenius norm with float32 output (torch ``Tensor.norm``)."""
+    x = np.asarray(x, dtype=F32)
+    return F32(np.sqrt(np.sum(np.square(x, dtype=np.float64))))
+
+
+# ---------------------------------------------------------------------------
+# utils.py
+# ---------------------------------------------------------------------------
+
+def quantize_sym_int8(x):
+    """utils.py:170-189.  Returns (int8 q, python-float scale)."""
+    x = np.asarray(x, dtype=F32)
+    abs_max = float(np.max(np.abs(x))) if x.size else 0.0
+    if abs_max < 1e-30:
+        return np.zeros(x.shape, np.int8), 1.0
+    scale = abs_max / 127.0
+    q = np.clip(np.rint(x / F32(scale)), -127, 127).astype(np.int8)
+    return q, scale
+
+
+def dequantize_sym_int8(q, scale):
+    """utils.py:192-203."""
+    return q.astype(F32) * F32(scale)
+
+
+def adaptive_rank(eigenvalues, epsilon=0.05, k_min=4, k_max=128):
+    """utils.py:121-151 (eigenvalues descending, float32)."""
+    ev = np.asarray(eigenvalues, dtype=F32)
+    total = float(np.sum(ev, dtype=F32))
+    if total < 1e-12:
+        return k_min
+    threshold = (1.0 - epsilon) * total
+    cumsum = np.cumsum(ev, dtype=F32)
+    idx = np.nonzero(cumsum >= F32(threshold))[0]
+    k = int(idx[0]) + 1 if idx.size > 0 else len(ev)
+    return int(min(k_max, max(k_min, k)))
+
+
+def to_2d(g):
+    """utils.py:208-219."""
+    if g.ndim == 1:
+        return g.reshape(1, -1)
+    if g.ndim == 2:
+        return g
+    return g.reshape(g.shape[0], -1)
+
+
+# ---------------------------------------------------------------------------
+# preconditioner.py
+# ---------------------------------------------------------------------------
+
+class OraclePreconditioner:
+    """preconditioner.py:72-644 (SparsePreconditioner), numpy float32."""
+
+    def __init__(self, shape, epsilon_sparse=0.05, k_min=8, k_max=128,
+                 rho=0.999, max_precond_dim=4096, use_int8_ema=False):
+        # preconditioner.py:108-124
+        shape = tuple(shape)
+        ndim = len(shape)
+        if ndim == 1:
+            m, n = 1, shape[0]
+        elif ndim == 2:
+            m, n = shape
+        else:
+            m, n = shape[0], int(np.prod(shape[1:]))
+        self.shape, self.m, self.n = shape, m, n
+        self.epsilon_sparse = epsilon_sparse
+        d_min = min(m, n)
+        self.k_min = min(k_min, d_min)
+        self.k_max = min(k_max, d_min // 2) if d_min > 2 * self.k_min else self.k_min
+        self.rho = rho
+        self.use_int8_ema = use_int8_ema
+        # preconditioner.py:142-153
+        self.use_block_diagonal = ndim >= 2 and m > 1 and n > 1 and max(m, n) > max_precond_dim
+        self.use_kronecker = ndim >= 2 and m > 1 and n > 1 and max(m, n) <= max_precond_dim
+        if self.use_block_diagonal:
+            # preconditioner.py:163-194
+            large, small = (m, n) if m >= n else (n, m)
+            self.block_dim = 0 if m >= n else 1
+            bs = max_precond_dim
+            self.block_sizes = [bs] * (large // bs) + ([large % bs] if large % bs else [])
+            self.blocks = []
+            for b in self.block_sizes:
+                fake = (b, small) if self.block_dim == 0 else (small, b)
+                self.blocks.append(OraclePreconditioner(
+                    fake, epsilon_sparse, k_min, k_max, rho, max_precond_dim,
+                    use_int8_ema))
+            self.k = self.blocks[0].k
+        elif self.use_kronecker:
+            # preconditioner.py:196-231
+            k_init = min(k_min, min(m, n))
+            self.k = k_init
+            L0 = np.eye(m, dtype=F32) * F32(1e-4)
+            R0 = np.eye(n, dtype=F32) * F32(1e-4)
+            if use_int8_ema:
+                self.L_q, self.L_scale = quantize_sym_int8(L0)
+                self.R_q, self.R_scale = quantize_sym_int8(R0)
+            else:
+                self.L, self.R = L0, R0
+            self.U_l = np.eye(m, k_init, dtype=F32)
+            self.S_l = np.ones(k_init, F32)
+            self.U_r = np.eye(n, k_init, dtype=F32)
+            self.S_r = np.ones(k_init, F32)
+        else:
+            # preconditioner.py:232-236
+            self.diag_ema = np.zeros(shape, F32)
+            self.diag_bias = 1e-8
+            self.k = 1
+        self.precond_step = 0
+
+    # -- iteration over leaf blocks (row/col slices of the 2-D gradient) ---
+    def _slices(self):
+        off = 0
+        for bs, blk in zip(self.block_sizes, self.blocks):
+            sl = (slice(off, off + bs), slice(None)) if self.block_dim == 0 else \
+                 (slice(None), slice(off, off + bs))
+            yield sl, blk
+            off += bs
+
+    def update_curvature(self, grad):
+        """preconditioner.py:297-361."""
+        self.precond_step += 1
+        g = to_2d(np.asarray(grad, dtype=F32))
+        if self.use_block_diagonal:
+            for sl, blk in self._slices():
+                blk.update_curvature(np.ascontiguousarray(g[sl]))
+            self.k = sum(b.k for b in self.blocks) // max(len(self.blocks), 1)
+            return
+        if not self.use_kronecker:
+            sq = g.reshape(self.diag_ema.shape)
+            self.diag_ema = self.diag_ema * F32(self.rho) + (F32(1.0 - self.rho) * (sq * sq))
+            self.diag_bias = max(1.0 - self.rho ** self.precond_step, 1e-8)
+            return
+        alpha = F32(1.0 - self.rho)
+        rho = F32(self.rho)
+        if self.use_int8_ema:
+            L = dequantize_sym_int8(self.L_q, self.L_scale) * rho + alpha * (g @ g.T)
+            self.L_q, self.L_scale = quantize_sym_int8(L)
+            R = dequantize_sym_int8(self.R_q, self.R_scale) * rho + alpha * (g.T @ g)
+            self.R_q, self.R_scale = quantize_sym_int8(R)
+        else:
+            self.L = self.L * rho + alpha * (g @ g.T)
+            self.R = self.R * rho + alpha * (g.T @ g)
+        self._update_eigenfactors(1.0 - self.rho ** self.precond_step)
+
+    def factor_matrices(self, bias_factor):
+        """L_reg, R_reg of preconditioner.py:383-406 (debias + Tikhonov)."""
+        eps = 1e-8
+        if self.use_int8_ema:
+            L = dequantize_sym_int8(self.L_q, self.L_scale)
+            R = dequantize_sym_int8(self.R_q, self.R_scale)
+        else:
+            L, R = self.L, self.R
+        L = L / F32(max(bias_factor, eps))
+        R = R / F32(max(bias_factor, eps))
+        eps_l = max(eps, 1e-4 * float(np.trace(L, dtype=F32)) / self.m)
+        eps_r = max(eps, 1e-4 * float(np.trace(R, dtype=F32)) / self.n)
+        L = L.copy()
+        R = R.copy()
+        L[np.diag_indices(self.m)] += F32(eps_l)
+        R[np.diag_indices(self.n)] += F32(eps_r)
+        return L, R
+
+    def _update_eigenfactors(self, bias_factor):
+        """preconditioner.py:363-451."""
+        L_reg, R_reg = self.factor_matrices(bias_factor)
+        S_l, U_l = np.linalg.eigh(L_reg)
+        S_r, U_r = np.linalg.eigh(R_reg)
+        S_l = np.clip(S_l[::-1], 0.0, None).astype(F32)
+        U_l = U_l[:, ::-1]
+        S_r = np.clip(S_r[::-1], 0.0, None).astype(F32)
+        U_r = U_r[:, ::-1]
+        self.S_l_full, self.S_r_full = S_l, S_r
+        k_l = adaptive_rank(S_l, self.epsilon_sparse, self.k_min, self.k_max)
+        k_r = adaptive_rank(S_r, self.epsilon_sparse, self.k_min, self.k_max)
+        k_new = min(k_l, k_r)
+        k_new = max(k_new, self.k - 1)
+        k_new = min(k_new, self.k + 4)
+        k_new = int(min(self.k_max, max(self.k_min, k_new)))
+        self.k = k_new
+        self.U_l = np.ascontiguousarray(U_l[:, :k_new], dtype=F32)
+        self.S_l = np.ascontiguousarray(S_l[:k_new])
+        self.U_r = np.ascontiguousarray(U_r[:, :k_new], dtype=F32)
+        self.S_r = np.ascontiguousarray(S_r[:k_new])
+
+    def precondition(self, grad, dtype="float32"):
+        """preconditioner.py:457-521 + cuda/__init__.py:95-99 (fp32 result
+        before the final cast; the caller rounds to the parameter dtype)."""
+        g = to_2d(np.asarray(grad, dtype=F32))
+        if self.use_block_diagonal:
+            out = np.zeros_like(g)
+            for sl, blk in self._slices():
+                out[sl] = blk.precondition(np.ascontiguousarray(g[sl]))
+            return round_to(out.reshape(self.shape), dtype)
+        if not self.use_kronecker:
+            denom = np.power(self.diag_ema / F32(self.diag_bias), F32(0.25)).reshape(g.shape) + F32(1e-8)
+            return round_to((g / denom).reshape(self.shape), dtype)
+        s_l = np.power(np.maximum(self.S_l, F32(1e-8)), F32(-0.25))
+        s_r = np.power(np.maximum(self.S_r, F32(1e-8)), F32(-0.25))
+        P = (self.U_l.T @ g) @ self.U_r
+        delta = (s_l[:, None] * s_r[None, :] - F32(1.0)) * P
+        out = g + (self.U_l @ delta) @ self.U_r.T
+        return round_to(out.reshape(self.shape), dtype)
+
+    def natural_grad_norm(self, grad, eps=1e-8):
+        """preconditioner.py:527-564 (float32 scalar)."""
+        g = to_2d(np.asarray(grad, dtype=F32))
+        if self.use_block_diagonal:
+            sq = [F32(blk.natural_grad_norm(np.ascontiguousarray(g[sl]), eps)) ** 2
+                  for sl, blk in self._slices()]
+            return F32(np.sqrt(np.sum(np.array(sq, F32), dtype=F32)))
+        if not self.use_kronecker:
+            denom = np.sqrt(self.diag_ema).reshape(g.shape) + F32(eps)
+            return F32(np.sqrt(np.sum(g * g / denom, dtype=F32)))
+        s_l = np.power(np.maximum(self.S_l, F32(eps)), F32(-0.5))
+        s_r = np.power(np.maximum(self.S_r, F32(eps)), F32(-0.5))
+        P = (self.U_l.T @ g) @ self.U_r
+        return norm_f32(s_l[:, None] * P * s_r[None, :])
+
+    def leaves(self):
+        """Leaf preconditioners in block order (self for non-split)."""
+        if self.use_block_diagonal:
+            out = []
+            for b in self.blocks:
+                out += b.leaves()
+            return out
+        return [self]
+
+
+# ---------------------------------------------------------------------------
+# optimizer.py
+# ---------------------------------------------------------------------------
+
+_DEFAULTS = dict(lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01,
+                 precond_freq=20, epsilon_sparse=0.05, k_min=8, k_max=128,
+                 rho=0.999, tau=1.0, warmup_steps=100, blend_steps=50,
+                 min_precond_updates=10, max_precond_dim=4096,
+                 use_int8_ema=False, beta3=0.99, lars_coeff=1e-3)
+
+
+class OracleSCAO:
+    """optimizer.py:221-645 restricted to the deterministic path
+    (sparsity=0, noise_std_init=0, no R1-R5 extensions), numpy float32.
+
+    ``params`` is a list of float32 arrays holding parameter-dtype values;
+    ``groups`` is a list of dicts {"params": [indices], **overrides}.
+    """
+
+    def __init__(self, params, dtype="float32", groups=None, lookahead_k=5,
+                 lookahead_alpha=0.5, **kw):
+        self.dtype = dtype
+        self.params = [round_to(np.array(p, dtype=F32), dtype) for p in params]
+        d = dict(_DEFAULTS)
+        for k in ("sparsity", "noise_std_init", "async_precond", "noise_anneal"):
+            kw.pop(k, None)
+        d.update(kw)
+        if groups is None:
+            groups = [{"params": list(range(len(params)))}]
+        self.groups = []
+        for g in groups:
+            gg = dict(d)
+            gg.update(g)
+            self.groups.append(gg)
+        self.state = {}
+        self.global_step = 0
+        self.global_norm_ema = 1.0
+        self.lookahead_k = lookahead_k
+        self.lookahead_alpha = lookahead_alpha
+        self.slow = {}
+
+    def _init_state(self, i, group):
+        """optimizer.py:407-433."""
+        if i in self.state:
+            return
+        p = self.params[i]
+        self.state[i] = dict(
+            step=0, scao_step=0, started=False,
+            m=np.zeros(p.shape, F32), v=np.zeros(p.shape, F32),
+            d=np.zeros(p.shape, F32), prev=np.zeros(p.shape, F32),
+            precond=OraclePreconditioner(
+                p.shape, group["epsilon_sparse"], group["k_min"], group["k_max"],
+                group["rho"], group["max_precond_dim"], group["use_int8_ema"]))
+
+    def step(self, grads):
+        """optimizer.py:452-503."""
+        self.global_step += 1
+        norms = [float(norm_f32(g)) for g in grads if g is not None]
+        if norms:
+            avg = sum(norms) / len(norms)
+            self.global_norm_ema = 0.95 * self.global_norm_ema + 0.05 * avg
+        for group in self.groups:
+            self._step_group(group, grads)
+        if self.lookahead_k > 0 and self.global_step % self.lookahead_k == 0:
+            self._lookahead_sync()
+
+    def _lookahead_sync(self):
+        """optimizer.py:356-365."""
+        a = F32(self.lookahead_alpha)
+        for group in self.groups:
+            for i in group["params"]:
+                p = self.params[i]
+                if i not in self.slow:
+                    self.slow[i] = p.copy()
+                s = self.slow[i]
+                s = round_to(s + round_to(a * round_to(p - s, self.dtype), self.dtype), self.dtype)
+                self.slow[i] = s
+                self.params[i] = s.copy()
+
+    def _step_group(self, group, grads):
+        """optimizer.py:509-645."""
+        dt = self.dtype
+        lr = group["lr"]
+        beta1, beta2 = group["betas"]
+        beta3 = group["beta3"]
+        eps = group["eps"]
+        wd = group["weight_decay"]
+        pf = group["precond_freq"]
+        tau = group["tau"]
+        lars = group["lars_coeff"]
+        for i in group["params"]:
+            gr = grads[i]
+            if gr is None:
+                continue
+            self._init_state(i, group)
+            st = self.state[i]
+            st["step"] += 1
+            step = st["step"]
+            raw = np.asarray(gr, dtype=F32)       # p.grad (param dtype values)
+            grad = raw
+            p = self.params[i]
+            if wd != 0.0:
+                p = round_to(p * F32(1.0 - lr * wd), dt)
+            m, v, d, prev = st["m"], st["v"], st["d"], st["prev"]
+            pc = st["precond"]
+            in_warmup = (step <= group["warmup_steps"]) or \
+                (pc.precond_step < group["min_precond_updates"])
+            if in_warmup:
+                m = fma(grad, F32(1.0 - beta1), m * F32(beta1))
+                v = fma(F32(1.0 - beta2) * grad, grad, v * F32(beta2))
+                bc1 = 1.0 - beta1 ** step
+                bc2 = 1.0 - beta2 ** step
+                denom = np.sqrt(v) / F32(math.sqrt(bc2)) + F32(eps)
+                if step % pf == 0:
+                    pc.update_curvature(raw)
+                p = add_alpha(p, round_to(m / denom, dt), -(lr / bc1), dt)
+                st.update(m=m, v=v, prev=grad.copy())
+                self.params[i] = p
+                continue
+            if not st["started"]:
+                st["started"] = True
+                st["scao_step"] = 0
+            st["scao_step"] += 1
+            sstep = st["scao_step"]
+            if step % pf == 0:
+                pc.update_curvature(raw)
+            gp = pc.precondition(raw, dt)
+            if tau is not None:
+                nat = pc.natural_grad_norm(raw, eps)
+                if nat > tau:
+                    gp = round_to(gp * (F32(tau) / max(nat, F32(eps))), dt)
+            bs = group["blend_steps"]
+            blend = min(1.0, sstep / bs) if bs > 0 else 1.0
+            g_eff = F32(blend) * gp + F32(1.0 - blend) * grad
+            delta = grad - prev
+            prev = grad.copy()
+            m = fma(g_eff, F32(1.0 - beta1), m * F32(beta1))
+            d = fma(delta, F32(1.0 - beta3), d * F32(beta3))
+            g_adan = g_eff + F32(1.0 - beta3) * delta
+            v = fma(F32(1.0 - beta2) * g_adan, g_adan, v * F32(beta2))
+            bc1 = 1.0 - beta1 ** step
+            bc2 = 1.0 - beta2 ** step
+            bc3 = 1.0 - beta3 ** step
+            upd = (m / F32(bc1) + F32(1.0 - beta3) * (d / F32(bc3))) / \
+                (np.sqrt(v / F32(bc2)) + F32(eps))
+            trust = self._lars(p, upd, lars, wd) if lars > 0 else 1.0
+            p = add_alpha(p, round_to(upd, dt), -(lr * trust), dt)
+            st.update(m=m, v=v, d=d, prev=prev)
+            self.params[i] = p
+
+    def _lars(self, p, upd, lars, wd):
+        """optimizer.py:371-377 with parameter-dtype scalar roundings."""
+        dt = self.dtype
+        pn = F32(round_to(np.array([norm_f32(p)], F32), dt)[0])
+        un = norm_f32(upd)
+        if pn == 0 or un == 0:
+            return 1.0
+        num = F32(round_to(np.array([F32(lars) * pn], F32), dt)[0])
+        wdp = F32(round_to(np.array([F32(wd) * pn], F32), dt)[0])
+        den = F32(F32(un + wdp) + F32(1e-8))
+        return float(F32(num / den))

@@ -1,0 +1,155 @@
+"""Generate the golden fixtures in this folder by running the REFERENCE package.
+
+Usage (needs the reference source tree, which only exists where fixtures are
+made; the fixtures themselves are committed and travel):
+
+    python tests/golden/make_golden.py --ref <path to whispering3/scao checkout>
+
+It imports ``scao`` from the reference checkout, runs the deterministic SCAO
+path (sparsity=0, noise_std_init=0, async_precond=False) on the ``tiny``
+workload of ``scao_b200.workloads`` with gradients from
+``scao_b200.synthetic``, and stores inputs checksums and outputs as .npz:
+
+  * quant.npz      -- ``utils.quantize_sym_int8`` on edge-case tensors
+  * rank.npz       -- ``utils.adaptive_rank`` on spectra incl. near-ties
+  * run_<case>.npz -- final params / moments / per-leaf preconditioner state
+                       and per-step ranks of a full optimizer run
+"""
+from __future__ import annotations
+
+import argparse
+import hashlib
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(HERE, "..", ".."))
+
+from scao_b200 import workloads, synthetic  # noqa: E402
+
+CASES = {
+    # name: (dtype, max_precond_dim, steps, grad_scale, int8 EMA)
+    "f32": ("float32", 4096, 40, 1e-2, True),
+    "bf16": ("bfloat16", 4096, 40, 1e-2, True),
+    "f32_blocks": ("float32", 48, 30, 1e-2, True),
+    "f32_spec": ("float32", 4096, 30, 1.0, False),
+    "int8_spec": ("float32", 48, 30, 1.0, True),
+    "bf16_spec": ("bfloat16", 48, 30, 1.0, True),
+}
+
+
+def grad_digest(grads):
+    h = hashlib.sha1()
+    for g in grads:
+        h.update(g.detach().float().contiguous().numpy().tobytes())
+    return h.hexdigest()
+
+
+def run_case(scao_mod, name, dtype, mpd, steps, gs, int8):
+    w = workloads.tiny(dtype=dtype, max_precond_dim=mpd, steps=steps,
+                       grad_scale=gs, int8=int8)
+    params0 = synthetic.init_params(w, seed=0)
+    params = [torch.nn.Parameter(p.clone()) for p in params0]
+    opt = scao_mod.SCAO(params, **w.scao_kwargs)
+    gen = synthetic.LowRankGradients(w, seed=0)
+    digests, ks = [], []
+    for t in range(steps):
+        grads = gen.next()
+        digests.append(grad_digest(grads))
+        for p, g in zip(params, grads):
+            p.grad = g.clone()
+        opt.step()
+        ks.append([opt.state[p]["preconditioner"].k for p in params])
+    out = {"steps": np.array(steps), "digests": np.array(digests),
+           "ks": np.array(ks, np.int32)}
+    for i, p in enumerate(params):
+        st = opt.state[p]
+        out[f"p{i}"] = p.detach().float().numpy()
+        for key in ("exp_avg", "exp_avg_sq", "exp_avg_diff", "prev_grad"):
+            out[f"{key}{i}"] = st[key].numpy()
+        pc = st["preconditioner"]
+        leaves = [pc] if not pc.use_block_diagonal else list(pc._blocks)
+        for j, lf in enumerate(leaves):
+            pre = f"leaf{i}_{j}_"
+            out[pre + "precond_step"] = np.array(lf.precond_step)
+            out[pre + "k"] = np.array(lf.k)
+            if lf.use_kronecker and lf.use_int8_ema:
+                out[pre + "Lq"] = lf.L_ema_q.numpy()
+                out[pre + "Ls"] = np.array(lf.L_ema_scale, np.float64)
+                out[pre + "Rq"] = lf.R_ema_q.numpy()
+                out[pre + "Rs"] = np.array(lf.R_ema_scale, np.float64)
+            elif lf.use_kronecker:
+                out[pre + "L"] = lf.L_ema.numpy()
+                out[pre + "R"] = lf.R_ema.numpy()
+            if lf.use_kronecker:
+                for key in ("U_l", "S_l", "U_r", "S_r"):
+                    out[pre + key] = getattr(lf, key).numpy()
+            else:
+                out[pre + "diag_ema"] = lf.diag_ema.numpy()
+    np.savez_compressed(os.path.join(HERE, f"run_{name}.npz"), **out)
+    print("wrote", name)
+
+
+def quant_cases(utils):
+    g = torch.Generator().manual_seed(1234)
+    xs = {
+        "randn": torch.randn(64, 64, generator=g),
+        "tiny_scale": torch.randn(32, 32, generator=g) * 1e-6,
+        "zeros": torch.zeros(16, 16),
+        "below_floor": torch.full((8, 8), 1e-31),
+        "eye": torch.eye(48) * 1e-4,
+        "ema_like": torch.eye(40) * 0.999e-4 + torch.randn(40, 40, generator=g) * 3e-7,
+        # values placed exactly on half-code boundaries of scale 1/127
+        "ties": (torch.arange(-254, 255, dtype=torch.float32) / 254.0).reshape(1, -1),
+        "huge": torch.randn(17, 33, generator=g) * 1e30,
+    }
+    out = {}
+    for k, x in xs.items():
+        q, s = utils.quantize_sym_int8(x.clone())
+        out[k + "_x"] = x.numpy()
+        out[k + "_q"] = q.numpy()
+        out[k + "_s"] = np.array(s, np.float64)
+        out[k + "_deq"] = utils.dequantize_sym_int8(q, s).numpy()
+    np.savez_compressed(os.path.join(HERE, "quant.npz"), **out)
+    print("wrote quant")
+
+
+def rank_cases(utils):
+    g = torch.Generator().manual_seed(99)
+    specs = []
+    for i in range(24):
+        n = [16, 64, 200, 1024][i % 4]
+        ev = torch.rand(n, generator=g).pow(6 + i % 5).sort(descending=True).values
+        specs.append((ev, 0.05, 4, 64))
+    specs.append((torch.zeros(32), 0.05, 4, 16))
+    specs.append((torch.full((50,), 0.5), 0.05, 3, 20))
+    specs.append((torch.tensor([1.0, 0.0, 0.0, 0.0]), 0.05, 1, 4))
+    out = {}
+    for i, (ev, e, kmin, kmax) in enumerate(specs):
+        out[f"ev{i}"] = ev.numpy()
+        out[f"args{i}"] = np.array([e, kmin, kmax], np.float64)
+        out[f"k{i}"] = np.array(utils.adaptive_rank(ev, e, kmin, kmax))
+    out["n"] = np.array(len(specs))
+    np.savez_compressed(os.path.join(HERE, "rank.npz"), **out)
+    print("wrote rank")
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", required=True, help="reference checkout root")
+    a = ap.parse_args()
+    sys.path.insert(0, a.ref)
+    import scao  # noqa: E402  (the reference package)
+    from scao import utils  # noqa: E402
+    torch.set_num_threads(min(8, os.cpu_count() or 1))
+    quant_cases(utils)
+    rank_cases(utils)
+    for name, args in CASES.items():
+        run_case(scao, name, *args)
+
+
+if __name__ == "__main__":
+    main()

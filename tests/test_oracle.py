@@ -1,0 +1,95 @@
+"""Pin the numpy oracle against golden vectors produced by the reference
+package itself (tests/golden/make_golden.py).  CPU only."""
+import numpy as np
+import pytest
+
+from golden_util import CASES, load, principal_angle, rel_err
+from oracle import scao_oracle as O
+from scao_b200 import synthetic, workloads
+
+
+def test_quant_golden_bit_exact():
+    g = load("quant")
+    names = sorted({k[:-2] for k in g if k.endswith("_x")})
+    assert len(names) >= 8
+    for n in names:
+        q, s = O.quantize_sym_int8(g[n + "_x"])
+        assert np.array_equal(q, g[n + "_q"]), n
+        assert s == float(g[n + "_s"]), n
+        assert np.array_equal(O.dequantize_sym_int8(q, s), g[n + "_deq"]), n
+
+
+def test_adaptive_rank_golden():
+    g = load("rank")
+    for i in range(int(g["n"])):
+        e, kmin, kmax = g[f"args{i}"]
+        assert O.adaptive_rank(g[f"ev{i}"], e, int(kmin), int(kmax)) == int(g[f"k{i}"]), i
+
+
+def test_bf16_rounding_matches_torch():
+    import torch
+    x = torch.randn(10000, generator=torch.Generator().manual_seed(3)) * 7
+    ref = x.bfloat16().float().numpy()
+    assert np.array_equal(O.round_bf16(x.numpy()), ref)
+
+
+def run_oracle(name):
+    dt, mpd, steps, gs, i8 = CASES[name]
+    w = workloads.tiny(dtype=dt, max_precond_dim=mpd, steps=steps,
+                       grad_scale=gs, int8=i8)
+    p0 = [p.float().numpy() for p in synthetic.init_params(w)]
+    opt = O.OracleSCAO(p0, dtype=dt, **w.scao_kwargs)
+    gen = synthetic.LowRankGradients(w)
+    ks = []
+    for _ in range(steps):
+        opt.step([g.float().numpy() for g in gen.next()])
+        ks.append([opt.state[i]["precond"].k for i in range(len(p0))])
+    return p0, opt, np.array(ks)
+
+
+@pytest.mark.parametrize("name", list(CASES))
+def test_oracle_matches_reference_run(name):
+    G = load("run_" + name)
+    p0, opt, ks = run_oracle(name)
+    assert np.array_equal(ks, G["ks"])
+    for i in range(len(p0)):
+        st = opt.state[i]
+        # Parameter update and moments: relative L2 <= 1e-3 is the parity
+        # bar; the oracle sits orders of magnitude inside it.
+        assert rel_err(opt.params[i] - p0[i], G[f"p{i}"] - p0[i]) < 1e-4
+        assert rel_err(st["m"], G[f"exp_avg{i}"]) < 1e-4
+        assert rel_err(st["v"], G[f"exp_avg_sq{i}"]) < 1e-4
+        assert rel_err(st["d"], G[f"exp_avg_diff{i}"]) < 1e-4
+        for j, lf in enumerate(st["precond"].leaves()):
+            pre = f"leaf{i}_{j}_"
+            assert lf.k == int(G[pre + "k"])
+            assert lf.precond_step == int(G[pre + "precond_step"])
+            if not lf.use_kronecker:
+                assert rel_err(lf.diag_ema, G[pre + "diag_ema"]) < 1e-5
+                continue
+            if lf.use_int8_ema:
+                assert np.array_equal(lf.L_q, G[pre + "Lq"])
+                assert np.array_equal(lf.R_q, G[pre + "Rq"])
+                assert lf.L_scale == float(G[pre + "Ls"])
+                assert lf.R_scale == float(G[pre + "Rs"])
+            assert principal_angle(lf.U_l, G[pre + "U_l"]) < 1e-3
+            assert principal_angle(lf.U_r, G[pre + "U_r"]) < 1e-3
+            assert rel_err(lf.S_l, G[pre + "S_l"]) < 1e-5
+            assert rel_err(lf.S_r, G[pre + "S_r"]) < 1e-5
+
+
+def test_grad_generator_is_reproducible():
+    """The fixtures store per-step gradient digests: the generator in this
+    tree must reproduce the reference run's inputs bit-for-bit."""
+    import hashlib
+    for name in ("f32", "bf16_spec"):
+        dt, mpd, steps, gs, i8 = CASES[name]
+        G = load("run_" + name)
+        w = workloads.tiny(dtype=dt, max_precond_dim=mpd, steps=steps,
+                           grad_scale=gs, int8=i8)
+        gen = synthetic.LowRankGradients(w)
+        for t in range(3):
+            h = hashlib.sha1()
+            for g in gen.next():
+                h.update(g.float().contiguous().numpy().tobytes())
+            assert h.hexdigest() == str(G["digests"][t])
