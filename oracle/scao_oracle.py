@@ -101,7 +101,8 @@ def adaptive_rank(eigenvalues, epsilon=0.05, k_min=4, k_max=128):
     if total < 1e-12:
         return k_min
     threshold = (1.0 - epsilon) * total
-    cumsum = np.cumsum(ev, dtype=F32)
+    # torch's CPU cumsum accumulates in float64 and rounds each prefix
+    cumsum = np.cumsum(ev.astype(np.float64)).astype(F32)
     idx = np.nonzero(cumsum >= F32(threshold))[0]
     k = int(idx[0]) + 1 if idx.size > 0 else len(ev)
     return int(min(k_max, max(k_min, k)))

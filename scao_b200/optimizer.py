@@ -1,0 +1,435 @@
+"""SCAO optimizer facade (drop-in for ``scao.SCAO``, scao/optimizer.py:221-801).
+
+The constructor keyword arguments, their defaults, the validation errors, the
+per-group hyper-parameters, ``step(closure)``, callbacks, ``state_dict`` /
+``load_state_dict`` schema and the diagnostics are those of the reference.
+Behind ``step()`` the per-parameter Python loop is replaced by a fixed
+sequence of batched sm_100a kernels (libscao_b200.so) covering every
+parameter: the host only decides phases and per-parameter scalars, writes a
+step table and launches.  There is no CPU path: parameters must be CUDA
+tensors and the library must be built.
+"""
+from __future__ import annotations
+
+import math
+from typing import Callable, Iterable
+
+import numpy as np
+import torch
+from torch.optim import Optimizer
+
+from . import _lib
+from .plan import Plan
+from .preconditioner import PrecondView
+
+_UNSUPPORTED = {
+    "dynamic_sparsity": False, "adaptive_warmup": False, "lazy_precond": False,
+    "use_gsnr_clip": False, "adaptive_rank": False,
+}
+
+
+class SCAO(Optimizer):
+    """B200-native SCAO.  Same signature and defaults as the reference
+    (optimizer.py:258-296)."""
+
+    def __init__(
+        self,
+        params: Iterable,
+        lr: float = 1e-3,
+        betas: tuple = (0.9, 0.999),
+        eps: float = 1e-8,
+        weight_decay: float = 0.01,
+        precond_freq: int = 20,
+        epsilon_sparse: float = 0.05,
+        k_min: int = 8,
+        k_max: int = 128,
+        rho: float = 0.999,
+        tau: float | None = 1.0,
+        warmup_steps: int = 100,
+        blend_steps: int = 50,
+        min_precond_updates: int = 10,
+        max_precond_dim: int = 4096,
+        use_newton_schulz: bool = False,
+        use_int8_ema: bool = False,
+        async_precond: bool = True,
+        beta3: float = 0.99,
+        sparsity: float = 0.7,
+        noise_std_init: float = 0.01,
+        noise_anneal: float = 0.998,
+        lars_coeff: float = 1e-3,
+        lookahead_k: int = 5,
+        lookahead_alpha: float = 0.5,
+        dynamic_sparsity: bool = False,
+        adaptive_warmup: bool = False,
+        warmup_stability_threshold: float = 0.05,
+        warmup_patience: int = 5,
+        lazy_precond: bool = False,
+        lazy_delta_threshold: float = 0.1,
+        lazy_max_skip: int = 50,
+        use_gsnr_clip: bool = False,
+        gsnr_threshold: float = 0.5,
+        adaptive_rank: bool = False,
+        eig_max_iters: int = 30,
+        eig_tol: float = 2e-5,
+    ) -> None:
+        # optimizer.py:297-304
+        if lr < 0:
+            raise ValueError(f"Invalid lr: {lr}")
+        if not (0.0 <= betas[0] < 1.0):
+            raise ValueError(f"Invalid beta1: {betas[0]}")
+        if not (0.0 <= betas[1] < 1.0):
+            raise ValueError(f"Invalid beta2: {betas[1]}")
+        if not (0.0 <= beta3 < 1.0):
+            raise ValueError(f"Invalid beta3: {beta3}")
+        defaults = dict(
+            lr=lr, betas=betas, eps=eps, weight_decay=weight_decay,
+            precond_freq=precond_freq, epsilon_sparse=epsilon_sparse,
+            k_min=k_min, k_max=k_max, rho=rho, tau=tau,
+            warmup_steps=warmup_steps, blend_steps=blend_steps,
+            min_precond_updates=min_precond_updates,
+            max_precond_dim=max_precond_dim, use_newton_schulz=use_newton_schulz,
+            use_int8_ema=use_int8_ema, beta3=beta3, lars_coeff=lars_coeff,
+        )
+        super().__init__(params, defaults)
+        self._callbacks: list = []
+        self._global_step = 0
+        self._noise_std = noise_std_init
+        self._noise_anneal = noise_anneal
+        self._lookahead_k = lookahead_k
+        self._lookahead_alpha = lookahead_alpha
+        self._lookahead_init = False
+        self._sparsity = sparsity
+        self._opts = dict(dynamic_sparsity=dynamic_sparsity, adaptive_warmup=adaptive_warmup,
+                          lazy_precond=lazy_precond, use_gsnr_clip=use_gsnr_clip,
+                          adaptive_rank=adaptive_rank)
+        self._warmup_cfg = (warmup_steps, warmup_stability_threshold, warmup_patience)
+        self._in_warmup_global = True
+        self._eig_max_iters = int(eig_max_iters)
+        self._eig_tol = float(eig_tol)
+        self._plan: Plan | None = None
+        self._ema_scratch = None
+        self._last_eig_status = None
+
+    # ------------------------------------------------------------------
+    # plan / state
+    # ------------------------------------------------------------------
+    def _flat(self):
+        ps, gs = [], []
+        for g in self.param_groups:
+            for p in g["params"]:
+                ps.append(p)
+                gs.append(g)
+        return ps, gs
+
+    def _build_plan(self):
+        ps, gs = self._flat()
+        if not ps:
+            return
+        dev = ps[0].device
+        if dev.type != "cuda":
+            raise RuntimeError("scao_b200.SCAO runs on CUDA tensors only (no CPU path)")
+        if any(p.device != dev for p in ps):
+            raise RuntimeError("all parameters must be on one CUDA device")
+        int8 = {bool(g["use_int8_ema"]) for g in gs}
+        if len(int8) != 1:
+            raise NotImplementedError("mixed use_int8_ema across param groups")
+        _lib.lib()
+        with torch.cuda.device(dev):
+            self._plan = Plan(ps, gs, dev, int8.pop())
+        for i, (p, g) in enumerate(zip(ps, gs)):
+            st = self.state[p]
+            st["step"] = 0
+            st["scao_step"] = 0
+            st["exp_avg"] = self._plan.state_view(self._plan.exp_avg, i)
+            st["exp_avg_sq"] = self._plan.state_view(self._plan.exp_avg_sq, i)
+            st["exp_avg_diff"] = self._plan.state_view(self._plan.exp_avg_diff, i)
+            st["prev_grad"] = self._plan.state_view(self._plan.prev_grad, i)
+            st["preconditioner"] = PrecondView(self._plan, i, g)
+
+    def _check_supported(self):
+        if self._sparsity > 0.0:
+            raise NotImplementedError(
+                "scao_b200: sparsity > 0 (the magnitude-EMA quantile mask, optimizer.py:42-57) "
+                "is not implemented on the device yet; pass sparsity=0")
+        if self._noise_std > 1e-9:
+            raise NotImplementedError(
+                "scao_b200: gradient noise (noise_std_init > 0, optimizer.py:544-545) is not "
+                "implemented on the device yet; pass noise_std_init=0")
+        for k, v in self._opts.items():
+            if v:
+                raise NotImplementedError(f"scao_b200: {k}=True is not implemented yet")
+
+    # ------------------------------------------------------------------
+    # step
+    # ------------------------------------------------------------------
+    @torch.no_grad()
+    def step(self, closure: Callable | None = None):
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+        self._check_supported()
+        if self._plan is None:
+            self._build_plan()
+            if self._plan is None:
+                return loss
+        plan = self._plan
+        L = _lib.lib()
+        if plan.step_event is not None:
+            plan.step_event.synchronize()   # previous table upload has left the pinned buffer
+        self._global_step += 1
+        ps, gs = self._flat()
+        tab = plan.step_np
+        curv_leaves: dict = {}
+        curv_diag: dict = {}
+        eig_leaves, eig_bias = [], []
+        keep = []
+        warm_max = max((g.get("warmup_steps", 100) for g in self.param_groups), default=100)
+        self._in_warmup_global = self._global_step <= warm_max
+        for i, (p, g) in enumerate(zip(ps, gs)):
+            row = tab[i]
+            row["p_ptr"] = p.data_ptr()
+            grad = p.grad
+            if grad is None:
+                row["phase"] = 0
+                continue
+            if grad.is_sparse:
+                raise RuntimeError("SCAO does not support sparse gradients.")
+            if grad.dtype != p.dtype or not grad.is_contiguous():
+                grad = grad.to(p.dtype).contiguous()
+                keep.append(grad)
+            if not p.is_contiguous():
+                raise RuntimeError("scao_b200 needs contiguous parameters")
+            st = self.state[p]
+            st["step"] += 1
+            step = st["step"]
+            pc = st["preconditioner"]
+            lr = float(g["lr"])
+            wd = float(g["weight_decay"])
+            b1, b2 = g["betas"]
+            b3 = g["beta3"]
+            in_warmup = (step <= g["warmup_steps"]) or (pc.precond_step < g["min_precond_updates"])
+            if step % g["precond_freq"] == 0:
+                pc.precond_step += 1
+                rho = float(g["rho"])
+                leaves = plan.param_leaves[i]
+                if leaves:
+                    curv_leaves.setdefault(rho, []).extend(leaves)
+                    bf = 1.0 - rho ** pc.precond_step
+                    eig_leaves.extend(leaves)
+                    eig_bias.extend([bf] * len(leaves))
+                else:
+                    curv_diag.setdefault(rho, []).append(i)
+            row["g_ptr"] = grad.data_ptr()
+            row["lr"] = lr
+            row["wd"] = wd
+            row["wd_mult"] = np.float32(1.0 - lr * wd) if wd != 0.0 else np.float32(1.0)
+            row["beta1"], row["beta2"], row["beta3"] = b1, b2, b3
+            row["c1"], row["c2"], row["c3"] = 1.0 - b1, 1.0 - b2, 1.0 - b3
+            row["eps"] = g["eps"]
+            row["lars"] = g["lars_coeff"]
+            row["diag_bias"] = pc.diag_bias
+            bc1 = 1.0 - b1 ** step
+            bc2 = 1.0 - b2 ** step
+            if in_warmup:
+                row["phase"] = 1
+                row["alpha1"] = -(lr / bc1)
+                row["sqrt_bc2"] = math.sqrt(bc2)
+                continue
+            row["phase"] = 2
+            if not st.get("scao_phase_started", False):
+                st["scao_phase_started"] = True
+                st["phase2_start_step"] = step
+                st["scao_step"] = 0
+            st["scao_step"] += 1
+            bs = g.get("blend_steps", 50)
+            blend = min(1.0, st["scao_step"] / bs) if bs > 0 else 1.0
+            row["blend"] = blend
+            row["one_minus_blend"] = 1.0 - blend
+            row["bc1"], row["bc2"], row["bc3"] = bc1, bc2, 1.0 - b3 ** step
+            tau = g["tau"]
+            row["clip"] = 0 if tau is None else 1
+            row["tau"] = 0.0 if tau is None else tau
+        dev = plan.device
+        stream = torch.cuda.current_stream(dev)
+        sp = C_stream(stream)
+        plan.t_step.copy_(plan.step_host, non_blocking=True)
+        plan.step_event = torch.cuda.Event()
+        plan.step_event.record(stream)
+        dptr = plan.dev
+        import ctypes
+        pd = ctypes.byref(dptr)
+        for rho, leaves in curv_leaves.items():
+            ids = torch.tensor(leaves, dtype=torch.int32, device=dev)
+            ma, mb, _ = plan.max_dims(leaves)
+            need = L.scao_ema_scratch_bytes(len(leaves), ma, mb)
+            scratch = self._get_ema_scratch(need)
+            _lib.check(L.scao_plan_curvature(pd, ids.data_ptr(), len(leaves), ma, mb, rho,
+                                             scratch.data_ptr(), scratch.numel(), sp),
+                       "scao_plan_curvature")
+            keep.append(ids)
+        for rho, pids in curv_diag.items():
+            ids = torch.tensor(pids, dtype=torch.int32, device=dev)
+            _lib.check(L.scao_plan_curvature_diag(pd, ids.data_ptr(), len(pids), rho, sp),
+                       "scao_plan_curvature_diag")
+            keep.append(ids)
+        if eig_leaves:
+            ids = torch.tensor(eig_leaves, dtype=torch.int32, device=dev)
+            bias = plan.t_bias
+            bias[ids.long()] = torch.tensor(eig_bias, dtype=torch.float32, device=dev)
+            ma, mb, smax = plan.max_dims(eig_leaves)
+            status = plan.eig_status[: 2 * len(eig_leaves)]
+            _lib.check(L.scao_plan_eigen(pd, ids.data_ptr(), len(eig_leaves), bias.data_ptr(),
+                                         plan.t_eps_sparse.data_ptr(), self._eig_max_iters,
+                                         self._eig_tol, status.data_ptr(), max(ma, mb), smax,
+                                         sp), "scao_plan_eigen")
+            self._last_eig_status = status
+            keep.append(ids)
+        _lib.check(L.scao_plan_step(pd, sp), "scao_plan_step")
+        self._noise_std *= self._noise_anneal
+        if self._lookahead_k > 0 and self._global_step % self._lookahead_k == 0:
+            plan.ensure_slow()
+            _lib.check(L.scao_plan_lookahead(pd, float(self._lookahead_alpha),
+                                             0 if self._lookahead_init else 1, sp),
+                       "scao_plan_lookahead")
+            self._lookahead_init = True
+        self._keep = keep   # keep temporaries alive until the next step
+        if self._callbacks:
+            metrics = self.collect_metrics()
+            for cb in self._callbacks:
+                cb(metrics)
+        return loss
+
+    def _get_ema_scratch(self, need):
+        cap = 2 << 30
+        need = min(int(need), cap)
+        if self._ema_scratch is None or self._ema_scratch.numel() < need:
+            self._ema_scratch = torch.empty(need, dtype=torch.uint8, device=self._plan.device)
+        return self._ema_scratch
+
+    # ------------------------------------------------------------------
+    # callbacks / diagnostics (optimizer.py:716-801, logging.py:151-220)
+    # ------------------------------------------------------------------
+    def add_callback(self, callback) -> None:
+        self._callbacks.append(callback)
+
+    def remove_callback(self, callback) -> None:
+        try:
+            self._callbacks.remove(callback)
+        except ValueError:
+            pass
+
+    def clear_callbacks(self) -> None:
+        self._callbacks.clear()
+
+    @property
+    def _global_norm_ema(self) -> float:
+        if self._plan is None:
+            return 1.0
+        return float(self._plan.global_norm_ema.item())
+
+    def collect_metrics(self) -> dict:
+        step = max((s.get("step", 0) for s in self.state.values()), default=0)
+        ranks = self.current_ranks()
+        m = {"step": step}
+        if ranks:
+            ks = list(ranks.values())
+            m["scao/rank_mean"] = sum(ks) / len(ks)
+            m["scao/rank_min"] = min(ks)
+            m["scao/rank_max"] = max(ks)
+            m["scao/layers"] = len(ks)
+        m["scao/precond_freq"] = self.param_groups[0].get("precond_freq", -1)
+        m["noise_std"] = self._noise_std
+        m["global_norm_ema"] = self._global_norm_ema
+        m["warmup_active"] = self._in_warmup_global
+        return m
+
+    def current_ranks(self) -> dict:
+        return {idx: st["preconditioner"].k for idx, st in enumerate(self.state.values())
+                if "preconditioner" in st}
+
+    def precond_stats(self) -> dict:
+        ks = list(self.current_ranks().values())
+        if not ks:
+            return {}
+        return {"num_precond_layers": len(ks), "rank_min": min(ks), "rank_max": max(ks),
+                "rank_mean": sum(ks) / len(ks), "global_norm_ema": self._global_norm_ema,
+                "warmup_exited_early": False,
+                "actual_warmup_steps": self._warmup_cfg[0]}
+
+    def synchronize_precond(self) -> None:
+        """Single-stream implementation: nothing is pending on a side stream."""
+        return None
+
+    # ------------------------------------------------------------------
+    # checkpoint (optimizer.py:732-776)
+    # ------------------------------------------------------------------
+    def state_dict(self) -> dict:
+        ps, _ = self._flat()
+        index = {id(p): i for i, p in enumerate(ps)}
+        packed = {}
+        precond = {}
+        for p, st in self.state.items():
+            i = index[id(p)]
+            d = {}
+            for k, v in st.items():
+                if k == "preconditioner":
+                    continue
+                d[k] = v.clone() if torch.is_tensor(v) else v
+            packed[i] = d
+            if "preconditioner" in st:
+                precond[i] = st["preconditioner"].state_dict()
+        groups = []
+        for g in self.param_groups:
+            gg = {k: v for k, v in g.items() if k != "params"}
+            gg["params"] = [index[id(p)] for p in g["params"]]
+            groups.append(gg)
+        return {
+            "state": packed,
+            "param_groups": groups,
+            "_scao_precond": precond,
+            "_scao_runtime": {
+                "global_step": self._global_step,
+                "noise_std": self._noise_std,
+                "global_norm_ema": self._global_norm_ema,
+                "warmup_prev_norm": float("inf"),
+                "warmup_stable_count": 0,
+                "warmup_early_exit_step": None,
+            },
+        }
+
+    def load_state_dict(self, state_dict: dict) -> None:
+        state_dict = dict(state_dict)
+        extra = state_dict.pop("_scao_precond", {})
+        runtime = state_dict.pop("_scao_runtime", {})
+        for g, sg in zip(self.param_groups, state_dict["param_groups"]):
+            for k, v in sg.items():
+                if k != "params":
+                    g[k] = v
+        if self._plan is None:
+            self._build_plan()
+        ps, _ = self._flat()
+        for i, p in enumerate(ps):
+            if i not in state_dict["state"]:
+                continue
+            src = state_dict["state"][i]
+            st = self.state[p]
+            for k, v in src.items():
+                if k == "preconditioner":
+                    continue
+                if torch.is_tensor(v) and k in st and torch.is_tensor(st[k]):
+                    st[k].copy_(v)
+                else:
+                    st[k] = v
+            if i in extra:
+                st["preconditioner"].load_state_dict(extra[i])
+        if runtime:
+            self._global_step = int(runtime.get("global_step", self._global_step))
+            self._noise_std = float(runtime.get("noise_std", self._noise_std))
+            if "global_norm_ema" in runtime:
+                self._plan.global_norm_ema.fill_(float(runtime["global_norm_ema"]))
+        self._lookahead_init = False
+
+
+def C_stream(stream):
+    return stream.cuda_stream

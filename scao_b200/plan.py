@@ -1,0 +1,307 @@
+"""Static execution plan: parameter/leaf/tile tables and device arenas.
+
+Built once on the first ``SCAO.step`` (scao/optimizer.py:407-433 initialises
+per-parameter state lazily in the same place).  Every Kronecker leaf block of
+the reference's recursive block-diagonal split (scao/preconditioner.py:142-194)
+becomes one row of the leaf table; moment buffers live in flat fp32 arenas so
+one kernel launch per phase covers every parameter.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import CHUNK_DT, LEAF_DT, PANEL_DT, PARAM_DT, STEP_DT, TILE_DT
+
+TILE = 64        # apply tile edge (apply.cu TT)
+PANEL = 64       # projection panel rows
+CHUNK = 4096     # flat chunk length
+SMAX = 160       # largest eigen subspace width (eig.cu SMAX)
+
+DTYPE_CODE = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16, torch.float16: _lib.F16}
+
+
+def to_2d_shape(shape):
+    """utils.py:208-219."""
+    if len(shape) == 1:
+        return 1, shape[0]
+    if len(shape) == 2:
+        return shape[0], shape[1]
+    n = 1
+    for d in shape[1:]:
+        n *= d
+    return shape[0], n
+
+
+def split_blocks(m, n, mpd):
+    """Leaf blocks (row0, col0, a, b) of the recursive block-diagonal split of
+    preconditioner.py:142-194.  Raises for remainder blocks of width 1, which
+    the reference turns into diagonal sub-preconditioners."""
+    if max(m, n) <= mpd:
+        return [(0, 0, m, n)]
+    large, small = (m, n) if m >= n else (n, m)
+    sizes = [mpd] * (large // mpd) + ([large % mpd] if large % mpd else [])
+    out, off = [], 0
+    for bs in sizes:
+        bm, bn = (bs, small) if m >= n else (small, bs)
+        if bm <= 1 or bn <= 1:
+            raise NotImplementedError(
+                f"block split of a {m}x{n} parameter at max_precond_dim={mpd} leaves a "
+                f"{bm}x{bn} block, which the reference preconditions diagonally; "
+                "not supported by scao_b200 yet")
+        for (r, c, a, b) in split_blocks(bm, bn, mpd):
+            out.append((r + off, c, a, b) if m >= n else (r, c + off, a, b))
+        off += bs
+    return out
+
+
+def _round_up(x, k):
+    return (x + k - 1) // k * k
+
+
+def k_bounds(m, n, k_min, k_max):
+    """preconditioner.py:122-124."""
+    d_min = min(m, n)
+    kmin = min(k_min, d_min)
+    kmax = min(k_max, d_min // 2) if d_min > 2 * kmin else kmin
+    return kmin, kmax
+
+
+def subspace_width(n, kpad):
+    if n <= SMAX:
+        return max(n, kpad)
+    return min(n, kpad + max(16, min(32, kpad // 2)))
+
+
+class Plan:
+    """Tables + device arenas for an ordered list of parameters."""
+
+    def __init__(self, params, groups_of, device, int8_ema):
+        self.params = params
+        self.device = device
+        self.int8_ema = bool(int8_ema)
+        self.n_params = len(params)
+        ptab = np.zeros(self.n_params, PARAM_DT)
+        leaves, tiles, panels, chunks = [], [], [], []
+        self.param_leaves = []
+        off = 0
+        fac_off = 0
+        u_off = 0
+        h_off = 0
+        ev_off = 0
+        w_off = 0
+        kpad_max = 0
+        self.eps_sparse = []
+        self.rho_leaf = []
+        for i, p in enumerate(params):
+            g = groups_of[i]
+            if p.dtype not in DTYPE_CODE:
+                raise TypeError(f"unsupported parameter dtype {p.dtype}")
+            m, n = to_2d_shape(tuple(p.shape))
+            numel = p.numel()
+            kron = p.dim() >= 2 and m > 1 and n > 1
+            r = ptab[i]
+            r["offset"] = off
+            r["numel"] = numel
+            r["rows"], r["cols"] = m, n
+            r["mode"] = 1 if kron else 0
+            r["dtype"] = DTYPE_CODE[p.dtype]
+            r["leaf_begin"] = len(leaves)
+            r["tile_begin"] = len(tiles)
+            r["chunk_begin"] = len(chunks)
+            mine = []
+            if kron:
+                blocks = split_blocks(m, n, g["max_precond_dim"])
+                for (r0, c0, a, b) in blocks:
+                    kmin, kmax = k_bounds(a, b, g["k_min"], g["k_max"])
+                    kpad = _round_up(max(kmax, 1), 8)
+                    if kpad > 128:
+                        raise NotImplementedError("k_max above 128 is not supported")
+                    kpad_max = max(kpad_max, kpad)
+                    sl, sr = subspace_width(a, kpad), subspace_width(b, kpad)
+                    L = np.zeros((), LEAF_DT)
+                    L["param"], L["row0"], L["col0"], L["a"], L["b"] = i, r0, c0, a, b
+                    L["ld"] = n
+                    L["kmin"], L["kmax"], L["kpad"], L["sl"], L["sr"] = kmin, kmax, kpad, sl, sr
+                    L["tile_begin"] = len(tiles)
+                    li = len(leaves)
+                    for tr in range(0, a, TILE):
+                        for tc in range(0, b, TILE):
+                            tiles.append((li, tr, tc, 0))
+                    L["tile_end"] = len(tiles)
+                    L["panel_begin"] = len(panels)
+                    for pr in range(0, a, PANEL):
+                        panels.append((li, pr, min(PANEL, a - pr), 0))
+                    L["panel_end"] = len(panels)
+                    L["lq_off"] = fac_off
+                    fac_off += _round_up(a * a, 16)
+                    L["rq_off"] = fac_off
+                    fac_off += _round_up(b * b, 16)
+                    L["ul_off"] = u_off
+                    u_off += _round_up(a * sl, 4)
+                    L["ur_off"] = u_off
+                    u_off += _round_up(b * sr, 4)
+                    L["hl_off"] = h_off
+                    h_off += _round_up(sl * sl, 4)
+                    L["hr_off"] = h_off
+                    h_off += _round_up(sr * sr, 4)
+                    L["evl_off"] = ev_off
+                    ev_off += _round_up(sl, 4)
+                    L["evr_off"] = ev_off
+                    ev_off += _round_up(sr, 4)
+                    L["w_off"] = w_off
+                    w_off += _round_up(a * kpad, 4)
+                    leaves.append(L)
+                    mine.append(li)
+                    self.eps_sparse.append(g["epsilon_sparse"])
+                    self.rho_leaf.append(g["rho"])
+            self.param_leaves.append(mine)
+            r["leaf_end"] = len(leaves)
+            r["tile_end"] = len(tiles)
+            for c0 in range(0, numel, CHUNK):
+                chunks.append((i, 0, c0, min(numel, c0 + CHUNK)))
+            r["chunk_end"] = len(chunks)
+            off += _round_up(numel, 4)
+        self.numel_total = off
+        self.ptab = ptab
+        self.ltab = np.array(leaves, LEAF_DT) if leaves else np.zeros(0, LEAF_DT)
+        self.ttab = np.array(tiles, TILE_DT) if tiles else np.zeros(0, TILE_DT)
+        self.pantab = np.array(panels, PANEL_DT) if panels else np.zeros(0, PANEL_DT)
+        self.ctab = np.array(chunks, CHUNK_DT) if chunks else np.zeros(0, CHUNK_DT)
+        self.kpad_max = kpad_max
+        self.p_stride = kpad_max * kpad_max + 4
+        self.n_leaves = len(leaves)
+        self._alloc(fac_off, u_off, h_off, ev_off, w_off)
+
+    # ------------------------------------------------------------------
+    def _dev(self, arr):
+        t = torch.from_numpy(np.ascontiguousarray(arr).view(np.uint8).copy())
+        return t.to(self.device)
+
+    def _alloc(self, fac_n, u_n, h_n, ev_n, w_n):
+        dev = self.device
+        z = lambda n, dt=torch.float32: torch.zeros(max(int(n), 1), dtype=dt, device=dev)
+        self.t_params = self._dev(self.ptab)
+        self.t_leaves = self._dev(self.ltab) if self.n_leaves else z(1)
+        self.t_tiles = self._dev(self.ttab) if len(self.ttab) else z(1)
+        self.t_panels = self._dev(self.pantab) if len(self.pantab) else z(1)
+        self.t_chunks = self._dev(self.ctab) if len(self.ctab) else z(1)
+        self.step_host = torch.zeros(self.n_params * STEP_DT.itemsize, dtype=torch.uint8,
+                                     pin_memory=torch.cuda.is_available())
+        self.step_np = self.step_host.numpy().view(STEP_DT)
+        self.step_event = None
+        self.t_step = torch.zeros(self.n_params * STEP_DT.itemsize, dtype=torch.uint8,
+                                  device=dev)
+        N = self.numel_total
+        self.exp_avg, self.exp_avg_sq = z(N), z(N)
+        self.exp_avg_diff, self.prev_grad = z(N), z(N)
+        self.diag_ema = z(N)
+        if self.int8_ema:
+            self.fac = z(fac_n, torch.int8)
+        else:
+            self.fac = z(fac_n)
+        self.absmax = z(2 * self.n_leaves)
+        self.u = z(u_n)
+        self.ev = z(ev_n)
+        self.k = z(self.n_leaves, torch.int32)
+        self.eig_y, self.eig_x, self.eig_ax = z(u_n), z(u_n), z(u_n)
+        self.eig_h, self.eig_v = z(h_n), z(h_n)
+        self.eig_aux = z(2 * self.n_leaves * 16)
+        self.eig_status = z(2 * self.n_leaves, torch.int32)
+        self.w = z(w_n)
+        self.p_part = z(len(self.pantab) * self.p_stride)
+        self.tile_part = z(len(self.ttab) * 4)
+        self.chunk_part = z(len(self.ctab) * 4)
+        has16 = any(p.dtype != torch.float32 for p in self.params)
+        has32 = any(p.dtype == torch.float32 for p in self.params)
+        self.upd = z(N if has16 else 1, torch.int16)
+        self.upd32 = z(N if has32 else 1)
+        self.leaf_nat2 = z(self.n_leaves)
+        self.param_scalars = z(self.n_params * 8)
+        self.global_norm_ema = torch.ones(1, dtype=torch.float64, device=dev)
+        self.slow = None
+        self.slow32 = None
+        self.t_eps_sparse = torch.tensor(self.eps_sparse or [0.0], dtype=torch.float32,
+                                         device=dev)
+        self.t_bias = torch.zeros(max(self.n_leaves, 1), dtype=torch.float32, device=dev)
+        self._init_factors()
+        self.dev = PlanDev_from(self)
+
+    def _init_factors(self):
+        """L = R = 1e-4*I (int8: q = 127*I, absmax = float32(1e-4)), U = reversed
+        identity (warm start; unused until the first eigen update), S = 1 for
+        the first k_init columns (preconditioner.py:196-231)."""
+        if not self.n_leaves:
+            return
+        L = self.ltab
+        fac = torch.zeros_like(self.fac, device="cpu")
+        u = torch.zeros(self.u.numel(), dtype=torch.float32)
+        ev = torch.zeros(self.ev.numel(), dtype=torch.float32)
+        eye_val = np.float32(1e-4)
+        for li in range(self.n_leaves):
+            for side in (0, 1):
+                n = int(L["a"][li] if side == 0 else L["b"][li])
+                s = int(L["sl"][li] if side == 0 else L["sr"][li])
+                fo = int(L["lq_off"][li] if side == 0 else L["rq_off"][li])
+                uo = int(L["ul_off"][li] if side == 0 else L["ur_off"][li])
+                eo = int(L["evl_off"][li] if side == 0 else L["evr_off"][li])
+                d = torch.arange(n)
+                if self.int8_ema:
+                    fac[fo + d * n + d] = 127
+                else:
+                    fac[fo + d * n + d] = float(eye_val)
+                c = torch.arange(min(n, s))
+                u[uo + (n - 1 - c) * s + c] = 1.0
+                ev[eo: eo + int(L["kmin"][li])] = 1.0
+        self.fac.copy_(fac)
+        self.u.copy_(u)
+        self.ev.copy_(ev)
+        self.absmax.fill_(float(eye_val))
+        self.k.copy_(torch.from_numpy(L["kmin"].astype(np.int32)))
+
+    def ensure_slow(self):
+        if self.slow is None:
+            N = self.numel_total
+            self.slow = torch.zeros(N, dtype=torch.int16, device=self.device)
+            self.slow32 = torch.zeros(N, dtype=torch.float32, device=self.device)
+            self.dev.slow = self.slow.data_ptr()
+            self.dev.slow32 = self.slow32.data_ptr()
+
+    # views ------------------------------------------------------------
+    def state_view(self, arena, i):
+        r = self.ptab[i]
+        o, n = int(r["offset"]), int(r["numel"])
+        return arena[o:o + n].view(self.params[i].shape)
+
+    def max_dims(self, leaf_ids):
+        L = self.ltab[leaf_ids]
+        return int(L["a"].max()), int(L["b"].max()), int(max(L["sl"].max(), L["sr"].max()))
+
+
+def PlanDev_from(plan):
+    d = _lib.PlanDev()
+    d.n_params = plan.n_params
+    d.n_leaves = plan.n_leaves
+    d.n_tiles = len(plan.ttab)
+    d.n_panels = len(plan.pantab)
+    d.n_chunks = len(plan.ctab)
+    d.int8_ema = int(plan.int8_ema)
+    d.kpad_max = plan.kpad_max
+    d.p_stride = plan.p_stride
+    ptr = lambda t: t.data_ptr() if t is not None else None
+    d.params, d.leaves, d.tiles = ptr(plan.t_params), ptr(plan.t_leaves), ptr(plan.t_tiles)
+    d.panels, d.chunks, d.step = ptr(plan.t_panels), ptr(plan.t_chunks), ptr(plan.t_step)
+    d.exp_avg, d.exp_avg_sq = ptr(plan.exp_avg), ptr(plan.exp_avg_sq)
+    d.exp_avg_diff, d.prev_grad = ptr(plan.exp_avg_diff), ptr(plan.prev_grad)
+    d.diag_ema, d.fac, d.absmax = ptr(plan.diag_ema), ptr(plan.fac), ptr(plan.absmax)
+    d.u, d.ev, d.k = ptr(plan.u), ptr(plan.ev), ptr(plan.k)
+    d.eig_y, d.eig_x, d.eig_ax = ptr(plan.eig_y), ptr(plan.eig_x), ptr(plan.eig_ax)
+    d.eig_h, d.eig_v, d.eig_aux = ptr(plan.eig_h), ptr(plan.eig_v), ptr(plan.eig_aux)
+    d.w, d.p_part, d.tile_part = ptr(plan.w), ptr(plan.p_part), ptr(plan.tile_part)
+    d.chunk_part, d.upd, d.upd32 = ptr(plan.chunk_part), ptr(plan.upd), ptr(plan.upd32)
+    d.leaf_nat2, d.param_scalars = ptr(plan.leaf_nat2), ptr(plan.param_scalars)
+    d.global_norm_ema = ptr(plan.global_norm_ema)
+    return d

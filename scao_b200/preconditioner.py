@@ -1,0 +1,174 @@
+"""Per-parameter preconditioner view over the plan's device arenas.
+
+``state["preconditioner"]`` of the reference is a ``SparsePreconditioner``
+object (scao/preconditioner.py:72-644).  Here the factors of all parameters
+live in flat device arenas owned by the plan; this class exposes one
+parameter's slice of them with the reference's attribute names and its exact
+``state_dict`` schema (preconditioner.py:570-600, 621-644).
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from .plan import to_2d_shape
+
+
+def _scale_from_absmax(am):
+    """utils.py:184-187: Python-float scale from the float32 absmax."""
+    am = float(np.float32(am))
+    return 1.0 if am < 1e-30 else am / 127.0
+
+
+def _absmax_from_scale(scale, q_nonzero):
+    """Inverse of _scale_from_absmax (exact: picks the float32 absmax whose
+    float64(absmax)/127 reproduces ``scale``)."""
+    if not q_nonzero or scale == 1.0 and not q_nonzero:
+        return np.float32(0.0)
+    a = np.float32(scale * 127.0)
+    for cand in (a, np.nextafter(a, np.float32(np.inf)), np.nextafter(a, np.float32(0))):
+        if float(cand) / 127.0 == scale:
+            return cand
+    return a
+
+
+class LeafView:
+    """One Kronecker leaf (a block of the reference's block-diagonal split)."""
+
+    def __init__(self, plan, li, owner):
+        self.plan, self.li, self.owner = plan, li, owner
+        L = plan.ltab[li]
+        self.m, self.n = int(L["a"]), int(L["b"])
+        self.k_min, self.k_max = int(L["kmin"]), int(L["kmax"])
+        self.use_kronecker = True
+        self.use_block_diagonal = False
+        self.use_int8_ema = plan.int8_ema
+
+    @property
+    def precond_step(self):
+        return self.owner.precond_step
+
+    @property
+    def k(self):
+        return int(self.plan.k[self.li].item())
+
+    def _fac(self, side):
+        L = self.plan.ltab[self.li]
+        n = self.m if side == 0 else self.n
+        o = int(L["lq_off"] if side == 0 else L["rq_off"])
+        return self.plan.fac[o:o + n * n].view(n, n)
+
+    def _u(self, side, k):
+        L = self.plan.ltab[self.li]
+        n = self.m if side == 0 else self.n
+        s = int(L["sl"] if side == 0 else L["sr"])
+        o = int(L["ul_off"] if side == 0 else L["ur_off"])
+        return self.plan.u[o:o + n * s].view(n, s)[:, :k]
+
+    def _s(self, side, k):
+        L = self.plan.ltab[self.li]
+        o = int(L["evl_off"] if side == 0 else L["evr_off"])
+        return self.plan.ev[o:o + k]
+
+    @property
+    def L_ema_scale(self):
+        return _scale_from_absmax(self.plan.absmax[2 * self.li].item())
+
+    @property
+    def R_ema_scale(self):
+        return _scale_from_absmax(self.plan.absmax[2 * self.li + 1].item())
+
+    def state_dict(self):
+        k = self.k
+        d = {"precond_step": self.precond_step, "k": k, "use_kronecker": True,
+             "use_block_diagonal": False}
+        if self.use_int8_ema:
+            d.update({"L_ema_q": self._fac(0).clone(), "L_ema_scale": self.L_ema_scale,
+                      "R_ema_q": self._fac(1).clone(), "R_ema_scale": self.R_ema_scale})
+        else:
+            d.update({"L_ema": self._fac(0).clone(), "R_ema": self._fac(1).clone()})
+        if self.precond_step == 0:
+            # before the first eigen update the reference holds eye(m, k), ones(k)
+            dev = self.plan.device
+            d.update({"U_l": torch.eye(self.m, k, device=dev), "S_l": torch.ones(k, device=dev),
+                      "U_r": torch.eye(self.n, k, device=dev), "S_r": torch.ones(k, device=dev)})
+        else:
+            d.update({"U_l": self._u(0, k).contiguous(), "S_l": self._s(0, k).clone(),
+                      "U_r": self._u(1, k).contiguous(), "S_r": self._s(1, k).clone()})
+        return d
+
+    def load_state_dict(self, st):
+        k = int(st["k"])
+        self.plan.k[self.li] = k
+        if self.use_int8_ema:
+            for side, qk, sk in ((0, "L_ema_q", "L_ema_scale"), (1, "R_ema_q", "R_ema_scale")):
+                q = st[qk].to(device=self.plan.device, dtype=torch.int8)
+                self._fac(side).copy_(q)
+                am = _absmax_from_scale(float(st[sk]), bool(q.ne(0).any().item()))
+                self.plan.absmax[2 * self.li + side] = float(am)
+        else:
+            self._fac(0).copy_(st["L_ema"])
+            self._fac(1).copy_(st["R_ema"])
+        for side, uk, sk in ((0, "U_l", "S_l"), (1, "U_r", "S_r")):
+            U = st[uk].to(device=self.plan.device, dtype=torch.float32)
+            S = st[sk].to(device=self.plan.device, dtype=torch.float32)
+            kk = U.shape[1]
+            self._u(side, kk).copy_(U)
+            self._s(side, kk).copy_(S)
+
+
+class PrecondView:
+    """``state["preconditioner"]`` of one parameter."""
+
+    def __init__(self, plan, pi, group):
+        self.plan, self.pi = plan, pi
+        p = plan.params[pi]
+        self.original_shape = tuple(p.shape)
+        self.m, self.n = to_2d_shape(self.original_shape)
+        self.precond_step = 0
+        self.rho = group["rho"]
+        self.use_int8_ema = plan.int8_ema
+        leaves = plan.param_leaves[pi]
+        self.use_kronecker = len(leaves) == 1 and int(plan.ptab[pi]["mode"]) == 1 and \
+            plan.ltab[leaves[0]]["a"] == self.m and plan.ltab[leaves[0]]["b"] == self.n
+        self.use_block_diagonal = int(plan.ptab[pi]["mode"]) == 1 and not self.use_kronecker
+        self._leaves = [LeafView(plan, li, self) for li in leaves]
+        self._blocks = self._leaves if self.use_block_diagonal else []
+
+    @property
+    def diag_bias(self):
+        return max(1.0 - self.rho ** self.precond_step, 1e-8) if self.precond_step else 1e-8
+
+    @property
+    def k(self):
+        if not self._leaves:
+            return 1
+        ks = self.plan.k[self.plan.param_leaves[self.pi]].tolist()
+        if self.use_block_diagonal:
+            return sum(ks) // max(len(ks), 1)
+        return ks[0]
+
+    @property
+    def diag_ema(self):
+        return self.plan.state_view(self.plan.diag_ema, self.pi)
+
+    def state_dict(self):
+        if self.use_block_diagonal:
+            d = {"precond_step": self.precond_step, "k": self.k, "use_kronecker": False,
+                 "use_block_diagonal": True}
+            d["blocks"] = [lf.state_dict() for lf in self._leaves]
+            return d
+        if self.use_kronecker:
+            return self._leaves[0].state_dict()
+        return {"precond_step": self.precond_step, "k": 1, "use_kronecker": False,
+                "use_block_diagonal": False, "diag_ema": self.diag_ema.clone()}
+
+    def load_state_dict(self, st):
+        self.precond_step = int(st["precond_step"])
+        if self.use_block_diagonal:
+            for lf, bs in zip(self._leaves, st["blocks"]):
+                lf.load_state_dict(bs)
+        elif self.use_kronecker:
+            self._leaves[0].load_state_dict(st)
+        else:
+            self.diag_ema.copy_(st["diag_ema"])

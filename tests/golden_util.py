@@ -33,3 +33,25 @@ def principal_angle(U, V):
     V = np.linalg.qr(np.asarray(V, np.float64))[0]
     s = np.linalg.svd(U.T @ V, compute_uv=False)
     return float(np.arccos(np.clip(s.min(), -1.0, 1.0)))
+
+
+def separated_prefix(S, rel_gap=1e-2):
+    """Largest j < len(S) such that the top-j eigen-subspace is separated from
+    the rest of the listed spectrum by a relative gap >= rel_gap; 0 if none.
+    Principal angles are only meaningful on such subspaces (near-equal
+    eigenvalues make the individual vectors arbitrary)."""
+    S = np.asarray(S, np.float64)
+    if S.size == 0 or S[0] <= 0:
+        return 0
+    best = 0
+    for j in range(1, len(S)):
+        if (S[j - 1] - S[j]) >= rel_gap * S[0]:
+            best = j
+    return best
+
+
+def subspace_angle(U, U_ref, S_ref, rel_gap=1e-2):
+    j = separated_prefix(S_ref, rel_gap)
+    if j == 0:
+        return 0.0
+    return principal_angle(np.asarray(U)[:, :j], np.asarray(U_ref)[:, :j])
