@@ -1,0 +1,381 @@
+"""Benchmark: SCAO optimizer step on the Llama-1B-shaped parameter set.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One "step" is one SCAO.step() over every parameter of the workload (bf16
+params, fp32 state, int8 curvature EMA, max_precond_dim=1024, k_max=64,
+precondition_freq=10) with synthetic seeded low-rank-plus-noise gradients.
+The optimizer is first primed through the 20 Adam-warmup steps, then W
+untimed and K timed Phase-2 steps run; K spans the natural curvature cadence
+(every 10th step refreshes curvature + eigenfactors), so ``ms_per_step`` is the
+amortised step time.  Inputs (2 GB of gradients, 16 GB of state) exceed L2.
+
+N > 1 (torchrun): owner-compute sharding -- every parameter is owned by one
+rank; gradients are reduce-scattered (average) into owner shards, each rank
+runs the step on its own parameters, and the updated bf16 parameters are
+all-gathered.  Time = max over ranks of CUDA-event time; the total work is
+fixed, so scaling is "strong".
+
+``--impl reference`` times the reference algorithm's CPU implementation (the
+numpy restatement in oracle/, the reference package itself cannot travel) on
+the host cores, on a bounded sample (one transformer layer) scaled to the full
+parameter set by element count.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "SCAO optimizer step ms (Llama-1B shapes)"
+UNIT = "ms"
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0}
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f), "measured"
+    except OSError:
+        return PEAKS_FALLBACK, "fallback"
+
+
+def algorithmic_bytes(workload, phase_of):
+    """Bytes a step must move per parameter (bf16 p/g, fp32 state):
+    Phase 2: read g,p,m,v,d,prev + write p,m,v,d,prev = 38 B/elem (44 fp32);
+    Phase 1: read g,p,m,v + write p,m,v,prev = 26 B/elem (32 fp32)."""
+    tot = 0
+    for spec in workload.params:
+        n = 1
+        for d in spec.shape:
+            n *= d
+        b16 = workload.param_dtype != "float32"
+        if phase_of(spec) == 2:
+            tot += n * (38 if b16 else 44)
+        else:
+            tot += n * (26 if b16 else 32)
+    return tot
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.out = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+# ---------------------------------------------------------------------------
+# reference (CPU) arm
+# ---------------------------------------------------------------------------
+
+def cpu_reference(workload, steps, warmup, sample_layers=1):
+    """Time the oracle's CPU restatement of the reference step on one
+    transformer layer (bounded sample) and scale to the full parameter set."""
+    from oracle.scao_oracle import OracleSCAO
+    from scao_b200 import synthetic, workloads
+
+    w_s = workloads.c4(n_layers=sample_layers)
+    w_s.params = [p for p in w_s.params if p.name not in ("embed", "final_norm")]
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    p0 = [p.float().numpy() for p in synthetic.init_params(w_s)]
+    kw = dict(w_s.scao_kwargs)
+    kw.update(warmup_steps=0, min_precond_updates=0)
+    opt = OracleSCAO(p0, dtype=w_s.param_dtype, threads=threads, **kw)
+    gen = synthetic.LowRankGradients(w_s)
+    grads = [g.float().numpy() for g in gen.next()]
+    pf = kw["precond_freq"]
+    t_reg, t_curv = [], []
+    total = steps + warmup
+    for i in range(total):
+        curv = (opt.global_step + 1) % pf == 0
+        t0 = time.perf_counter()
+        opt.step(grads)
+        dt = (time.perf_counter() - t0) * 1e3
+        if i >= warmup:
+            (t_curv if curv else t_reg).append(dt)
+    if not t_reg:
+        t_reg = [float("nan")]
+    reg = statistics.mean(t_reg)
+    # curvature step = regular step + update_curvature (EMA GEMMs + eigh per
+    # block) of every parameter; time the latter directly on the sample
+    if not t_curv:
+        def upd(i):
+            opt.state[i]["precond"].update_curvature(grads[i])
+        t0 = time.perf_counter()
+        if opt._pool is not None:
+            list(opt._pool.map(upd, range(len(grads))))
+        else:
+            for i in range(len(grads)):
+                upd(i)
+        t_curv = [reg + (time.perf_counter() - t0) * 1e3]
+    curv = statistics.mean(t_curv)
+    scale = workload.numel / w_s.numel
+    amort = ((pf - 1) * reg + curv) / pf * scale
+    sample = (f"{sample_layers} of 16 transformer layers ({w_s.numel / 1e6:.1f}M elems, "
+              f"{len(w_s.params)} params); regular step {reg:.0f} ms, curvature step "
+              f"{curv:.0f} ms on the sample; amortised ((pf-1)*reg+curv)/pf and scaled "
+              f"x{scale:.2f} by element count to the full {workload.numel / 1e9:.3f}B set")
+    return amort, threads, sample, reg * scale, curv * scale
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+def build_opt(workload, params, scao_cls, **extra):
+    groups = [{"params": [p for p, s in zip(params, workload.params) if not s.adam_only]}]
+    adam = [p for p, s in zip(params, workload.params) if s.adam_only]
+    if adam:
+        # Adam-only (Phase-1-forever) group: warmup_steps beyond any run
+        groups.append({"params": adam, "warmup_steps": 10 ** 9})
+    return scao_cls(groups, **workload.scao_kwargs, **extra)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--layers", type=int, default=16, help="debug: fewer layers")
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--json-out", default=None)
+    a = ap.parse_args()
+    a.warmup = max(a.warmup, 3)
+
+    from scao_b200 import workloads
+    workload = workloads.c4(n_layers=a.layers)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    cfg = {"workload": workload.name, "params": workload.numel,
+           "param_dtype": workload.param_dtype, "state_dtype": "float32",
+           "int8_ema": True, "max_precond_dim": 1024, "k_max": 64, "precond_freq": 10,
+           "warmup_steps": 20, "blend_steps": 50, "grad_rank": workload.grad_rank,
+           "l2": "inputs larger than L2 (2.1 GB grads, 16.6 GB fp32 state per step)"}
+
+    if a.impl == "reference":
+        if rank != 0:
+            return
+        amort, cores, sample, reg, curv = cpu_reference(workload, steps=2, warmup=1)
+        line = {"impl": "reference", "metric": METRIC, "value": round(amort, 3), "unit": UNIT,
+                "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
+                "ms_per_step": round(amort, 3), "higher_is_better": False,
+                "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic", "config": cfg,
+                "cpu_baseline": {"value": round(amort, 3), "unit": UNIT, "cores": cores,
+                                 "kind": "port", "sample": sample,
+                                 "regular_step_ms": round(reg, 1),
+                                 "curvature_step_ms": round(curv, 1)},
+                "e2e": {"value": round(amort, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    from scao_b200 import SCAO, _lib, synthetic
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
+    L = _lib.lib()
+
+    # ---------------- setup ----------------
+    params0 = synthetic.init_params(workload, seed=0, device=dev)
+    params = [torch.nn.Parameter(p) for p in params0]
+    gen = synthetic.LowRankGradients(workload, seed=0, device=dev)
+    n_sets = 3
+    grad_sets = [gen.next() for _ in range(n_sets)]
+    torch.cuda.synchronize()
+    if world > 1:
+        from scao_b200.distributed import ShardedSCAO
+        opt = ShardedSCAO(params, workload, lambda ps: build_opt_list(workload, ps, SCAO))
+    else:
+        opt = build_opt(workload, params, SCAO)
+
+    def set_grads(k):
+        if world > 1:
+            opt.load_grads(grad_sets[k % n_sets])
+        else:
+            for p, g in zip(params, grad_sets[k % n_sets]):
+                p.grad = g
+
+    stream = torch.cuda.current_stream(dev)
+    # prime through the Adam warmup (20 steps) + W warm-up steps
+    n_prime = workload.scao_kwargs["warmup_steps"] + a.warmup
+    for k in range(n_prime):
+        set_grads(k)
+        opt.step()
+    torch.cuda.synchronize()
+
+    # ---------------- timed region ----------------
+    clocks = ClockSampler(local)
+    L.scao_prof_reset()
+    L.scao_prof_enable(1)
+    launches0 = L.scao_launch_count()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(a.steps + 1)]
+    curv_flags = []
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.3)
+    ev[0].record(stream)
+    for k in range(a.steps):
+        gstep = opt._global_step + 1 if world == 1 else opt.global_step + 1
+        curv_flags.append(gstep % 10 == 0)
+        set_grads(n_prime + k)
+        opt.step()
+        ev[k + 1].record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    clk = clocks.stop()
+    launches = L.scao_launch_count() - launches0
+    L.scao_prof_enable(0)
+    prof = _lib.prof_read()
+    step_ms = [ev[k].elapsed_time(ev[k + 1]) for k in range(a.steps)]
+    total_ms = ev[0].elapsed_time(ev[a.steps])
+    if world > 1:
+        t = torch.tensor([total_ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        total_ms = t.item()
+    ms_per_step = total_ms / a.steps
+    reg = [t for t, c in zip(step_ms, curv_flags) if not c]
+    cur = [t for t, c in zip(step_ms, curv_flags) if c]
+
+    # ---------------- roofline of the apply (regular-step kernels) ----------
+    pk, pname = peaks()
+    hbm = float(pk.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
+    apply_slots = ["proj", "diag_pre", "leaf_coef", "param_pre", "apply_kron", "apply_flat",
+                   "param_post", "global_norm", "apply_p"]
+    apply_ms = sum(prof.get(s, (0.0, 0))[0] for s in apply_slots) / a.steps
+    owned = opt.owned_specs() if world > 1 else workload.params
+    wl_local = type(workload)(workload.name, owned, workload.scao_kwargs, workload.grad_rank,
+                              workload.grad_decay, workload.param_dtype)
+    abytes = algorithmic_bytes(wl_local, lambda s: 1 if s.adam_only else 2)
+    achieved = abytes / (apply_ms * 1e-3) / 1e9 if apply_ms > 0 else 0.0
+    kern = {k: {"ms_total": round(v[0], 3), "launches": v[1]} for k, v in sorted(prof.items())}
+
+    # ---------------- e2e: public API with host gradient buffers -------------
+    e2e = None
+    if world == 1 and a.e2e_steps > 0:
+        host = [g.cpu().pin_memory() for g in grad_sets[0]]
+        h2d = sum(h.numel() * h.element_size() for h in host)
+        res = torch.empty(1, dtype=torch.float64).pin_memory()
+        for p in params:
+            p.grad = torch.empty_like(p)
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for k in range(a.e2e_steps):
+            for p, h in zip(params, host):
+                p.grad.copy_(h, non_blocking=True)
+            opt.step()
+            res.copy_(opt._plan.global_norm_ema, non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e2e = {"value": round(e0.elapsed_time(e1) / a.e2e_steps, 3), "unit": UNIT,
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 8,
+               "note": "grads copied H2D from pinned host memory every step, "
+                       "global-norm EMA read back"}
+
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": round(ms_per_step, 3), "unit": UNIT, "n_gpus": world,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms_per_step, 3),
+        "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (seeded low-rank+noise gradients, N(0,0.02^2) params)",
+        "config": dict(cfg, parallelism=f"owner-compute x{world}" if world > 1 else "single"),
+        "regular_step_ms": round(statistics.mean(reg), 3) if reg else None,
+        "curvature_step_ms": round(statistics.mean(cur), 3) if cur else None,
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
+                     "unit": "GB/s", "frac": round(achieved / hbm, 4), "traffic": None,
+                     "kernel": "regular-step apply sequence (" + "+".join(apply_slots) + ")",
+                     "algorithmic_bytes_per_step": abytes, "apply_ms_per_step": round(apply_ms, 3),
+                     "peak_source": pname},
+        "kernels": kern,
+        "gpu_launches": int(launches),
+        "clocks": clk,
+    }
+    if e2e:
+        line["e2e"] = e2e
+    if world == 1 and not a.no_cpu_baseline:
+        amort, cores, sample, creg, ccurv = cpu_reference(workload, steps=2, warmup=1)
+        line["cpu_baseline"] = {"value": round(amort, 1), "unit": UNIT, "cores": cores,
+                                "kind": "port", "sample": sample}
+    print(json.dumps(line), flush=True)
+    if a.json_out:
+        with open(a.json_out, "w") as f:
+            json.dump(line, f, indent=1)
+
+
+def build_opt_list(workload, params_specs, scao_cls):
+    """Optimizer over a rank's owned (param, spec) pairs."""
+    ps = [p for p, s in params_specs if not s.adam_only]
+    adam = [p for p, s in params_specs if s.adam_only]
+    groups = []
+    if ps:
+        groups.append({"params": ps})
+    if adam:
+        groups.append({"params": adam, "warmup_steps": 10 ** 9})
+    return scao_cls(groups, **workload.scao_kwargs)
+
+
+if __name__ == "__main__":
+    main()

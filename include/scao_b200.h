@@ -237,6 +237,16 @@ SCAO_API int scao_plan_step(const ScaoPlanDev* plan_host, void* stream);
 SCAO_API int scao_plan_lookahead(const ScaoPlanDev* plan_host, float alpha, int init,
                         void* stream);
 
+/* Instrumentation: number of kernels this library has launched so far, and
+ * optional CUDA-event timing of every launch on its own stream (per kernel
+ * slot; names from scao_prof_name).                                        */
+SCAO_API int64_t scao_launch_count(void);
+SCAO_API void scao_prof_enable(int on);
+SCAO_API int scao_prof_read(double* ms, int64_t* counts, int nslots);
+SCAO_API void scao_prof_reset(void);
+SCAO_API const char* scao_prof_name(int slot);
+SCAO_API int scao_prof_slots(void);
+
 /* Library identification. */
 SCAO_API const char* scao_version(void);
 

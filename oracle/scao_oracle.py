@@ -319,7 +319,7 @@ class OracleSCAO:
     """
 
     def __init__(self, params, dtype="float32", groups=None, lookahead_k=5,
-                 lookahead_alpha=0.5, **kw):
+                 lookahead_alpha=0.5, threads=1, **kw):
         self.dtype = dtype
         self.params = [round_to(np.array(p, dtype=F32), dtype) for p in params]
         d = dict(_DEFAULTS)
@@ -339,6 +339,11 @@ class OracleSCAO:
         self.lookahead_k = lookahead_k
         self.lookahead_alpha = lookahead_alpha
         self.slow = {}
+        self.threads = threads
+        self._pool = None
+        if threads > 1:
+            from concurrent.futures import ThreadPoolExecutor
+            self._pool = ThreadPoolExecutor(threads)
 
     def _init_state(self, i, group):
         """optimizer.py:407-433."""
@@ -379,7 +384,19 @@ class OracleSCAO:
                 self.params[i] = s.copy()
 
     def _step_group(self, group, grads):
-        """optimizer.py:509-645."""
+        """optimizer.py:509-645 (parameters are independent: optionally run
+        on a thread pool; numpy releases the GIL inside its loops)."""
+        for i in group["params"]:
+            if grads[i] is not None:
+                self._init_state(i, group)
+        todo = [i for i in group["params"] if grads[i] is not None]
+        if self._pool is not None:
+            list(self._pool.map(lambda i: self._step_param(i, group, grads[i]), todo))
+        else:
+            for i in todo:
+                self._step_param(i, group, grads[i])
+
+    def _step_param(self, i, group, gr):
         dt = self.dtype
         lr = group["lr"]
         beta1, beta2 = group["betas"]
@@ -389,11 +406,7 @@ class OracleSCAO:
         pf = group["precond_freq"]
         tau = group["tau"]
         lars = group["lars_coeff"]
-        for i in group["params"]:
-            gr = grads[i]
-            if gr is None:
-                continue
-            self._init_state(i, group)
+        if True:
             st = self.state[i]
             st["step"] += 1
             step = st["step"]
@@ -417,7 +430,7 @@ class OracleSCAO:
                 p = add_alpha(p, round_to(m / denom, dt), -(lr / bc1), dt)
                 st.update(m=m, v=v, prev=grad.copy())
                 self.params[i] = p
-                continue
+                return
             if not st["started"]:
                 st["started"] = True
                 st["scao_step"] = 0

@@ -96,6 +96,12 @@ SIGNATURES = {
     "scao_plan_step": (C.c_int, [C.POINTER(PlanDev), _P]),
     "scao_plan_lookahead": (C.c_int, [C.POINTER(PlanDev), C.c_float, C.c_int, _P]),
     "scao_version": (C.c_char_p, []),
+    "scao_launch_count": (C.c_int64, []),
+    "scao_prof_enable": (None, [C.c_int]),
+    "scao_prof_read": (C.c_int, [_P, _P, C.c_int]),
+    "scao_prof_reset": (None, []),
+    "scao_prof_name": (C.c_char_p, [C.c_int]),
+    "scao_prof_slots": (C.c_int, []),
 }
 
 _lib = None
@@ -111,9 +117,13 @@ def lib():
     if _lib is not None:
         return _lib
     if not os.path.exists(LIB_PATH):
-        raise ScaoError(
-            f"scao_b200 CUDA library not built ({LIB_PATH}); run "
-            "`python -m scao_b200.build` (needs nvcc, sm_100a).")
+        try:
+            from . import build as _build
+            _build.build()
+        except Exception as e:  # noqa: BLE001
+            raise ScaoError(
+                f"scao_b200 CUDA library not built ({LIB_PATH}) and building it failed: {e}; "
+                "run `python -m scao_b200.build` (needs nvcc, sm_100a).") from e
     L = C.CDLL(LIB_PATH)
     for name, (res, args) in SIGNATURES.items():
         f = getattr(L, name)
@@ -126,3 +136,13 @@ def lib():
 def check(rc, what):
     if rc != 0:
         raise ScaoError(f"{what} failed with status {rc}")
+
+
+def prof_read():
+    """{kernel slot name: (total ms, launches)} accumulated since the last reset."""
+    L = lib()
+    n = L.scao_prof_slots()
+    ms = (C.c_double * n)()
+    cnt = (C.c_int64 * n)()
+    check(L.scao_prof_read(C.cast(ms, _P), C.cast(cnt, _P), n), "scao_prof_read")
+    return {L.scao_prof_name(i).decode(): (ms[i], cnt[i]) for i in range(n) if cnt[i]}

@@ -22,6 +22,7 @@
 // torch contracts to a fused multiply-add on CPU (add_ with alpha, addcmul_)
 // use fmaf.  Parameter-dtype roundings are reproduced exactly.
 #include "common.cuh"
+#include "prof.cuh"
 
 namespace {
 
@@ -572,7 +573,7 @@ extern "C" int scao_plan_step(const ScaoPlanDev* P, void* stream) {
         SCAO_CHECK_LAUNCH();
     }
     if (P->n_chunks > 0) {
-        diag_pre_kernel<<<P->n_chunks, NT, 0, st>>>(*P);
+        { ProfScope _ps(SLOT_DIAG_PRE, st); diag_pre_kernel<<<P->n_chunks, NT, 0, st>>>(*P); }
         SCAO_CHECK_LAUNCH();
     }
     if (P->n_leaves > 0) {
@@ -586,26 +587,26 @@ extern "C" int scao_plan_step(const ScaoPlanDev* P, void* stream) {
                                  2 * 128 * (TT + 4) * 4);
             attr = true;
         }
-        leaf_coef_kernel<<<P->n_leaves, NT, sm, st>>>(*P);
+        { ProfScope _ps(SLOT_LEAF_COEF, st); leaf_coef_kernel<<<P->n_leaves, NT, sm, st>>>(*P); }
         SCAO_CHECK_LAUNCH();
     }
-    param_pre_kernel<<<P->n_params, NT, 0, st>>>(*P);
+    { ProfScope _ps(SLOT_PARAM_PRE, st); param_pre_kernel<<<P->n_params, NT, 0, st>>>(*P); }
     SCAO_CHECK_LAUNCH();
     if (P->n_tiles > 0) {
         const size_t sm = (size_t)2 * P->kpad_max * (TT + 4) * 4;
-        apply_kron_kernel<<<P->n_tiles, NT, sm, st>>>(*P);
+        { ProfScope _ps(SLOT_APPLY_KRON, st); apply_kron_kernel<<<P->n_tiles, NT, sm, st>>>(*P); }
         SCAO_CHECK_LAUNCH();
     }
     if (P->n_chunks > 0) {
-        apply_flat_kernel<<<P->n_chunks, NT, 0, st>>>(*P);
+        { ProfScope _ps(SLOT_APPLY_FLAT, st); apply_flat_kernel<<<P->n_chunks, NT, 0, st>>>(*P); }
         SCAO_CHECK_LAUNCH();
     }
-    param_post_kernel<<<P->n_params, NT, 0, st>>>(*P);
+    { ProfScope _ps(SLOT_PARAM_POST, st); param_post_kernel<<<P->n_params, NT, 0, st>>>(*P); }
     SCAO_CHECK_LAUNCH();
-    global_norm_kernel<<<1, 512, 0, st>>>(*P);
+    { ProfScope _ps(SLOT_GLOBAL_NORM, st); global_norm_kernel<<<1, 512, 0, st>>>(*P); }
     SCAO_CHECK_LAUNCH();
     if (P->n_chunks > 0) {
-        apply_p_kernel<<<P->n_chunks, NT, 0, st>>>(*P);
+        { ProfScope _ps(SLOT_APPLY_P, st); apply_p_kernel<<<P->n_chunks, NT, 0, st>>>(*P); }
         SCAO_CHECK_LAUNCH();
     }
     return SCAO_OK;
@@ -615,7 +616,7 @@ extern "C" int scao_plan_lookahead(const ScaoPlanDev* P, float alpha, int init,
                                    void* stream) {
     if (!P) return SCAO_ERR_ARG;
     if (P->n_chunks == 0) return SCAO_OK;
-    lookahead_kernel<<<P->n_chunks, NT, 0, (cudaStream_t)stream>>>(*P, alpha, init);
+    { ProfScope _ps(SLOT_LOOKAHEAD, (cudaStream_t)stream); lookahead_kernel<<<P->n_chunks, NT, 0, (cudaStream_t)stream>>>(*P, alpha, init); }
     SCAO_CHECK_LAUNCH();
     return SCAO_OK;
 }

@@ -19,6 +19,7 @@
 //   kept as the warm start for the next curvature step.
 // All GEMMs here are batched SIMT FP32 tiles.
 #include "common.cuh"
+#include "prof.cuh"
 
 namespace {
 
@@ -567,10 +568,10 @@ extern "C" int scao_plan_eigen(const ScaoPlanDev* P, const int32_t* leaf_ids, in
     if (n_ids == 0) return SCAO_OK;
     cudaStream_t st = (cudaStream_t)stream;
     const int np = 2 * n_ids;
-    eig_prep_kernel<<<np, NT, 0, st>>>(*P, leaf_ids, bias_factor);
+    { ProfScope _ps(SLOT_EIG_PREP, st); eig_prep_kernel<<<np, NT, 0, st>>>(*P, leaf_ids, bias_factor); }
     SCAO_CHECK_LAUNCH();
     const size_t dsm = 4096 * 8;
-    eig_diag_kernel<<<np, NT, dsm, st>>>(*P, leaf_ids);
+    { ProfScope _ps(SLOT_EIG_DIAG, st); eig_diag_kernel<<<np, NT, dsm, st>>>(*P, leaf_ids); }
     SCAO_CHECK_LAUNCH();
     const size_t jsm = jacobi_smem(smax);
     const size_t csm = (size_t)2 * smax * (smax + 1) * 4;
@@ -589,43 +590,43 @@ extern "C" int scao_plan_eigen(const ScaoPlanDev* P, const int32_t* leaf_ids, in
         GemmSpec g;
         // Y = A U
         g = {BUF_FAC, BUF_U, BUF_Y, DIM_N, DIM_S, DIM_N, 0, 0};
-        eig_gemm_kernel<<<dim3(tiles_nn, np), NT, 0, st>>>(*P, leaf_ids, g);
+        { ProfScope _ps(SLOT_EIG_GEMM, 0); eig_gemm_kernel<<<dim3(tiles_nn, np), NT, 0, st>>>(*P, leaf_ids, g); }
         SCAO_CHECK_LAUNCH();
         // H = U^T Y
         g = {BUF_U, BUF_Y, BUF_H, DIM_S, DIM_S, DIM_N, 1, 0};
-        eig_gemm_kernel<<<dim3(tiles_ss, np), NT, 0, st>>>(*P, leaf_ids, g);
+        { ProfScope _ps(SLOT_EIG_GEMM, 0); eig_gemm_kernel<<<dim3(tiles_ss, np), NT, 0, st>>>(*P, leaf_ids, g); }
         SCAO_CHECK_LAUNCH();
-        eig_jacobi_kernel<<<np, NT, jsm, st>>>(*P, leaf_ids, 30);
+        { ProfScope _ps(SLOT_EIG_JACOBI, st); eig_jacobi_kernel<<<np, NT, jsm, st>>>(*P, leaf_ids, 30); }
         SCAO_CHECK_LAUNCH();
         // X = U V, AX = Y V
         g = {BUF_U, BUF_V, BUF_X, DIM_N, DIM_S, DIM_S, 0, 0};
-        eig_gemm_kernel<<<dim3(tiles_nn, np), NT, 0, st>>>(*P, leaf_ids, g);
+        { ProfScope _ps(SLOT_EIG_GEMM, 0); eig_gemm_kernel<<<dim3(tiles_nn, np), NT, 0, st>>>(*P, leaf_ids, g); }
         SCAO_CHECK_LAUNCH();
         g = {BUF_Y, BUF_V, BUF_AX, DIM_N, DIM_S, DIM_S, 0, 0};
-        eig_gemm_kernel<<<dim3(tiles_nn, np), NT, 0, st>>>(*P, leaf_ids, g);
+        { ProfScope _ps(SLOT_EIG_GEMM, 0); eig_gemm_kernel<<<dim3(tiles_nn, np), NT, 0, st>>>(*P, leaf_ids, g); }
         SCAO_CHECK_LAUNCH();
-        eig_residual_kernel<<<np, NT, 0, st>>>(*P, leaf_ids, tol, it, last);
+        { ProfScope _ps(SLOT_EIG_RESIDUAL, st); eig_residual_kernel<<<np, NT, 0, st>>>(*P, leaf_ids, tol, it, last); }
         SCAO_CHECK_LAUNCH();
         if (last) break;
         // CholeskyQR2 of the normalised AX: AX -> Y -> U
         g = {BUF_AX, BUF_AX, BUF_H, DIM_S, DIM_S, DIM_N, 1, 1};
-        eig_gemm_kernel<<<dim3(tiles_ss, np), NT, 0, st>>>(*P, leaf_ids, g);
+        { ProfScope _ps(SLOT_EIG_GEMM, 0); eig_gemm_kernel<<<dim3(tiles_ss, np), NT, 0, st>>>(*P, leaf_ids, g); }
         SCAO_CHECK_LAUNCH();
-        eig_cholinv_kernel<<<np, NT, csm, st>>>(*P, leaf_ids);
+        { ProfScope _ps(SLOT_EIG_CHOLINV, st); eig_cholinv_kernel<<<np, NT, csm, st>>>(*P, leaf_ids); }
         SCAO_CHECK_LAUNCH();
         g = {BUF_AX, BUF_H, BUF_Y, DIM_N, DIM_S, DIM_S, 0, 1};
-        eig_gemm_kernel<<<dim3(tiles_nn, np), NT, 0, st>>>(*P, leaf_ids, g);
+        { ProfScope _ps(SLOT_EIG_GEMM, 0); eig_gemm_kernel<<<dim3(tiles_nn, np), NT, 0, st>>>(*P, leaf_ids, g); }
         SCAO_CHECK_LAUNCH();
         g = {BUF_Y, BUF_Y, BUF_H, DIM_S, DIM_S, DIM_N, 1, 1};
-        eig_gemm_kernel<<<dim3(tiles_ss, np), NT, 0, st>>>(*P, leaf_ids, g);
+        { ProfScope _ps(SLOT_EIG_GEMM, 0); eig_gemm_kernel<<<dim3(tiles_ss, np), NT, 0, st>>>(*P, leaf_ids, g); }
         SCAO_CHECK_LAUNCH();
-        eig_cholinv_kernel<<<np, NT, csm, st>>>(*P, leaf_ids);
+        { ProfScope _ps(SLOT_EIG_CHOLINV, st); eig_cholinv_kernel<<<np, NT, csm, st>>>(*P, leaf_ids); }
         SCAO_CHECK_LAUNCH();
         g = {BUF_Y, BUF_H, BUF_U, DIM_N, DIM_S, DIM_S, 0, 1};
-        eig_gemm_kernel<<<dim3(tiles_nn, np), NT, 0, st>>>(*P, leaf_ids, g);
+        { ProfScope _ps(SLOT_EIG_GEMM, 0); eig_gemm_kernel<<<dim3(tiles_nn, np), NT, 0, st>>>(*P, leaf_ids, g); }
         SCAO_CHECK_LAUNCH();
     }
-    eig_rank_kernel<<<(n_ids + 127) / 128, 128, 0, st>>>(*P, leaf_ids, n_ids, eps_sparse, status);
+    { ProfScope _ps(SLOT_EIG_RANK, st); eig_rank_kernel<<<(n_ids + 127) / 128, 128, 0, st>>>(*P, leaf_ids, n_ids, eps_sparse, status); }
     SCAO_CHECK_LAUNCH();
     return SCAO_OK;
 }

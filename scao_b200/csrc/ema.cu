@@ -12,6 +12,7 @@
 // This file holds the portable SIMT-FMA tile kernel; see gram_tc.cu for the
 // tcgen05 tensor-core path used for 16-bit gradients.
 #include "common.cuh"
+#include "prof.cuh"
 
 namespace {
 
@@ -228,12 +229,12 @@ extern "C" int scao_plan_curvature(const ScaoPlanDev* P, const int32_t* leaf_ids
             return SCAO_ERR_LAUNCH;
         const int32_t* ids = leaf_ids + j0 / 2;
         dim3 grid(tiles, np);
-        gram_ema_simt_kernel<<<grid, NT, 0, st>>>(*P, ids, xbuf, xstride, amnew,
-                                                   rho_f, alpha_f);
+        { ProfScope _ps(SLOT_GRAM_EMA, st); gram_ema_simt_kernel<<<grid, NT, 0, st>>>(*P, ids, xbuf, xstride, amnew,
+                                                   rho_f, alpha_f); }
         SCAO_CHECK_LAUNCH();
         if (P->int8_ema) {
             dim3 g2((int)((mx * mx + 255) / 256 < 64 ? (mx * mx + 255) / 256 : 64), np);
-            requant_batch_kernel<<<g2, 256, 0, st>>>(*P, ids, xbuf, xstride, amnew);
+            { ProfScope _ps(SLOT_REQUANT, st); requant_batch_kernel<<<g2, 256, 0, st>>>(*P, ids, xbuf, xstride, amnew); }
             SCAO_CHECK_LAUNCH();
         }
     }
@@ -246,8 +247,8 @@ extern "C" int scao_plan_curvature_diag(const ScaoPlanDev* P,
     if (!P || n_ids < 0) return SCAO_ERR_ARG;
     if (n_ids == 0) return SCAO_OK;
     dim3 grid(32, n_ids);
-    diag_ema_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(
-        *P, param_ids, (float)rho, (float)(1.0 - rho));
+    { ProfScope _ps(SLOT_DIAG_EMA, (cudaStream_t)stream); diag_ema_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(
+        *P, param_ids, (float)rho, (float)(1.0 - rho)); }
     SCAO_CHECK_LAUNCH();
     return SCAO_OK;
 }

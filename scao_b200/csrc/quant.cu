@@ -12,6 +12,7 @@
 // Every multiply and add is rounded separately (no FMA contraction), as the
 // reference evaluates them as separate tensor ops.
 #include "common.cuh"
+#include "prof.cuh"
 
 namespace {
 
@@ -76,10 +77,10 @@ extern "C" int scao_int8_ema_update(const int8_t* q, double scale,
     float* x = (float*)scratch;
     float* am = (float*)((char*)scratch + ((n * 4 + 255) / 256) * 256);
     if (cudaMemsetAsync(am, 0, sizeof(float), st) != cudaSuccess) return SCAO_ERR_LAUNCH;
-    ema_pass1_kernel<<<grid_for(n), kThreads, 0, st>>>(q, (float)scale, (float)rho,
-                                                       new_val, n, x, am);
+    { ProfScope _ps(SLOT_QUANT, st); ema_pass1_kernel<<<grid_for(n), kThreads, 0, st>>>(q, (float)scale, (float)rho,
+                                                       new_val, n, x, am); }
     SCAO_CHECK_LAUNCH();
-    requant_kernel<<<grid_for(n), kThreads, 0, st>>>(x, n, am, q_out, scale_out);
+    { ProfScope _ps(SLOT_QUANT, st); requant_kernel<<<grid_for(n), kThreads, 0, st>>>(x, n, am, q_out, scale_out); }
     SCAO_CHECK_LAUNCH();
     return SCAO_OK;
 }
@@ -92,10 +93,10 @@ extern "C" int scao_quantize_sym_int8(const float* x, int64_t n, int8_t* q,
     float* am = (float*)scratch;
     if (cudaMemsetAsync(am, 0, sizeof(float), st) != cudaSuccess) return SCAO_ERR_LAUNCH;
     // pass 1 with no dequantised term and no output: absmax of x only
-    ema_pass1_kernel<<<grid_for(n), kThreads, 0, st>>>(nullptr, 0.f, 0.f, x, n,
-                                                       nullptr, am);
+    { ProfScope _ps(SLOT_QUANT, st); ema_pass1_kernel<<<grid_for(n), kThreads, 0, st>>>(nullptr, 0.f, 0.f, x, n,
+                                                       nullptr, am); }
     SCAO_CHECK_LAUNCH();
-    requant_kernel<<<grid_for(n), kThreads, 0, st>>>(x, n, am, q, scale_out);
+    { ProfScope _ps(SLOT_QUANT, st); requant_kernel<<<grid_for(n), kThreads, 0, st>>>(x, n, am, q, scale_out); }
     SCAO_CHECK_LAUNCH();
     return SCAO_OK;
 }
@@ -103,7 +104,7 @@ extern "C" int scao_quantize_sym_int8(const float* x, int64_t n, int8_t* q,
 extern "C" int scao_dequantize_sym_int8(const int8_t* q, double scale, int64_t n,
                                         float* out, void* stream) {
     if (n <= 0 || !q || !out) return SCAO_ERR_ARG;
-    dequant_kernel<<<grid_for(n), kThreads, 0, (cudaStream_t)stream>>>(q, (float)scale, n, out);
+    { ProfScope _ps(SLOT_QUANT, (cudaStream_t)stream); dequant_kernel<<<grid_for(n), kThreads, 0, (cudaStream_t)stream>>>(q, (float)scale, n, out); }
     SCAO_CHECK_LAUNCH();
     return SCAO_OK;
 }

@@ -7,6 +7,7 @@
 // They run a generic tiled FP32 GEMM in four (resp. two) launches; the
 // optimizer itself uses the batched plan kernels in apply.cu.
 #include "common.cuh"
+#include "prof.cuh"
 
 namespace {
 
@@ -82,7 +83,7 @@ __global__ void delta_kernel(float* Pm, const float* sl, const float* sr, int k)
 int launch_gemm(Op A, Op B, int M, int N, int K, void* C, int64_t ldc, int cdt,
                 const void* Gadd, int gdt, cudaStream_t st) {
     const int tiles = ((M + TM - 1) / TM) * ((N + TN - 1) / TN);
-    gemm_kernel<<<tiles, NT, 0, st>>>(A, B, M, N, K, C, ldc, cdt, Gadd, gdt);
+    { ProfScope _ps(SLOT_SEAM, st); gemm_kernel<<<tiles, NT, 0, st>>>(A, B, M, N, K, C, ldc, cdt, Gadd, gdt); }
     SCAO_CHECK_LAUNCH();
     return SCAO_OK;
 }
@@ -117,7 +118,7 @@ extern "C" int scao_fused_kronecker_precond(const float* U_l, const float* s_l_i
     rc = launch_gemm({U_l, SCAO_F32, k, 1, nullptr}, {T, SCAO_F32, k, 0, nullptr}, k, k, m,
                      Pm, k, SCAO_F32, nullptr, 0, st);
     if (rc) return rc;
-    delta_kernel<<<(k * k + 255) / 256, 256, 0, st>>>(Pm, s_l_inv4, s_r_inv4, k);
+    { ProfScope _ps(SLOT_SEAM, st); delta_kernel<<<(k * k + 255) / 256, 256, 0, st>>>(Pm, s_l_inv4, s_r_inv4, k); }
     SCAO_CHECK_LAUNCH();
     // W = U_l Delta  (m x k)
     rc = launch_gemm({U_l, SCAO_F32, k, 0, nullptr}, {Pm, SCAO_F32, k, 0, nullptr}, m, k, k,

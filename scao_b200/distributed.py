@@ -1,0 +1,232 @@
+"""Owner-compute sharding of the SCAO step across the GPUs of one node.
+
+The reference's distributed helpers (scao/distributed.py:60-160) keep the full
+optimizer state on every rank and all-reduce-average preconditioner factors
+after curvature steps.  Here every parameter -- with its moments, its int8
+curvature factors and its eigenfactors -- is owned by exactly one rank:
+
+    1. reduce-scatter (average) of the gradients into owner-contiguous shards
+       (the data-parallel gradient reduction, done once, by owner);
+    2. each rank runs the batched SCAO step on the parameters it owns;
+    3. all-gather of the updated parameters.
+
+Because the step is independent per parameter (the LARS trust ratio and the
+curvature clip are per-parameter reductions), the result is identical to the
+single-GPU step on the averaged gradient.  ``sync_preconditioners`` and
+``wrap_scao_for_fsdp`` keep the reference's API for replicated optimizers.
+"""
+from __future__ import annotations
+
+import heapq
+
+import torch
+import torch.distributed as dist
+
+ALIGN = 64   # elements: every parameter slot starts on a 128-byte boundary
+
+
+def partition(costs, world):
+    """Greedy LPT: assign items (largest cost first) to the least-loaded rank.
+    Deterministic (ties broken by rank, then item index)."""
+    order = sorted(range(len(costs)), key=lambda i: (-costs[i], i))
+    heap = [(0, r) for r in range(world)]
+    owner = [0] * len(costs)
+    for i in order:
+        load, r = heapq.heappop(heap)
+        owner[i] = r
+        heapq.heappush(heap, (load + costs[i], r))
+    return owner
+
+
+def _round_up(x, k):
+    return (x + k - 1) // k * k
+
+
+class FlatLayout:
+    """Owner-major flat layout: rank r's parameters (in model order) occupy
+    [r*shard, (r+1)*shard) of a flat buffer."""
+
+    def __init__(self, numels, owner, world):
+        self.world = world
+        self.owner = owner
+        self.offsets = [0] * len(numels)
+        fill = [0] * world
+        for i, n in enumerate(numels):
+            r = owner[i]
+            self.offsets[i] = fill[r]
+            fill[r] += _round_up(n, ALIGN)
+        self.shard = max(max(fill), ALIGN)
+        self.numels = numels
+
+    def global_offset(self, i):
+        return self.owner[i] * self.shard + self.offsets[i]
+
+
+class ShardedSCAO:
+    """Owner-compute wrapper.  ``make_inner(list of (param, spec))`` builds the
+    per-rank optimizer over the owned parameters (a ``scao_b200.SCAO`` on GPUs;
+    tests inject CPU stand-ins).  Parameters are re-pointed into one flat
+    buffer so the all-gather writes them in place."""
+
+    def __init__(self, params, workload, make_inner, group=None, costs=None):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.params = list(params)
+        self.specs = list(workload.params)
+        numels = [p.numel() for p in self.params]
+        self.owner = partition(costs or numels, self.world)
+        self.layout = FlatLayout(numels, self.owner, self.world)
+        p0 = self.params[0]
+        self.dtype, self.device = p0.dtype, p0.device
+        n = self.layout.shard * self.world
+        self.flat_p = torch.zeros(n, dtype=self.dtype, device=self.device)
+        for i, p in enumerate(self.params):
+            o = self.layout.global_offset(i)
+            view = self.flat_p[o:o + p.numel()].view_as(p)
+            view.copy_(p.data)
+            p.data = view
+        self.my = [i for i in range(len(self.params)) if self.owner[i] == self.rank]
+        s0 = self.rank * self.layout.shard
+        self.my_p = self.flat_p[s0:s0 + self.layout.shard]
+        self.my_g = torch.zeros(self.layout.shard, dtype=self.dtype, device=self.device)
+        for i in self.my:
+            o = self.layout.offsets[i]
+            self.params[i].grad = self.my_g[o:o + numels[i]].view_as(self.params[i])
+        self.inner = make_inner([(self.params[i], self.specs[i]) for i in self.my])
+        self.global_step = 0
+        self.grad_sets = []
+        self.cur = None
+        self.nccl = dist.get_backend(group) == "nccl"
+
+    def owned_specs(self):
+        return [self.specs[i] for i in self.my]
+
+    # gradients ------------------------------------------------------------
+    def stage_grads(self, full_grads):
+        """Lay a full (per-rank) gradient list out as one owner-major flat
+        buffer; returns its index for ``use_grads``."""
+        flat = torch.zeros(self.layout.shard * self.world, dtype=self.dtype, device=self.device)
+        for i, g in enumerate(full_grads):
+            o = self.layout.global_offset(i)
+            flat[o:o + g.numel()].copy_(g.reshape(-1))
+        self.grad_sets.append(flat)
+        return len(self.grad_sets) - 1
+
+    def load_grads(self, full_grads):
+        key = id(full_grads)
+        if not hasattr(self, "_staged"):
+            self._staged = {}
+        if key not in self._staged:
+            self._staged[key] = self.stage_grads(full_grads)
+        self.cur = self.grad_sets[self._staged[key]]
+
+    def flat_grad_from_params(self):
+        """Training-loop entry: gather every parameter's local .grad (as left
+        by backward) into the owner-major flat buffer."""
+        flat = torch.zeros(self.layout.shard * self.world, dtype=self.dtype, device=self.device)
+        for i, p in enumerate(self.params):
+            if p.grad is None:
+                continue
+            o = self.layout.global_offset(i)
+            flat[o:o + p.numel()].copy_(p.grad.reshape(-1))
+        self.cur = flat
+
+    # step -------------------------------------------------------------------
+    def step(self):
+        self.global_step += 1
+        if self.cur is None:
+            raise RuntimeError("no gradients staged (load_grads / flat_grad_from_params)")
+        if self.nccl:
+            dist.reduce_scatter_tensor(self.my_g, self.cur, op=dist.ReduceOp.AVG,
+                                       group=self.group)
+        else:
+            tmp = self.cur.clone()
+            dist.all_reduce(tmp, group=self.group)
+            s0 = self.rank * self.layout.shard
+            self.my_g.copy_(tmp[s0:s0 + self.layout.shard] / self.world)
+        if self.my:
+            self.inner.step()
+        if self.nccl:
+            dist.all_gather_into_tensor(self.flat_p, self.my_p, group=self.group)
+        else:
+            parts = list(self.flat_p.chunk(self.world))
+            dist.all_gather(parts, self.my_p.clone(), group=self.group)
+            self.flat_p.copy_(torch.cat(parts))
+
+    @property
+    def _global_step(self):
+        return self.global_step
+
+
+# ---------------------------------------------------------------------------
+# reference-API helpers for replicated optimizers (scao/distributed.py)
+# ---------------------------------------------------------------------------
+
+def sync_preconditioners(optimizer, process_group=None):
+    """scao/distributed.py:60-128: all-reduce-average the preconditioner state
+    of a replicated optimizer.  Here the state lives in flat arenas, so the
+    average is one all-reduce per arena; int8 factors are dequantised,
+    averaged and requantised on the device (same as the reference's
+    dequant -> all_reduce -> quant)."""
+    if not dist.is_available() or not dist.is_initialized():
+        return
+    world = dist.get_world_size(process_group)
+    if world == 1:
+        return
+    plan = getattr(optimizer, "_plan", None)
+    if plan is None:
+        return
+    for t in (plan.u, plan.ev, plan.diag_ema):
+        dist.all_reduce(t, group=process_group)
+        t.div_(world)
+    if plan.int8_ema:
+        _requant_average(plan, process_group, world)
+    else:
+        dist.all_reduce(plan.fac, group=process_group)
+        plan.fac.div_(world)
+
+
+def wrap_scao_for_fsdp(optimizer):
+    """scao/distributed.py:131-160: run sync_preconditioners after every
+    curvature step."""
+    original = optimizer.step
+
+    def patched(closure=None):
+        out = original(closure)
+        step = next((s.get("step", 0) for s in optimizer.state.values() if "step" in s), 0)
+        if step % optimizer.defaults["precond_freq"] == 0:
+            sync_preconditioners(optimizer)
+        return out
+
+    optimizer.step = patched
+    return optimizer
+
+
+def _requant_average(plan, group, world):
+    """int8 factors: dequantise (utils.py:192-203), all-reduce, average,
+    requantise (utils.py:170-189) -- each step through the library's C ABI."""
+    import numpy as np
+    from . import _lib
+    L = _lib.lib()
+    stream = torch.cuda.current_stream(plan.device).cuda_stream
+    scratch = torch.empty(256, dtype=torch.uint8, device=plan.device)
+    sc = torch.zeros(1, dtype=torch.float64, device=plan.device)
+    lt = plan.ltab
+    for li in range(plan.n_leaves):
+        for side in (0, 1):
+            n = int(lt["a"][li] if side == 0 else lt["b"][li])
+            o = int(lt["lq_off"][li] if side == 0 else lt["rq_off"][li])
+            q = plan.fac[o:o + n * n]
+            am = float(np.float32(plan.absmax[2 * li + side].item()))
+            scale = 1.0 if am < 1e-30 else am / 127.0
+            x = torch.empty(n * n, dtype=torch.float32, device=plan.device)
+            _lib.check(L.scao_dequantize_sym_int8(q.data_ptr(), scale, n * n, x.data_ptr(),
+                                                  stream), "dequantize")
+            dist.all_reduce(x, group=group)
+            x.div_(world)
+            _lib.check(L.scao_quantize_sym_int8(x.data_ptr(), n * n, q.data_ptr(), sc.data_ptr(),
+                                                scratch.data_ptr(), stream), "quantize")
+            s_new = sc.item()
+            plan.absmax[2 * li + side] = float(np.float32(s_new * 127.0)) if s_new != 1.0 or \
+                bool(q.ne(0).any().item()) else 0.0

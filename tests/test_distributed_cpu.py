@@ -1,0 +1,90 @@
+"""Owner-compute sharding host logic on CPU: 2 gloo ranks (127.0.0.1)."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from scao_b200 import workloads
+from scao_b200.distributed import FlatLayout, ShardedSCAO, partition
+
+
+def test_partition_balanced_and_deterministic():
+    costs = [100, 7, 50, 50, 3, 99, 1, 60]
+    a = partition(costs, 3)
+    assert a == partition(costs, 3)
+    loads = [sum(c for c, o in zip(costs, a) if o == r) for r in range(3)]
+    assert max(loads) - min(loads) <= max(costs)
+    assert set(a) == {0, 1, 2}
+
+
+def test_flat_layout_disjoint_aligned():
+    numels = [10, 300, 64, 1, 1000]
+    owner = partition(numels, 2)
+    lay = FlatLayout(numels, owner, 2)
+    spans = sorted((lay.global_offset(i), lay.global_offset(i) + n) for i, n in enumerate(numels))
+    for (a0, a1), (b0, _) in zip(spans, spans[1:]):
+        assert a1 <= b0
+    assert all(lay.offsets[i] % 64 == 0 for i in range(len(numels)))
+    assert all(lay.offsets[i] + numels[i] <= lay.shard for i in range(len(numels)))
+
+
+class _SGD:
+    """Stand-in for the per-rank optimizer: p -= 0.1 * grad (grads are views
+    into the reduce-scattered shard)."""
+
+    def __init__(self, pairs):
+        self.ps = [p for p, _ in pairs]
+
+    def step(self):
+        for p in self.ps:
+            p.data.add_(p.grad, alpha=-0.1)
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        w = workloads.tiny()
+        torch.manual_seed(0)
+        params = [torch.randn(s.shape) for s in w.params]
+        ref = [p.clone() for p in params]
+        # per-rank gradients differ; the owner update must use their average
+        grads = [torch.full(s.shape, float(rank + 1)) * (i + 1) for i, s in enumerate(w.params)]
+        avg = [torch.full(s.shape, (1 + world) / 2.0) * (i + 1) for i, s in enumerate(w.params)]
+        opt = ShardedSCAO(params, w, _SGD)
+        opt.load_grads(grads)
+        opt.step()
+        errs = [float((p - (r - 0.1 * g)).abs().max()) for p, r, g in zip(params, ref, avg)]
+        ok = max(errs) < 1e-5
+        if not ok:
+            print(rank, errs, opt.my, flush=True)
+        q.put((rank, ok, sorted(opt.my)))
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def test_sharded_step_two_gloo_ranks():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert all(ok for _, ok, _ in res)
+    owned = sorted(i for _, _, m in res for i in m)
+    assert owned == list(range(len(workloads.tiny().params)))
