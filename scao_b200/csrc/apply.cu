@@ -568,6 +568,7 @@ extern "C" int scao_plan_step(const ScaoPlanDev* P, void* stream) {
                                  (int)proj_smem(128));
             pattr = true;
         }
+        ProfScope _ps(SLOT_PROJ, st);
         if (P->kpad_max <= 64) proj_kernel<64><<<P->n_panels, NT, proj_smem(64), st>>>(*P);
         else proj_kernel<128><<<P->n_panels, NT, proj_smem(128), st>>>(*P);
         SCAO_CHECK_LAUNCH();
