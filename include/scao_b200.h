@@ -185,6 +185,22 @@ SCAO_API int scao_int8_ema_update(const int8_t* q, double scale, const float* ne
                          double* scale_out, void* scratch, void* stream);
 SCAO_API int64_t scao_int8_ema_scratch_bytes(int64_t n);
 
+/* Allocation-free form of scao_int8_ema_update, same semantics and results.
+ * No counterpart in the reference.  For callers that cannot allocate device
+ * memory (a host with its own fixed device-memory pool, or a stream that
+ * must not see cudaMalloc/cudaFree): the staging buffer is a file-scope
+ * device array of scao_int8_ema_update_noalloc_max_n() = 1,048,576 elements
+ * (a 1024 x 1024 factor); larger n returns SCAO_ERR_ARG.  The first call on
+ * each device looks up that array's device address (cudaGetSymbolAddress)
+ * with the device current -- make that first call before any stream capture.
+ * All calls on a device share the one array: calls that overlap on the GPU
+ * (different streams without ordering) race and corrupt each other.       */
+SCAO_API int scao_int8_ema_update_noalloc(const int8_t* q, double scale,
+                                          const float* new_val, double rho,
+                                          int64_t n, int8_t* q_out,
+                                          double* scale_out, void* stream);
+SCAO_API int64_t scao_int8_ema_update_noalloc_max_n(void);
+
 /* Symmetric per-tensor quantisation alone (utils.py:170-189): x (n fp32)
  * -> q (int8), scale_out[0] (double, device).                              */
 SCAO_API int scao_quantize_sym_int8(const float* x, int64_t n, int8_t* q,

@@ -85,6 +85,9 @@ SIGNATURES = {
     "scao_int8_ema_update": (C.c_int, [_P, C.c_double, _P, C.c_double, C.c_int64, _P, _P,
                                        _P, _P]),
     "scao_int8_ema_scratch_bytes": (C.c_int64, [C.c_int64]),
+    "scao_int8_ema_update_noalloc": (C.c_int, [_P, C.c_double, _P, C.c_double, C.c_int64, _P,
+                                               _P, _P]),
+    "scao_int8_ema_update_noalloc_max_n": (C.c_int64, []),
     "scao_quantize_sym_int8": (C.c_int, [_P, C.c_int64, _P, _P, _P, _P]),
     "scao_dequantize_sym_int8": (C.c_int, [_P, C.c_double, C.c_int64, _P, _P]),
     "scao_plan_curvature": (C.c_int, [C.POINTER(PlanDev), _P, C.c_int, C.c_int, C.c_int,

@@ -14,6 +14,8 @@
 #include "common.cuh"
 #include "prof.cuh"
 
+#include <mutex>
+
 namespace {
 
 constexpr int kThreads = 256;
@@ -105,6 +107,68 @@ extern "C" int scao_dequantize_sym_int8(const int8_t* q, double scale, int64_t n
                                         float* out, void* stream) {
     if (n <= 0 || !q || !out) return SCAO_ERR_ARG;
     { ProfScope _ps(SLOT_QUANT, (cudaStream_t)stream); dequant_kernel<<<grid_for(n), kThreads, 0, (cudaStream_t)stream>>>(q, (float)scale, n, out); }
+    SCAO_CHECK_LAUNCH();
+    return SCAO_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of scao_int8_ema_update.
+//
+// Some callers cannot allocate device memory at all: code running inside a
+// host that owns a fixed memory pool (an inference server or a framework
+// plugin whose allocator is not reachable from this library), or a caller
+// that must not add cudaMalloc/cudaFree synchronisation points to its stream.
+// For them the fp32 staging buffer and the max|x| slot live in this
+// file-scope device array, sized for factors up to 1024 x 1024.  Every GPU
+// that loads the library holds these 4 MiB until the process exits.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr int64_t kNoAllocMaxN = int64_t(1) << 20;   // elements (a 1024 x 1024 factor)
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocMaxN + 64];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on the current device.  The name of the
+// array in host code is only a host-side stand-in, never a device pointer.
+int noalloc_scratch(float** out) {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+        return SCAO_ERR_LAUNCH;
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) {
+            (void)cudaGetLastError();
+            return SCAO_ERR_LAUNCH;
+        }
+        g_noalloc_ptr[dev] = (float*)p;
+    }
+    *out = g_noalloc_ptr[dev];
+    return SCAO_OK;
+}
+
+}  // namespace
+
+extern "C" int64_t scao_int8_ema_update_noalloc_max_n(void) { return kNoAllocMaxN; }
+
+extern "C" int scao_int8_ema_update_noalloc(const int8_t* q, double scale,
+                                            const float* new_val, double rho,
+                                            int64_t n, int8_t* q_out,
+                                            double* scale_out, void* stream) {
+    if (n <= 0 || n > kNoAllocMaxN || !q || !new_val || !q_out) return SCAO_ERR_ARG;
+    float* x = nullptr;
+    const int rc = noalloc_scratch(&x);
+    if (rc != SCAO_OK) return rc;
+    float* am = x + kNoAllocMaxN;
+    cudaStream_t st = (cudaStream_t)stream;
+    // the array keeps the previous call's contents: the max slot must restart at 0
+    if (cudaMemsetAsync(am, 0, sizeof(float), st) != cudaSuccess) return SCAO_ERR_LAUNCH;
+    { ProfScope _ps(SLOT_QUANT, st); ema_pass1_kernel<<<grid_for(n), kThreads, 0, st>>>(q, (float)scale, (float)rho, new_val, n, x, am); }
+    SCAO_CHECK_LAUNCH();
+    { ProfScope _ps(SLOT_QUANT, st); requant_kernel<<<grid_for(n), kThreads, 0, st>>>(x, n, am, q_out, scale_out); }
     SCAO_CHECK_LAUNCH();
     return SCAO_OK;
 }
