@@ -1,0 +1,117 @@
+// Minimal sm_100a tensor-core toolkit: tcgen05.mma (kind::f16, bf16 inputs,
+// fp32 accumulators in TMEM), shared-memory matrix descriptors for the
+// K-major no-swizzle canonical layout, TMEM allocation and loads, mbarriers.
+//
+// Canonical K-major SWIZZLE_NONE operand layout used by every kernel here:
+// the tile is cut into 8-row x 16-byte "core matrices" (8 bf16 along K);
+// element (r, k) of a tile with K columns sits at byte
+//     (r / 8) * SBO + (k / 8) * 128 + (r % 8) * 16 + (k % 8) * 2,
+// with LBO = 128 B (next core matrix along K) and SBO = 16 * K bytes (next
+// 8-row group).  One MMA consumes K = 16 (two core matrices along K); the
+// descriptor for k-step s starts at byte offset s * 256.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define TC_DEV __device__ __forceinline__
+
+TC_DEV uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// byte offset of element (r, k) in a canonical K-major tile with K columns
+TC_DEV uint32_t canon_off(int r, int k, int K) {
+    return (uint32_t)((r >> 3) * (16 * K) + (k >> 3) * 128 + (r & 7) * 16 + (k & 7) * 2);
+}
+
+// Shared-memory matrix descriptor (sm_100 format, version 1, no swizzle).
+TC_DEV uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+    d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+    d |= (uint64_t)1 << 46;            // version
+    return d;                          // base offset 0, lbo mode 0, layout 0 (no swizzle)
+}
+
+// Instruction descriptor: D fp32, A/B bf16, both K-major, M x N.
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) |
+           ((uint32_t)(M >> 4) << 24);
+}
+
+TC_DEV void tc_mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                        uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n"
+        :
+        : "r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+TC_DEV void tc_commit(uint64_t* mbar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 :: "r"(smem_u32(mbar)) : "memory");
+}
+
+// whole warp: allocate ncols TMEM columns, address written to *slot (smem)
+TC_DEV void tc_alloc(uint32_t* slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                 :: "r"(smem_u32(slot)), "r"(ncols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+TC_DEV void tc_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;"
+                 :: "r"(taddr), "r"(ncols) : "memory");
+}
+
+TC_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+TC_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// make generic-proxy shared-memory writes visible to the tensor core
+TC_DEV void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// 32 lanes x 32 bits, 16 consecutive columns per thread
+TC_DEV void tc_ld16(uint32_t taddr, float* v) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+          "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
+          "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+TC_DEV void mbar_init(uint64_t* mbar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(smem_u32(mbar)), "r"(count)
+                 : "memory");
+}
+
+// Bounded wait for phase `parity` of an mbarrier.  Returns false when the
+// iteration limit ran out (the caller records an error and exits cleanly).
+TC_DEV bool mbar_wait(uint64_t* mbar, uint32_t parity, uint32_t limit = (1u << 26)) {
+    const uint32_t a = smem_u32(mbar);
+    for (uint32_t it = 0; it < limit; ++it) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}\n"
+            : "=r"(ok) : "r"(a), "r"(parity) : "memory");
+        if (ok) return true;
+    }
+    return false;
+}
+
+// split an fp32 value into bf16 hi + bf16 lo (x ~= hi + lo to ~2^-17 relative)
+TC_DEV void split_bf16(float x, uint16_t& hi, uint16_t& lo) {
+    const __nv_bfloat16 h = __float2bfloat16_rn(x);
+    const float r = x - __bfloat162float(h);
+    hi = __bfloat16_as_ushort(h);
+    lo = __bfloat16_as_ushort(__float2bfloat16_rn(r));
+}

@@ -1,0 +1,75 @@
+// Known-answer check of the tcgen05 toolkit (tc.cuh): C = A * B^T for one
+// 128 x N tile, bf16 inputs, fp32 accumulate in TMEM.  Exposed through the C
+// ABI so the GPU tests can compare it with a float64 product.
+#include <cuda_bf16.h>
+
+#include "common.cuh"
+#include "prof.cuh"
+#include "tc.cuh"
+
+namespace {
+
+__global__ void __launch_bounds__(128)
+tc_selftest_kernel(const uint16_t* __restrict__ A, const uint16_t* __restrict__ B,
+                   float* __restrict__ C, int N, int K, int* err) {
+    extern __shared__ __align__(1024) unsigned char sm[];
+    unsigned char* sa = sm;                       // 128 x K
+    unsigned char* sb = sm + 128 * K * 2;         // N x K
+    __shared__ uint64_t mbar;
+    __shared__ uint32_t tslot;
+    const int tid = threadIdx.x, warp = tid >> 5;
+    for (int e = tid; e < 128 * K; e += 128) {
+        const int r = e / K, k = e % K;
+        *(uint16_t*)(sa + canon_off(r, k, K)) = A[e];
+    }
+    for (int e = tid; e < N * K; e += 128) {
+        const int r = e / K, k = e % K;
+        *(uint16_t*)(sb + canon_off(r, k, K)) = B[e];
+    }
+    uint32_t ncols = 32;
+    while ((int)ncols < N) ncols <<= 1;
+    if (warp == 0) tc_alloc(&tslot, ncols);
+    if (tid == 0) mbar_init(&mbar, 1);
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tslot;
+    if (tid == 0) {
+        const uint32_t idesc = idesc_bf16(128, N);
+        for (int s = 0; s < K / 16; ++s) {
+            const uint64_t ad = smem_desc(smem_u32(sa) + s * 256, 128, 16 * K);
+            const uint64_t bd = smem_desc(smem_u32(sb) + s * 256, 128, 16 * K);
+            tc_mma_bf16(tmem, ad, bd, idesc, s > 0);
+        }
+        tc_commit(&mbar);
+    }
+    const bool ok = mbar_wait(&mbar, 0);
+    if (!ok && err) atomicExch(err, 1);
+    tc_fence_after();
+    if (ok) {
+        const int row = warp * 32 + (tid & 31);
+        for (int c0 = 0; c0 < N; c0 += 16) {
+            float v[16];
+            tc_ld16(tmem + ((uint32_t)(warp * 32) << 16) + c0, v);
+            for (int c = 0; c < 16; ++c) C[row * N + c0 + c] = v[c];
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tc_dealloc(tmem, ncols);
+}
+
+}  // namespace
+
+extern "C" int scao_tc_selftest(const uint16_t* A, const uint16_t* B, float* C, int N, int K,
+                                int* err, void* stream) {
+    if (!A || !B || !C || N < 16 || N > 256 || N % 16 || K < 16 || K > 128 || K % 16)
+        return SCAO_ERR_ARG;
+    cudaStream_t st = (cudaStream_t)stream;
+    const size_t sm = (size_t)(128 + N) * K * 2;
+    cudaFuncSetAttribute(tc_selftest_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    { ProfScope _ps(SLOT_SEAM, st); tc_selftest_kernel<<<1, 128, sm, st>>>(A, B, C, N, K, err); }
+    SCAO_CHECK_LAUNCH();
+    return SCAO_OK;
+}
