@@ -100,6 +100,13 @@ typedef struct {
     int64_t hl_off, hr_off;/* small s x s arena offsets                     */
     int64_t evl_off, evr_off; /* eigenvalue arena offsets (sl, sr floats)   */
     int64_t w_off;         /* W = U_l*Delta scratch: a*kpad floats          */
+    /* bf16 hi/lo operand tiles for the tensor-core kernels (byte offsets;
+     * Kp = kpad rounded up to 16; tile layouts are the canonical K-major
+     * no-swizzle layout of tc.cuh):
+     *   ua: U_r rows, per 128-row tile [hi 128 x Kp][lo 128 x Kp]
+     *   ut: U_r^T,    per 64-row block of U_r [hi Kp x 64][lo Kp x 64]
+     *   wa: W rows,   per 128-row tile [hi 128 x Kp][lo 128 x Kp]          */
+    int64_t ua_off, ut_off, wa_off;
 } ScaoLeaf;
 
 /* Apply tile of a Kronecker leaf: 64x64 elements.                          */
@@ -146,6 +153,9 @@ typedef struct {
     double* global_norm_ema;     /* 1 double (device)                       */
     uint16_t* slow;              /* lookahead slow weights, 16-bit params   */
     float* slow32;               /* lookahead slow weights, fp32 params     */
+    uint8_t *ua, *ut, *wa;       /* operand tile arenas (see ScaoLeaf)      */
+    int32_t* err;                /* device error flag: set to 1 when a bounded
+                                    wait on the tensor core timed out       */
 } ScaoPlanDev;
 
 /* ---------------------------------------------------------------------- */
@@ -247,6 +257,12 @@ SCAO_API int scao_plan_eigen(const ScaoPlanDev* plan_host, const int32_t* leaf_i
  * moments, LARS trust ratio and the parameter write.  The per-step table
  * plan->step must already be on the device.                                */
 SCAO_API int scao_plan_step(const ScaoPlanDev* plan_host, void* stream);
+
+/* Refresh the bf16 hi/lo operand tiles (ua, ut) of the listed leaves from
+ * their fp32 eigenvectors; scao_plan_eigen does this itself, the plan
+ * builder calls it once after initialising U.                             */
+SCAO_API int scao_plan_prep_factors(const ScaoPlanDev* plan_host, const int32_t* leaf_ids,
+                                    int n_ids, void* stream);
 
 /* Lookahead (optimizer.py:356-365): slow += alpha (p - slow); p <- slow.
  * init=1 on the first sync copies p into slow first.                      */

@@ -38,7 +38,7 @@ LEAF_DT = np.dtype([
     ("panel_end", "<i4"), ("pad0", "<i4"),
     ("lq_off", "<i8"), ("rq_off", "<i8"), ("ul_off", "<i8"), ("ur_off", "<i8"),
     ("hl_off", "<i8"), ("hr_off", "<i8"), ("evl_off", "<i8"), ("evr_off", "<i8"),
-    ("w_off", "<i8")], align=True)
+    ("w_off", "<i8"), ("ua_off", "<i8"), ("ut_off", "<i8"), ("wa_off", "<i8")], align=True)
 
 TILE_DT = np.dtype([("leaf", "<i4"), ("row0", "<i4"), ("col0", "<i4"), ("pad0", "<i4")])
 PANEL_DT = np.dtype([("leaf", "<i4"), ("row0", "<i4"), ("nrows", "<i4"), ("pad0", "<i4")])
@@ -60,14 +60,15 @@ class PlanDev(C.Structure):
         ("eig_y", _P), ("eig_x", _P), ("eig_ax", _P), ("eig_h", _P), ("eig_v", _P),
         ("eig_aux", _P), ("w", _P), ("p_part", _P), ("tile_part", _P), ("chunk_part", _P),
         ("upd", _P), ("upd32", _P), ("leaf_nat2", _P), ("param_scalars", _P),
-        ("global_norm_ema", _P), ("slow", _P), ("slow32", _P),
+        ("global_norm_ema", _P), ("slow", _P), ("slow32", _P), ("ua", _P), ("ut", _P), ("wa", _P),
+        ("err", _P),
     ]
 
 
 def check_layout():
     assert PARAM_DT.itemsize == 56, PARAM_DT.itemsize
     assert STEP_DT.itemsize == 120, STEP_DT.itemsize
-    assert LEAF_DT.itemsize == 136, LEAF_DT.itemsize
+    assert LEAF_DT.itemsize == 160, LEAF_DT.itemsize
     assert CHUNK_DT.itemsize == 24, CHUNK_DT.itemsize
 
 
@@ -97,6 +98,7 @@ SIGNATURES = {
     "scao_plan_eigen": (C.c_int, [C.POINTER(PlanDev), _P, C.c_int, _P, _P, C.c_int,
                                   C.c_float, _P, C.c_int, C.c_int, _P]),
     "scao_plan_step": (C.c_int, [C.POINTER(PlanDev), _P]),
+    "scao_plan_prep_factors": (C.c_int, [C.POINTER(PlanDev), _P, C.c_int, _P]),
     "scao_plan_lookahead": (C.c_int, [C.POINTER(PlanDev), C.c_float, C.c_int, _P]),
     "scao_version": (C.c_char_p, []),
     "scao_tc_selftest": (C.c_int, [_P, _P, _P, C.c_int, C.c_int, _P, _P]),

@@ -23,12 +23,13 @@
 // use fmaf.  Parameter-dtype roundings are reproduced exactly.
 #include "common.cuh"
 #include "prof.cuh"
+#include "tc.cuh"
 
 namespace {
 
 constexpr int NT = 256;
 constexpr int TT = 64;       // apply tile edge
-constexpr int CH = 4096;     // flat chunk length (elements), 16 per thread
+constexpr int TC_T = 128;    // tensor-core tile edge (rows and columns)
 
 enum { PS_CLIPMUL = 0, PS_CLIP, PS_PNORM2, PS_UNORM2, PS_GNORM2, PS_ALPHA, PS_NAT, PS_TRUST };
 
@@ -198,15 +199,26 @@ leaf_coef_kernel(ScaoPlanDev P) {
     }
     nat = block_sum(nat, red);
     if (threadIdx.x == 0) P.leaf_nat2[blockIdx.x] = nat;
-    // W = U_l * Delta  (a x kp), only the first k columns of U_l contribute
+    // W = U_l * Delta (a x kp; only the first k columns of U_l contribute),
+    // written as bf16 hi/lo canonical tiles for the tensor-core apply
     const float* Ul = P.u + L.ul_off;
-    float* W = P.w + L.w_off;
-    for (int64_t e = threadIdx.x; e < (int64_t)L.a * kp; e += NT) {
-        const int i = (int)(e / kp), b = (int)(e % kp);
+    const int Kp = (kp + 15) & ~15;
+    const int64_t tbytes = (int64_t)TC_T * Kp * 2;
+    uint8_t* wa = P.wa + L.wa_off;
+    const int arows = (L.a + TC_T - 1) / TC_T * TC_T;
+    for (int64_t e = threadIdx.x; e < (int64_t)arows * Kp; e += NT) {
+        const int i = (int)(e / Kp), b = (int)(e % Kp);
         float s = 0.f;
-        const float* urow = Ul + (int64_t)i * L.sl;
-        for (int a = 0; a < k; ++a) s = fmaf(urow[a], D[a * kp + b], s);
-        W[e] = s;
+        if (i < L.a && b < kp) {
+            const float* urow = Ul + (int64_t)i * L.sl;
+            for (int a = 0; a < k; ++a) s = fmaf(urow[a], D[a * kp + b], s);
+        }
+        uint16_t h, l;
+        split_bf16(s, h, l);
+        uint8_t* t = wa + (int64_t)(i / TC_T) * 2 * tbytes;
+        const uint32_t o = canon_off(i % TC_T, b, Kp);
+        *(uint16_t*)(t + o) = h;
+        *(uint16_t*)(t + tbytes + o) = l;
     }
 }
 
@@ -552,6 +564,375 @@ lookahead_kernel(ScaoPlanDev P, float alpha, int init) {
     }
 }
 
+// ===========================================================================
+// Tensor-core (tcgen05) projection and correction.
+// fp32 operands (U_r, W) are pre-split into bf16 hi + lo canonical tiles
+// (prep_factors_kernel, leaf_coef_kernel) and brought into shared memory by
+// TMA bulk copies; products hi*hi + hi*lo + lo*hi keep ~2^-16 relative
+// accuracy.  bf16 gradients enter the MMA unsplit (exact); fp16/fp32
+// gradients are split while staging.
+// ===========================================================================
+
+// U_r rows -> ua tiles; U_r^T 64-row blocks -> ut tiles
+__global__ void __launch_bounds__(256)
+prep_factors_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids) {
+    const ScaoLeaf& L = P.leaves[ids[blockIdx.y]];
+    const int kp = L.kpad, Kp = (kp + 15) & ~15;
+    const float* Ur = P.u + L.ur_off;
+    const int brows = (L.b + TC_T - 1) / TC_T * TC_T;
+    const int64_t tb = (int64_t)TC_T * Kp * 2;
+    const int64_t nA = (int64_t)brows * Kp;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < nA; e += stride) {
+        const int j = (int)(e / Kp), c = (int)(e % Kp);
+        const float x = (j < L.b && c < kp) ? Ur[(int64_t)j * L.sr + c] : 0.f;
+        uint16_t h, l;
+        split_bf16(x, h, l);
+        uint8_t* t = P.ua + L.ua_off + (int64_t)(j / TC_T) * 2 * tb;
+        const uint32_t o = canon_off(j % TC_T, c, Kp);
+        *(uint16_t*)(t + o) = h;
+        *(uint16_t*)(t + tb + o) = l;
+    }
+    // ut: block kb holds B[n][c] = U_r[64 kb + c][n], n < Kp, c < 64
+    const int nkb = (L.b + 63) / 64;
+    const int64_t bb = (int64_t)Kp * 64 * 2;
+    const int64_t nB = (int64_t)nkb * 64 * Kp;
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < nB; e += stride) {
+        const int row = (int)(e / Kp), n = (int)(e % Kp);   // row = 64 kb + c
+        const float x = (row < L.b && n < kp) ? Ur[(int64_t)row * L.sr + n] : 0.f;
+        uint16_t h, l;
+        split_bf16(x, h, l);
+        uint8_t* t = P.ut + L.ut_off + (int64_t)(row / 64) * 2 * bb;
+        const uint32_t o = canon_off(n, row % 64, 64);
+        *(uint16_t*)(t + o) = h;
+        *(uint16_t*)(t + bb + o) = l;
+    }
+}
+
+// corr^T tile: D[j][i] = sum_b U_r[j][b] W[i][b], then the Adan epilogue.
+// 256 threads: warp w reads TMEM lanes 32*(w%4) (columns j) and the
+// 64-row half w/4 of the tile.
+__global__ void __launch_bounds__(256)
+apply_kron_tc_kernel(ScaoPlanDev P, int* err) {
+    const ScaoTile tl = P.tiles[blockIdx.x];
+    const ScaoLeaf& L = P.leaves[tl.leaf];
+    const ScaoParamStep& S = P.step[L.param];
+    if (S.phase != 2) return;
+    const ScaoParam& pr = P.params[L.param];
+    const int dt = pr.dtype;
+    const int Kp = (L.kpad + 15) & ~15;
+    extern __shared__ __align__(1024) unsigned char smx[];
+    const uint32_t tb = TC_T * Kp * 2;
+    unsigned char* A = smx;            // [hi][lo] of U_r rows j0..
+    unsigned char* B = smx + 2 * tb;   // [hi][lo] of W rows i0..
+    __shared__ uint64_t mbar_ld, mbar_mma;
+    __shared__ uint32_t tslot;
+    __shared__ float red[32];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int i0 = tl.row0, j0 = tl.col0;
+    if (tid == 0) {
+        mbar_init(&mbar_ld, 1);
+        mbar_init(&mbar_mma, 1);
+        fence_async_smem();
+        mbar_expect_tx(&mbar_ld, 4 * tb);
+        bulk_g2s(A, P.ua + L.ua_off + (int64_t)(j0 / TC_T) * 2 * tb, 2 * tb, &mbar_ld);
+        bulk_g2s(B, P.wa + L.wa_off + (int64_t)(i0 / TC_T) * 2 * tb, 2 * tb, &mbar_ld);
+    }
+    if (warp == 0) tc_alloc(&tslot, TC_T);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tslot;
+    bool ok = mbar_wait(&mbar_ld, 0);
+    if (tid == 0 && ok) {
+        const uint32_t idesc = idesc_bf16(TC_T, TC_T);
+        const uint32_t sbo = 16 * Kp;
+        const uint32_t a0 = smem_u32(A), b0 = smem_u32(B);
+        for (int s = 0; s < Kp / 16; ++s) {
+            const uint64_t ah = smem_desc(a0 + s * 256, 128, sbo);
+            const uint64_t al = smem_desc(a0 + tb + s * 256, 128, sbo);
+            const uint64_t bh = smem_desc(b0 + s * 256, 128, sbo);
+            const uint64_t bl = smem_desc(b0 + tb + s * 256, 128, sbo);
+            tc_mma_bf16(tmem, ah, bh, idesc, s > 0);
+            tc_mma_bf16(tmem, ah, bl, idesc, 1);
+            tc_mma_bf16(tmem, al, bh, idesc, 1);
+        }
+        tc_commit(&mbar_mma);
+    }
+    ok = ok && mbar_wait(&mbar_mma, 0);
+    if (!ok && err) atomicExch(err, 1);
+    tc_fence_after();
+    float usq = 0.f, gsq = 0.f;
+    if (ok) {
+        const float* ps = P.param_scalars + L.param * 8;
+        const bool clip = ps[PS_CLIP] != 0.f;
+        const float clipmul = ps[PS_CLIPMUL];
+        const void* g = (const void*)S.g_ptr;
+        float* M = P.exp_avg + pr.offset;
+        float* V = P.exp_avg_sq + pr.offset;
+        float* Dd = P.exp_avg_diff + pr.offset;
+        float* Pv = P.prev_grad + pr.offset;
+        const int q = warp & 3, h = warp >> 2;
+        const int j = j0 + q * 32 + lane;
+        const bool jok = j < L.b;
+        const int64_t obase = (int64_t)L.row0 * L.ld + L.col0 + j;
+        for (int c0 = h * 64; c0 < h * 64 + 64; c0 += 16) {
+            float corr[16];
+            tc_ld16(tmem + ((uint32_t)(q * 32) << 16) + c0, corr);
+            const int ib = i0 + c0;
+            if (!jok || ib >= L.a) continue;
+            const int nr = min(16, L.a - ib);
+            if (nr == 16) {
+                // full chunk: issue all loads first (memory-level parallelism)
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    float gv[8], mv[8], vv[8], dv[8], pv[8];
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        const int64_t o = obase + (int64_t)(ib + half * 8 + c) * L.ld;
+                        gv[c] = load_dt(g, o, dt);
+                        mv[c] = __ldcs(M + o); vv[c] = __ldcs(V + o);
+                        dv[c] = __ldcs(Dd + o); pv[c] = __ldcs(Pv + o);
+                    }
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        const int64_t o = obase + (int64_t)(ib + half * 8 + c) * L.ld;
+                        const float gp = round_dt(fadd(gv[c], corr[half * 8 + c]), dt);
+                        const float u = adan_elem(S, dt, gv[c], gp, mv[c], vv[c], dv[c], pv[c],
+                                                  clip, clipmul);
+                        usq = fmaf(u, u, usq);
+                        gsq = fmaf(gv[c], gv[c], gsq);
+                        __stcs(M + o, mv[c]); __stcs(V + o, vv[c]);
+                        __stcs(Dd + o, dv[c]); __stcs(Pv + o, pv[c]);
+                        if (dt == SCAO_F32) P.upd32[pr.offset + o] = u;
+                        else store_dt(P.upd + pr.offset, o, dt, u);
+                    }
+                }
+            } else {
+                for (int c = 0; c < nr; ++c) {
+                    const int64_t o = obase + (int64_t)(ib + c) * L.ld;
+                    const float gv = load_dt(g, o, dt);
+                    float mv = M[o], vv = V[o], dv = Dd[o], pv = Pv[o];
+                    const float gp = round_dt(fadd(gv, corr[c]), dt);
+                    const float u = adan_elem(S, dt, gv, gp, mv, vv, dv, pv, clip, clipmul);
+                    usq = fmaf(u, u, usq);
+                    gsq = fmaf(gv, gv, gsq);
+                    M[o] = mv; V[o] = vv; Dd[o] = dv; Pv[o] = pv;
+                    if (dt == SCAO_F32) P.upd32[pr.offset + o] = u;
+                    else store_dt(P.upd + pr.offset, o, dt, u);
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tc_dealloc(tmem, TC_T);
+    usq = block_sum(usq, red);
+    gsq = block_sum(gsq, red);
+    if (tid == 0) {
+        P.tile_part[blockIdx.x * 4 + 0] = usq;
+        P.tile_part[blockIdx.x * 4 + 1] = gsq;
+    }
+}
+
+// Load one 128 x 64 block of the gradient panel (8 chunks of 8 elements per
+// thread) into registers as fp32, plus the decayed parameter's squares.
+struct GChunk { float v[8]; };
+
+__device__ __forceinline__ void load_gblock(const void* g, const void* pp, int dt, int64_t base,
+                                            int64_t ld, int nrows, int ncols, int c0, float wdm,
+                                            bool vec, GChunk* out, float& psq) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        const int ch = threadIdx.x + q * 128;       // 1024 chunks: 128 rows x 8 chunks
+        const int r = ch >> 3, cc = (ch & 7) * 8;
+        const int64_t off = base + (int64_t)r * ld + c0 + cc;
+        float gx[8], px[8];
+        if (r < nrows && vec && c0 + cc + 8 <= ncols) {
+            if (dt == SCAO_F32) {
+                const float4 a = *(const float4*)((const float*)g + off);
+                const float4 b = *(const float4*)((const float*)g + off + 4);
+                const float4 c = *(const float4*)((const float*)pp + off);
+                const float4 d = *(const float4*)((const float*)pp + off + 4);
+                gx[0] = a.x; gx[1] = a.y; gx[2] = a.z; gx[3] = a.w;
+                gx[4] = b.x; gx[5] = b.y; gx[6] = b.z; gx[7] = b.w;
+                px[0] = c.x; px[1] = c.y; px[2] = c.z; px[3] = c.w;
+                px[4] = d.x; px[5] = d.y; px[6] = d.z; px[7] = d.w;
+            } else {
+                const float4 a = load4_dt(g, off, dt), b = load4_dt(g, off + 4, dt);
+                const float4 c = load4_dt(pp, off, dt), d = load4_dt(pp, off + 4, dt);
+                gx[0] = a.x; gx[1] = a.y; gx[2] = a.z; gx[3] = a.w;
+                gx[4] = b.x; gx[5] = b.y; gx[6] = b.z; gx[7] = b.w;
+                px[0] = c.x; px[1] = c.y; px[2] = c.z; px[3] = c.w;
+                px[4] = d.x; px[5] = d.y; px[6] = d.z; px[7] = d.w;
+            }
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+                const float pd = round_dt(fmul(px[t], wdm), dt);
+                psq = fmaf(pd, pd, psq);
+            }
+        } else {
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+                gx[t] = 0.f;
+                if (r < nrows && c0 + cc + t < ncols) {
+                    gx[t] = load_dt(g, off + t, dt);
+                    const float pd = round_dt(fmul(load_dt(pp, off + t, dt), wdm), dt);
+                    psq = fmaf(pd, pd, psq);
+                }
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < 8; ++t) out[q].v[t] = gx[t];
+    }
+}
+
+// T = G_panel (128 x b) * U_r (b x Kp) on the tensor core (2-stage pipeline:
+// registers hold the next gradient block while the MMA consumes the current
+// one; U_r^T blocks arrive by TMA bulk copy), then P_part = U_l[rows]^T T
+// with FFMA, and sum p_dec^2 over the panel.
+__global__ void __launch_bounds__(128)
+proj_tc_kernel(ScaoPlanDev P, int* err) {
+    const ScaoPanel pn = P.panels[blockIdx.x];
+    const ScaoLeaf& L = P.leaves[pn.leaf];
+    const ScaoParamStep& S = P.step[L.param];
+    if (S.phase != 2) return;
+    const ScaoParam& pr = P.params[L.param];
+    const int dt = pr.dtype;
+    const int Kp = (L.kpad + 15) & ~15;
+    constexpr int KB = 64;
+    const int gparts = dt == SCAO_BF16 ? 1 : 2;
+    extern __shared__ __align__(1024) unsigned char smx[];
+    const uint32_t abytes = TC_T * KB * 2, bbytes = Kp * KB * 2;
+    const uint32_t sbytes = 2 * abytes + 2 * bbytes;   // [A hi][A lo][B hi][B lo]
+    __shared__ uint64_t mbar_b[2], mbar_m[2];
+    __shared__ uint32_t tslot;
+    __shared__ float red[32];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const void* g = (const void*)S.g_ptr;
+    const void* pp = (const void*)S.p_ptr;
+    const float* Ul = P.u + L.ul_off;
+    uint32_t ncols = 32;
+    while ((int)ncols < Kp) ncols <<= 1;
+    if (warp == 0) tc_alloc(&tslot, ncols);
+    if (tid == 0) {
+        for (int i = 0; i < 2; ++i) { mbar_init(&mbar_b[i], 1); mbar_init(&mbar_m[i], 1); }
+        fence_async_smem();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tslot;
+    const uint32_t idesc = idesc_bf16(TC_T, Kp);
+    const float wdm = S.wd_mult;
+    const int64_t base = (int64_t)(L.row0 + pn.row0) * L.ld + L.col0;
+    const bool vec = ((L.ld & 7) == 0) && ((L.col0 & 7) == 0) && ((S.g_ptr & 15) == 0) &&
+                     ((S.p_ptr & 15) == 0);
+    float psq = 0.f;
+    const int nkb = (L.b + KB - 1) / KB;
+    bool ok = true;
+    GChunk cur[8];
+    load_gblock(g, pp, dt, base, L.ld, pn.nrows, L.b, 0, wdm, vec, cur, psq);
+    for (int kb = 0; kb < nkb; ++kb) {
+        const int buf = kb & 1;
+        unsigned char* st = smx + buf * sbytes;
+        if (kb >= 2) ok = mbar_wait(&mbar_m[buf], ((kb - 2) >> 1) & 1) && ok;
+        if (tid == 0) {
+            mbar_expect_tx(&mbar_b[buf], 2 * bbytes);
+            bulk_g2s(st + 2 * abytes, P.ut + L.ut_off + (int64_t)kb * 2 * bbytes, 2 * bbytes,
+                     &mbar_b[buf]);
+        }
+        // registers -> canonical A tile(s): one 16-byte core-matrix row per chunk
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const int ch = tid + q * 128;
+            const int r = ch >> 3, cc = (ch & 7) * 8;
+            const uint32_t o = canon_off(r, cc, KB);
+            uint32_t hw[4], lw[4];
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                uint16_t h0, l0, h1, l1;
+                if (gparts == 1) {
+                    h0 = f_to_bf16_bits(cur[q].v[2 * t]); h1 = f_to_bf16_bits(cur[q].v[2 * t + 1]);
+                    l0 = l1 = 0;
+                } else {
+                    split_bf16(cur[q].v[2 * t], h0, l0);
+                    split_bf16(cur[q].v[2 * t + 1], h1, l1);
+                }
+                hw[t] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+                lw[t] = (uint32_t)l0 | ((uint32_t)l1 << 16);
+            }
+            *(uint4*)(st + o) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            if (gparts == 2) *(uint4*)(st + abytes + o) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        }
+        if (kb + 1 < nkb)
+            load_gblock(g, pp, dt, base, L.ld, pn.nrows, L.b, (kb + 1) * KB, wdm, vec, cur, psq);
+        fence_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+        if (tid == 0) {
+            ok = mbar_wait(&mbar_b[buf], (kb >> 1) & 1) && ok;
+            const uint32_t sa = smem_u32(st), sbh = sa + 2 * abytes, sbl = sbh + bbytes;
+            for (int s = 0; s < KB / 16; ++s) {
+                const uint64_t a0 = smem_desc(sa + s * 256, 128, 16 * KB);
+                const uint64_t dh = smem_desc(sbh + s * 256, 128, 16 * KB);
+                const uint64_t dl = smem_desc(sbl + s * 256, 128, 16 * KB);
+                tc_mma_bf16(tmem, a0, dh, idesc, (kb > 0 || s > 0));
+                tc_mma_bf16(tmem, a0, dl, idesc, 1);
+                if (gparts == 2) {
+                    const uint64_t a1 = smem_desc(sa + abytes + s * 256, 128, 16 * KB);
+                    tc_mma_bf16(tmem, a1, dh, idesc, 1);
+                }
+            }
+            tc_commit(&mbar_m[buf]);
+        }
+    }
+    const int lastbuf = (nkb - 1) & 1;
+    ok = mbar_wait(&mbar_m[lastbuf], ((nkb - 1) >> 1) & 1) && ok;
+    if (!ok && err) atomicExch(err, 1);
+    tc_fence_after();
+    __syncthreads();
+    float* Ts = (float*)smx;                  // 128 x (Kp+1)
+    float* Ls = Ts + TC_T * (Kp + 1);         // 128 x (Kp+1)
+    if (ok) {
+        const int r = warp * 32 + lane;
+        for (int c0 = 0; c0 < Kp; c0 += 16) {
+            float v[16];
+            tc_ld16(tmem + ((uint32_t)(warp * 32) << 16) + c0, v);
+            for (int c = 0; c < 16; ++c) Ts[r * (Kp + 1) + c0 + c] = v[c];
+        }
+    }
+    for (int e = tid; e < TC_T * Kp; e += 128) {
+        const int r = e / Kp, a = e - (e / Kp) * Kp;
+        Ls[r * (Kp + 1) + a] = (r < pn.nrows && a < L.kpad) ? Ul[(int64_t)(pn.row0 + r) * L.sl + a] : 0.f;
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tc_dealloc(tmem, ncols);
+    float* out = P.p_part + (int64_t)blockIdx.x * P.p_stride;
+    const int kp = L.kpad;
+    for (int e = tid; e < kp * kp; e += 128) {
+        const int a = e / kp, b = e - (e / kp) * kp;
+        float s = 0.f;
+        for (int r = 0; r < pn.nrows; ++r) s = fmaf(Ls[r * (Kp + 1) + a], Ts[r * (Kp + 1) + b], s);
+        out[e] = ok ? s : 0.f;
+    }
+    psq = block_sum(psq, red);
+    if (tid == 0) out[P.p_stride - 4] = psq;
+}
+
+size_t apply_tc_smem(int kpad) {
+    const int Kp = (kpad + 15) & ~15;
+    return (size_t)4 * TC_T * Kp * 2;
+}
+size_t proj_tc_smem(int kpad) {
+    const int Kp = (kpad + 15) & ~15;
+    const size_t stage = (size_t)2 * 128 * 64 * 2 + 2 * (size_t)Kp * 64 * 2;
+    const size_t epi = (size_t)2 * 128 * (Kp + 1) * 4;
+    return 2 * stage > epi ? 2 * stage : epi;
+}
+
 size_t proj_smem(int kp) {
     return (size_t)(16 * (TT + 4) + (16 + 2 * TT) * (kp + 4)) * 4;
 }
@@ -564,13 +945,14 @@ extern "C" int scao_plan_step(const ScaoPlanDev* P, void* stream) {
     if (P->n_panels > 0) {
         static bool pattr = false;
         if (!pattr) {
-            cudaFuncSetAttribute(proj_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)proj_smem(128));
+            cudaFuncSetAttribute(proj_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)proj_tc_smem(128));
+            cudaFuncSetAttribute(apply_kron_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)apply_tc_smem(128));
             pattr = true;
         }
-        ProfScope _ps(SLOT_PROJ, st);
-        if (P->kpad_max <= 64) proj_kernel<64><<<P->n_panels, NT, proj_smem(64), st>>>(*P);
-        else proj_kernel<128><<<P->n_panels, NT, proj_smem(128), st>>>(*P);
+        { ProfScope _ps(SLOT_PROJ, st);
+          proj_tc_kernel<<<P->n_panels, 128, proj_tc_smem(P->kpad_max), st>>>(*P, P->err); }
         SCAO_CHECK_LAUNCH();
     }
     if (P->n_chunks > 0) {
@@ -594,8 +976,8 @@ extern "C" int scao_plan_step(const ScaoPlanDev* P, void* stream) {
     { ProfScope _ps(SLOT_PARAM_PRE, st); param_pre_kernel<<<P->n_params, NT, 0, st>>>(*P); }
     SCAO_CHECK_LAUNCH();
     if (P->n_tiles > 0) {
-        const size_t sm = (size_t)2 * P->kpad_max * (TT + 4) * 4;
-        { ProfScope _ps(SLOT_APPLY_KRON, st); apply_kron_kernel<<<P->n_tiles, NT, sm, st>>>(*P); }
+        { ProfScope _ps(SLOT_APPLY_KRON, st);
+          apply_kron_tc_kernel<<<P->n_tiles, 256, apply_tc_smem(P->kpad_max), st>>>(*P, P->err); }
         SCAO_CHECK_LAUNCH();
     }
     if (P->n_chunks > 0) {
@@ -618,6 +1000,16 @@ extern "C" int scao_plan_lookahead(const ScaoPlanDev* P, float alpha, int init,
     if (!P) return SCAO_ERR_ARG;
     if (P->n_chunks == 0) return SCAO_OK;
     { ProfScope _ps(SLOT_LOOKAHEAD, (cudaStream_t)stream); lookahead_kernel<<<P->n_chunks, NT, 0, (cudaStream_t)stream>>>(*P, alpha, init); }
+    SCAO_CHECK_LAUNCH();
+    return SCAO_OK;
+}
+
+extern "C" int scao_plan_prep_factors(const ScaoPlanDev* P, const int32_t* leaf_ids, int n_ids,
+                                      void* stream) {
+    if (!P || n_ids < 0) return SCAO_ERR_ARG;
+    if (n_ids == 0) return SCAO_OK;
+    cudaStream_t st = (cudaStream_t)stream;
+    { ProfScope _ps(SLOT_EIG_RANK, st); prep_factors_kernel<<<dim3(16, n_ids), 256, 0, st>>>(*P, leaf_ids); }
     SCAO_CHECK_LAUNCH();
     return SCAO_OK;
 }

@@ -628,5 +628,5 @@ extern "C" int scao_plan_eigen(const ScaoPlanDev* P, const int32_t* leaf_ids, in
     }
     { ProfScope _ps(SLOT_EIG_RANK, st); eig_rank_kernel<<<(n_ids + 127) / 128, 128, 0, st>>>(*P, leaf_ids, n_ids, eps_sparse, status); }
     SCAO_CHECK_LAUNCH();
-    return SCAO_OK;
+    return scao_plan_prep_factors(P, leaf_ids, n_ids, stream);
 }

@@ -115,3 +115,15 @@ TC_DEV void split_bf16(float x, uint16_t& hi, uint16_t& lo) {
     hi = __bfloat16_as_ushort(h);
     lo = __bfloat16_as_ushort(__float2bfloat16_rn(r));
 }
+
+// TMA bulk copy (non-tensor) global -> shared, completion counted in bytes
+// on an mbarrier.  Both addresses 16-byte aligned, size a multiple of 16.
+TC_DEV void mbar_expect_tx(uint64_t* mbar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+                 :: "r"(smem_u32(mbar)), "r"(bytes) : "memory");
+}
+TC_DEV void bulk_g2s(void* dst_smem, const void* src_gmem, uint32_t bytes, uint64_t* mbar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        :: "r"(smem_u32(dst_smem)), "l"(src_gmem), "r"(bytes), "r"(smem_u32(mbar)) : "memory");
+}

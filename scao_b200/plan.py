@@ -16,8 +16,8 @@ import torch
 from . import _lib
 from ._lib import CHUNK_DT, LEAF_DT, PANEL_DT, PARAM_DT, STEP_DT, TILE_DT
 
-TILE = 64        # apply tile edge (apply.cu TT)
-PANEL = 64       # projection panel rows
+TILE = 128       # apply tile edge (apply.cu TC_T)
+PANEL = 128      # projection panel rows
 CHUNK = 4096     # flat chunk length
 SMAX = 160       # largest eigen subspace width (eig.cu SMAX)
 
@@ -93,6 +93,7 @@ class Plan:
         h_off = 0
         ev_off = 0
         w_off = 0
+        ua_off = ut_off = wa_off = 0
         kpad_max = 0
         self.eps_sparse = []
         self.rho_leaf = []
@@ -154,6 +155,13 @@ class Plan:
                     ev_off += _round_up(sr, 4)
                     L["w_off"] = w_off
                     w_off += _round_up(a * kpad, 4)
+                    kp16 = _round_up(kpad, 16)
+                    L["ua_off"] = ua_off
+                    ua_off += -(-b // 128) * 2 * 128 * kp16 * 2
+                    L["ut_off"] = ut_off
+                    ut_off += -(-b // 64) * 2 * kp16 * 64 * 2
+                    L["wa_off"] = wa_off
+                    wa_off += -(-a // 128) * 2 * 128 * kp16 * 2
                     leaves.append(L)
                     mine.append(li)
                     self.eps_sparse.append(g["epsilon_sparse"])
@@ -174,6 +182,7 @@ class Plan:
         self.kpad_max = kpad_max
         self.p_stride = kpad_max * kpad_max + 4
         self.n_leaves = len(leaves)
+        self._tile_bytes = (ua_off, ut_off, wa_off)
         self._alloc(fac_off, u_off, h_off, ev_off, w_off)
 
     # ------------------------------------------------------------------
@@ -222,6 +231,10 @@ class Plan:
         self.leaf_nat2 = z(self.n_leaves)
         self.param_scalars = z(self.n_params * 8)
         self.global_norm_ema = torch.ones(1, dtype=torch.float64, device=dev)
+        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.ua = z(self._tile_bytes[0], torch.uint8)
+        self.ut = z(self._tile_bytes[1], torch.uint8)
+        self.wa = z(self._tile_bytes[2], torch.uint8)
         self.slow = None
         self.slow32 = None
         self.t_eps_sparse = torch.tensor(self.eps_sparse or [0.0], dtype=torch.float32,
@@ -229,6 +242,12 @@ class Plan:
         self.t_bias = torch.zeros(max(self.n_leaves, 1), dtype=torch.float32, device=dev)
         self._init_factors()
         self.dev = PlanDev_from(self)
+        if self.n_leaves and self.device.type == "cuda":
+            import ctypes
+            ids = torch.arange(self.n_leaves, dtype=torch.int32, device=dev)
+            _lib.check(_lib.lib().scao_plan_prep_factors(
+                ctypes.byref(self.dev), ids.data_ptr(), self.n_leaves,
+                torch.cuda.current_stream(dev).cuda_stream), "scao_plan_prep_factors")
 
     def _init_factors(self):
         """L = R = 1e-4*I (int8: q = 127*I, absmax = float32(1e-4)), U = reversed
@@ -261,6 +280,11 @@ class Plan:
         self.ev.copy_(ev)
         self.absmax.fill_(float(eye_val))
         self.k.copy_(torch.from_numpy(L["kmin"].astype(np.int32)))
+
+    def check_error(self):
+        """Raise if a kernel recorded a timed-out wait (synchronises)."""
+        if int(self.err.item()):
+            raise RuntimeError("scao_b200: a tensor-core completion wait timed out")
 
     def ensure_slow(self):
         if self.slow is None:
@@ -304,4 +328,6 @@ def PlanDev_from(plan):
     d.chunk_part, d.upd, d.upd32 = ptr(plan.chunk_part), ptr(plan.upd), ptr(plan.upd32)
     d.leaf_nat2, d.param_scalars = ptr(plan.leaf_nat2), ptr(plan.param_scalars)
     d.global_norm_ema = ptr(plan.global_norm_ema)
+    d.err = ptr(plan.err)
+    d.ua, d.ut, d.wa = ptr(plan.ua), ptr(plan.ut), ptr(plan.wa)
     return d

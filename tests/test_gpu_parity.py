@@ -144,6 +144,7 @@ def run_gpu(name, steps=None):
         opt.step()
         ks.append([opt.state[p]["preconditioner"].k for p in params])
     torch.cuda.synchronize()
+    opt._plan.check_error()
     return p0, params, opt, np.array(ks)
 
 
