@@ -124,6 +124,8 @@ typedef struct {
     int32_t int8_ema;      /* 1: L/R stored int8 + absmax; 0: fp32          */
     int32_t kpad_max;      /* largest leaf kpad (<= 128)                    */
     int32_t p_stride;      /* floats per projection partial: kpad_max^2 + 4 */
+    int32_t kron_dtypes;   /* bit mask (1 << dtype) over Kronecker params   */
+    int32_t pad_;
     const ScaoParam* params;
     const ScaoLeaf* leaves;
     const ScaoTile* tiles;

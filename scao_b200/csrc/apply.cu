@@ -238,9 +238,6 @@ param_pre_kernel(ScaoPlanDev P) {
         for (int l = pr.leaf_begin + threadIdx.x; l < pr.leaf_end; l += NT) {
             const float bn = sqrtf(P.leaf_nat2[l]);
             nat2 = fmaf(bn, bn, nat2);
-            const ScaoLeaf& L = P.leaves[l];
-            for (int q = L.panel_begin; q < L.panel_end; ++q)
-                psq += P.p_part[(int64_t)q * P.p_stride + P.p_stride - 4];
         }
     } else {
         for (int c = pr.chunk_begin + threadIdx.x; c < pr.chunk_end; c += NT) {
@@ -256,7 +253,7 @@ param_pre_kernel(ScaoPlanDev P) {
         const bool clip = S.clip && nat > S.tau;
         ps[PS_CLIP] = clip ? 1.f : 0.f;
         ps[PS_CLIPMUL] = clip ? fdiv(S.tau, fmaxf(nat, S.eps)) : 1.f;
-        ps[PS_PNORM2] = psq;
+        if (pr.mode == 0) ps[PS_PNORM2] = psq;   // Kronecker params: from the apply tiles
         ps[PS_NAT] = nat;
     }
 }
@@ -449,12 +446,13 @@ param_post_kernel(ScaoPlanDev P) {
     const ScaoParamStep& S = P.step[pi];
     if (S.phase == 0) return;
     __shared__ float red[32];
-    float usq = 0.f, gsq = 0.f;
+    float usq = 0.f, gsq = 0.f, psq = 0.f;
     const bool kron2 = (S.phase == 2 && pr.mode == 1);
     if (kron2) {
         for (int t = pr.tile_begin + threadIdx.x; t < pr.tile_end; t += NT) {
             usq += P.tile_part[t * 4 + 0];
             gsq += P.tile_part[t * 4 + 1];
+            psq += P.tile_part[t * 4 + 2];
         }
     } else {
         for (int c = pr.chunk_begin + threadIdx.x; c < pr.chunk_end; c += NT) {
@@ -464,8 +462,10 @@ param_post_kernel(ScaoPlanDev P) {
     }
     usq = block_sum(usq, red);
     gsq = block_sum(gsq, red);
+    psq = block_sum(psq, red);
     if (threadIdx.x != 0) return;
     float* ps = P.param_scalars + pi * 8;
+    if (kron2) ps[PS_PNORM2] = psq;
     ps[PS_GNORM2] = gsq;
     if (S.phase != 2) return;
     ps[PS_UNORM2] = usq;
@@ -573,6 +573,13 @@ lookahead_kernel(ScaoPlanDev P, float alpha, int init) {
 // gradients are split while staging.
 // ===========================================================================
 
+// Panels whose gradient the cp.async path can stream (bf16, 16-byte rows).
+__device__ __forceinline__ bool proj_fast(const ScaoLeaf& L, const ScaoParamStep& S,
+                                          const ScaoParam& pr) {
+    return pr.dtype == SCAO_BF16 && ((L.ld & 7) == 0) && ((L.col0 & 7) == 0) &&
+           ((L.b & 7) == 0) && ((S.g_ptr & 15) == 0);
+}
+
 // U_r rows -> ua tiles; U_r^T 64-row blocks -> ut tiles
 __global__ void __launch_bounds__(256)
 prep_factors_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids) {
@@ -609,10 +616,11 @@ prep_factors_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids) {
     }
 }
 
-// corr^T tile: D[j][i] = sum_b U_r[j][b] W[i][b], then the Adan epilogue.
-// 256 threads: warp w reads TMEM lanes 32*(w%4) (columns j) and the
-// 64-row half w/4 of the tile.
-__global__ void __launch_bounds__(256)
+// corr^T tile on the tensor core, then a row-major streaming epilogue:
+// TMEM -> shared (corr[i][j]) -> every thread handles 4 consecutive columns
+// of a row (128-bit state accesses, 512 contiguous bytes per warp).  Also
+// accumulates ||round(p*(1-lr wd))||^2 for the LARS ratio.
+__global__ void __launch_bounds__(256, 2)
 apply_kron_tc_kernel(ScaoPlanDev P, int* err) {
     const ScaoTile tl = P.tiles[blockIdx.x];
     const ScaoLeaf& L = P.leaves[tl.leaf];
@@ -625,6 +633,8 @@ apply_kron_tc_kernel(ScaoPlanDev P, int* err) {
     const uint32_t tb = TC_T * Kp * 2;
     unsigned char* A = smx;            // [hi][lo] of U_r rows j0..
     unsigned char* B = smx + 2 * tb;   // [hi][lo] of W rows i0..
+    float* Cs = (float*)smx;           // after the MMA: corr[i][j], 128 x 132
+    constexpr int CLD = TC_T + 4;
     __shared__ uint64_t mbar_ld, mbar_mma;
     __shared__ uint32_t tslot;
     __shared__ float red[32];
@@ -659,80 +669,225 @@ apply_kron_tc_kernel(ScaoPlanDev P, int* err) {
         }
         tc_commit(&mbar_mma);
     }
-    ok = ok && mbar_wait(&mbar_mma, 0);
+    ok = mbar_wait(&mbar_mma, 0) && ok;
     if (!ok && err) atomicExch(err, 1);
     tc_fence_after();
-    float usq = 0.f, gsq = 0.f;
-    if (ok) {
-        const float* ps = P.param_scalars + L.param * 8;
-        const bool clip = ps[PS_CLIP] != 0.f;
-        const float clipmul = ps[PS_CLIPMUL];
-        const void* g = (const void*)S.g_ptr;
-        float* M = P.exp_avg + pr.offset;
-        float* V = P.exp_avg_sq + pr.offset;
-        float* Dd = P.exp_avg_diff + pr.offset;
-        float* Pv = P.prev_grad + pr.offset;
+    // the MMA has consumed A/B: reuse the staging area for corr[i][j]
+    {
         const int q = warp & 3, h = warp >> 2;
-        const int j = j0 + q * 32 + lane;
-        const bool jok = j < L.b;
-        const int64_t obase = (int64_t)L.row0 * L.ld + L.col0 + j;
+        const int jj = q * 32 + lane;
         for (int c0 = h * 64; c0 < h * 64 + 64; c0 += 16) {
-            float corr[16];
-            tc_ld16(tmem + ((uint32_t)(q * 32) << 16) + c0, corr);
-            const int ib = i0 + c0;
-            if (!jok || ib >= L.a) continue;
-            const int nr = min(16, L.a - ib);
-            if (nr == 16) {
-                // full chunk: issue all loads first (memory-level parallelism)
+            float v[16];
+            tc_ld16(tmem + ((uint32_t)(q * 32) << 16) + c0, v);
 #pragma unroll
-                for (int half = 0; half < 2; ++half) {
-                    float gv[8], mv[8], vv[8], dv[8], pv[8];
-#pragma unroll
-                    for (int c = 0; c < 8; ++c) {
-                        const int64_t o = obase + (int64_t)(ib + half * 8 + c) * L.ld;
-                        gv[c] = load_dt(g, o, dt);
-                        mv[c] = __ldcs(M + o); vv[c] = __ldcs(V + o);
-                        dv[c] = __ldcs(Dd + o); pv[c] = __ldcs(Pv + o);
-                    }
-#pragma unroll
-                    for (int c = 0; c < 8; ++c) {
-                        const int64_t o = obase + (int64_t)(ib + half * 8 + c) * L.ld;
-                        const float gp = round_dt(fadd(gv[c], corr[half * 8 + c]), dt);
-                        const float u = adan_elem(S, dt, gv[c], gp, mv[c], vv[c], dv[c], pv[c],
-                                                  clip, clipmul);
-                        usq = fmaf(u, u, usq);
-                        gsq = fmaf(gv[c], gv[c], gsq);
-                        __stcs(M + o, mv[c]); __stcs(V + o, vv[c]);
-                        __stcs(Dd + o, dv[c]); __stcs(Pv + o, pv[c]);
-                        if (dt == SCAO_F32) P.upd32[pr.offset + o] = u;
-                        else store_dt(P.upd + pr.offset, o, dt, u);
-                    }
-                }
-            } else {
-                for (int c = 0; c < nr; ++c) {
-                    const int64_t o = obase + (int64_t)(ib + c) * L.ld;
-                    const float gv = load_dt(g, o, dt);
-                    float mv = M[o], vv = V[o], dv = Dd[o], pv = Pv[o];
-                    const float gp = round_dt(fadd(gv, corr[c]), dt);
-                    const float u = adan_elem(S, dt, gv, gp, mv, vv, dv, pv, clip, clipmul);
-                    usq = fmaf(u, u, usq);
-                    gsq = fmaf(gv, gv, gsq);
-                    M[o] = mv; V[o] = vv; Dd[o] = dv; Pv[o] = pv;
-                    if (dt == SCAO_F32) P.upd32[pr.offset + o] = u;
-                    else store_dt(P.upd + pr.offset, o, dt, u);
-                }
-            }
+            for (int c = 0; c < 16; ++c) Cs[(c0 + c) * CLD + jj] = ok ? v[c] : 0.f;
         }
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 0) tc_dealloc(tmem, TC_T);
+    float usq = 0.f, gsq = 0.f, psq = 0.f;
+    const float* ps = P.param_scalars + L.param * 8;
+    const bool clip = ps[PS_CLIP] != 0.f;
+    const float clipmul = ps[PS_CLIPMUL];
+    const void* g = (const void*)S.g_ptr;
+    const void* pp = (const void*)S.p_ptr;
+    float* M = P.exp_avg + pr.offset;
+    float* V = P.exp_avg_sq + pr.offset;
+    float* Dd = P.exp_avg_diff + pr.offset;
+    float* Pv = P.prev_grad + pr.offset;
+    const float wdm = S.wd_mult;
+    const int cg = (tid & 31) * 4;          // 4 columns
+    const int jcol = j0 + cg;
+    const bool vec = ((L.ld & 3) == 0) && ((L.col0 & 3) == 0) && ((S.g_ptr & 15) == 0) &&
+                     ((S.p_ptr & 15) == 0) && ((pr.offset & 3) == 0) && (jcol + 3 < L.b);
+    const int nrow = min(TC_T, L.a - i0);
+    for (int rr = tid >> 5; rr < nrow; rr += 8) {
+        const int i = i0 + rr;
+        const int64_t o = (int64_t)(L.row0 + i) * L.ld + L.col0 + jcol;
+        const float4 cr = *(const float4*)&Cs[rr * CLD + cg];
+        const float crv[4] = {cr.x, cr.y, cr.z, cr.w};
+        if (vec) {
+            const float4 gg = load4_dt(g, o, dt);
+            const float4 p4 = load4_dt(pp, o, dt);
+            float4 m4 = ldg_stream4(M + o), v4 = ldg_stream4(V + o);
+            float4 d4 = ldg_stream4(Dd + o), q4 = ldg_stream4(Pv + o);
+            float gv[4] = {gg.x, gg.y, gg.z, gg.w}, pv[4] = {p4.x, p4.y, p4.z, p4.w};
+            float mv[4] = {m4.x, m4.y, m4.z, m4.w}, vv[4] = {v4.x, v4.y, v4.z, v4.w};
+            float dv[4] = {d4.x, d4.y, d4.z, d4.w}, qv[4] = {q4.x, q4.y, q4.z, q4.w};
+            float uo[4];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const float gp = round_dt(fadd(gv[c], crv[c]), dt);
+                const float u = adan_elem(S, dt, gv[c], gp, mv[c], vv[c], dv[c], qv[c], clip, clipmul);
+                usq = fmaf(u, u, usq);
+                gsq = fmaf(gv[c], gv[c], gsq);
+                const float pd = round_dt(fmul(pv[c], wdm), dt);
+                psq = fmaf(pd, pd, psq);
+                uo[c] = round_dt(u, dt);
+            }
+            stg_stream4(M + o, make_float4(mv[0], mv[1], mv[2], mv[3]));
+            stg_stream4(V + o, make_float4(vv[0], vv[1], vv[2], vv[3]));
+            stg_stream4(Dd + o, make_float4(dv[0], dv[1], dv[2], dv[3]));
+            stg_stream4(Pv + o, make_float4(qv[0], qv[1], qv[2], qv[3]));
+            if (dt == SCAO_F32) store4_dt(P.upd32 + pr.offset, o, dt, make_float4(uo[0], uo[1], uo[2], uo[3]));
+            else store4_dt(P.upd + pr.offset, o, dt, make_float4(uo[0], uo[1], uo[2], uo[3]));
+        } else {
+            for (int c = 0; c < 4; ++c) {
+                if (jcol + c >= L.b) break;
+                const int64_t oc = o + c;
+                const float gv = load_dt(g, oc, dt);
+                float mv = M[oc], vv = V[oc], dv = Dd[oc], qv = Pv[oc];
+                const float gp = round_dt(fadd(gv, crv[c]), dt);
+                const float u = adan_elem(S, dt, gv, gp, mv, vv, dv, qv, clip, clipmul);
+                usq = fmaf(u, u, usq);
+                gsq = fmaf(gv, gv, gsq);
+                const float pd = round_dt(fmul(load_dt(pp, oc, dt), wdm), dt);
+                psq = fmaf(pd, pd, psq);
+                M[oc] = mv; V[oc] = vv; Dd[oc] = dv; Pv[oc] = qv;
+                if (dt == SCAO_F32) P.upd32[pr.offset + oc] = u;
+                else store_dt(P.upd + pr.offset, oc, dt, u);
+            }
+        }
+    }
     usq = block_sum(usq, red);
     gsq = block_sum(gsq, red);
+    psq = block_sum(psq, red);
     if (tid == 0) {
         P.tile_part[blockIdx.x * 4 + 0] = usq;
         P.tile_part[blockIdx.x * 4 + 1] = gsq;
+        P.tile_part[blockIdx.x * 4 + 2] = psq;
     }
+}
+
+// bf16 gradients: T = G_panel * U_r with the gradient streamed into shared
+// memory by cp.async (16-byte chunks land directly in the canonical layout),
+// a 4-stage pipeline, U_r^T blocks by TMA bulk copy.
+constexpr int PJ_STAGES = 4;
+__global__ void __launch_bounds__(128)
+proj_bf16_kernel(ScaoPlanDev P, int* err) {
+    const ScaoPanel pn = P.panels[blockIdx.x];
+    const ScaoLeaf& L = P.leaves[pn.leaf];
+    const ScaoParamStep& S = P.step[L.param];
+    if (S.phase != 2) return;
+    const ScaoParam& pr = P.params[L.param];
+    if (!proj_fast(L, S, pr)) return;        // handled by proj_tc_kernel
+    const int Kp = (L.kpad + 15) & ~15;
+    constexpr int KB = 64;
+    extern __shared__ __align__(1024) unsigned char smx[];
+    const uint32_t abytes = TC_T * KB * 2, bbytes = Kp * KB * 2;
+    const uint32_t sbytes = abytes + 2 * bbytes;     // [A][B hi][B lo]
+    __shared__ uint64_t mbar_b[PJ_STAGES], mbar_m[PJ_STAGES];
+    __shared__ uint32_t tslot;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint16_t* g = (const uint16_t*)S.g_ptr;
+    const float* Ul = P.u + L.ul_off;
+    uint32_t ncols = 32;
+    while ((int)ncols < Kp) ncols <<= 1;
+    if (warp == 0) tc_alloc(&tslot, ncols);
+    if (tid == 0) {
+        for (int i = 0; i < PJ_STAGES; ++i) { mbar_init(&mbar_b[i], 1); mbar_init(&mbar_m[i], 1); }
+        fence_async_smem();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tslot;
+    const uint32_t idesc = idesc_bf16(TC_T, Kp);
+    const int64_t base = (int64_t)(L.row0 + pn.row0) * L.ld + L.col0;
+    const int nkb = (L.b + KB - 1) / KB;
+    bool ok = true;
+    auto issue = [&](int kb) {
+        const int buf = kb % PJ_STAGES;
+        unsigned char* st = smx + buf * sbytes;
+        const int c0 = kb * KB;
+        if (tid == 0) {
+            mbar_expect_tx(&mbar_b[buf], 2 * bbytes);
+            bulk_g2s(st + abytes, P.ut + L.ut_off + (int64_t)kb * 2 * bbytes, 2 * bbytes,
+                     &mbar_b[buf]);
+        }
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const int ch = tid + q * 128;
+            const int r = ch >> 3, cc = (ch & 7) * 8;
+            const uint32_t dst = smem_u32(st + canon_off(r, cc, KB));
+            const bool in = r < pn.nrows && c0 + cc + 8 <= L.b;
+            const uint16_t* src = g + base + (int64_t)(in ? r : 0) * L.ld + (in ? c0 + cc : 0);
+            const int sz = in ? 16 : 0;      // zero-fill rows/cols outside the panel
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;"
+                         :: "r"(dst), "l"(src), "r"(sz) : "memory");
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    // prologue: always S-1 commit groups (empty ones past the last block) so
+    // that "wait_group S-1" in iteration kb means block kb has landed
+    for (int kb = 0; kb < PJ_STAGES - 1; ++kb) {
+        if (kb < nkb) issue(kb);
+        else asm volatile("cp.async.commit_group;" ::: "memory");
+    }
+    for (int kb = 0; kb < nkb; ++kb) {
+        const int buf = kb % PJ_STAGES;
+        const int nxt = kb + PJ_STAGES - 1;
+        if (nxt < nkb) {
+            // buffer of nxt was last used by block nxt - STAGES: wait for its MMA
+            if (nxt >= PJ_STAGES)
+                ok = mbar_wait(&mbar_m[nxt % PJ_STAGES], ((nxt - PJ_STAGES) / PJ_STAGES) & 1) && ok;
+            issue(nxt);
+        } else {
+            asm volatile("cp.async.commit_group;" ::: "memory");   // keep group count uniform
+        }
+        asm volatile("cp.async.wait_group %0;" :: "n"(PJ_STAGES - 1) : "memory");
+        fence_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+        if (tid == 0) {
+            ok = mbar_wait(&mbar_b[buf], (kb / PJ_STAGES) & 1) && ok;
+            const uint32_t sa = smem_u32(smx + buf * sbytes), sbh = sa + abytes, sbl = sbh + bbytes;
+            for (int s = 0; s < KB / 16; ++s) {
+                const uint64_t a0 = smem_desc(sa + s * 256, 128, 16 * KB);
+                tc_mma_bf16(tmem, a0, smem_desc(sbh + s * 256, 128, 16 * KB), idesc, (kb > 0 || s > 0));
+                tc_mma_bf16(tmem, a0, smem_desc(sbl + s * 256, 128, 16 * KB), idesc, 1);
+            }
+            tc_commit(&mbar_m[buf]);
+        }
+    }
+    ok = mbar_wait(&mbar_m[(nkb - 1) % PJ_STAGES], ((nkb - 1) / PJ_STAGES) & 1) && ok;
+    if (!ok && err) atomicExch(err, 1);
+    tc_fence_after();
+    __syncthreads();
+    float* Ts = (float*)smx;
+    float* Ls = Ts + TC_T * (Kp + 1);
+    {
+        const int r = warp * 32 + lane;
+        for (int c0 = 0; c0 < Kp; c0 += 16) {
+            float v[16];
+            tc_ld16(tmem + ((uint32_t)(warp * 32) << 16) + c0, v);
+            for (int c = 0; c < 16; ++c) Ts[r * (Kp + 1) + c0 + c] = ok ? v[c] : 0.f;
+        }
+    }
+    for (int e = tid; e < TC_T * Kp; e += 128) {
+        const int r = e / Kp, a = e - (e / Kp) * Kp;
+        Ls[r * (Kp + 1) + a] = (r < pn.nrows && a < L.kpad) ? Ul[(int64_t)(pn.row0 + r) * L.sl + a] : 0.f;
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tc_dealloc(tmem, ncols);
+    float* out = P.p_part + (int64_t)blockIdx.x * P.p_stride;
+    const int kp = L.kpad;
+    for (int e = tid; e < kp * kp; e += 128) {
+        const int a = e / kp, b = e - (e / kp) * kp;
+        float s = 0.f;
+        for (int r = 0; r < pn.nrows; ++r) s = fmaf(Ls[r * (Kp + 1) + a], Ts[r * (Kp + 1) + b], s);
+        out[e] = s;
+    }
+}
+
+size_t proj_bf16_smem(int kpad) {
+    const int Kp = (kpad + 15) & ~15;
+    const size_t stage = (size_t)128 * 64 * 2 + 2 * (size_t)Kp * 64 * 2;
+    const size_t epi = (size_t)2 * 128 * (Kp + 1) * 4;
+    return PJ_STAGES * stage > epi ? PJ_STAGES * stage : epi;
 }
 
 // Load one 128 x 64 block of the gradient panel (8 chunks of 8 elements per
@@ -828,6 +983,7 @@ proj_tc_kernel(ScaoPlanDev P, int* err) {
     const int64_t base = (int64_t)(L.row0 + pn.row0) * L.ld + L.col0;
     const bool vec = ((L.ld & 7) == 0) && ((L.col0 & 7) == 0) && ((S.g_ptr & 15) == 0) &&
                      ((S.p_ptr & 15) == 0);
+    if (proj_fast(L, S, pr)) return;         // handled by proj_bf16_kernel
     float psq = 0.f;
     const int nkb = (L.b + KB - 1) / KB;
     bool ok = true;
@@ -918,13 +1074,13 @@ proj_tc_kernel(ScaoPlanDev P, int* err) {
         for (int r = 0; r < pn.nrows; ++r) s = fmaf(Ls[r * (Kp + 1) + a], Ts[r * (Kp + 1) + b], s);
         out[e] = ok ? s : 0.f;
     }
-    psq = block_sum(psq, red);
-    if (tid == 0) out[P.p_stride - 4] = psq;
+    (void)psq;
 }
 
 size_t apply_tc_smem(int kpad) {
     const int Kp = (kpad + 15) & ~15;
-    return (size_t)4 * TC_T * Kp * 2;
+    const size_t st = (size_t)4 * TC_T * Kp * 2, cs = (size_t)TC_T * (TC_T + 4) * 4;
+    return st > cs ? st : cs;
 }
 size_t proj_tc_smem(int kpad) {
     const int Kp = (kpad + 15) & ~15;
@@ -949,10 +1105,14 @@ extern "C" int scao_plan_step(const ScaoPlanDev* P, void* stream) {
                                  (int)proj_tc_smem(128));
             cudaFuncSetAttribute(apply_kron_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)apply_tc_smem(128));
+            cudaFuncSetAttribute(proj_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)proj_bf16_smem(128));
             pattr = true;
         }
         { ProfScope _ps(SLOT_PROJ, st);
-          proj_tc_kernel<<<P->n_panels, 128, proj_tc_smem(P->kpad_max), st>>>(*P, P->err); }
+          proj_bf16_kernel<<<P->n_panels, 128, proj_bf16_smem(P->kpad_max), st>>>(*P, P->err);
+          if (P->kron_dtypes & ~(1 << SCAO_BF16))
+              proj_tc_kernel<<<P->n_panels, 128, proj_tc_smem(P->kpad_max), st>>>(*P, P->err); }
         SCAO_CHECK_LAUNCH();
     }
     if (P->n_chunks > 0) {

@@ -315,6 +315,8 @@ def PlanDev_from(plan):
     d.int8_ema = int(plan.int8_ema)
     d.kpad_max = plan.kpad_max
     d.p_stride = plan.p_stride
+    d.kron_dtypes = int(np.bitwise_or.reduce(
+        [1 << int(r["dtype"]) for r in plan.ptab if int(r["mode"]) == 1] or [0]))
     ptr = lambda t: t.data_ptr() if t is not None else None
     d.params, d.leaves, d.tiles = ptr(plan.t_params), ptr(plan.t_leaves), ptr(plan.t_tiles)
     d.panels, d.chunks, d.step = ptr(plan.t_panels), ptr(plan.t_chunks), ptr(plan.t_step)
