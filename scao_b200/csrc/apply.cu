@@ -620,7 +620,7 @@ prep_factors_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids) {
 // TMEM -> shared (corr[i][j]) -> every thread handles 4 consecutive columns
 // of a row (128-bit state accesses, 512 contiguous bytes per warp).  Also
 // accumulates ||round(p*(1-lr wd))||^2 for the LARS ratio.
-__global__ void __launch_bounds__(256, 2)
+__global__ void __launch_bounds__(256, 3)
 apply_kron_tc_kernel(ScaoPlanDev P, int* err) {
     const ScaoTile tl = P.tiles[blockIdx.x];
     const ScaoLeaf& L = P.leaves[tl.leaf];
@@ -763,7 +763,7 @@ apply_kron_tc_kernel(ScaoPlanDev P, int* err) {
 // bf16 gradients: T = G_panel * U_r with the gradient streamed into shared
 // memory by cp.async (16-byte chunks land directly in the canonical layout),
 // a 4-stage pipeline, U_r^T blocks by TMA bulk copy.
-constexpr int PJ_STAGES = 4;
+constexpr int PJ_STAGES = 3;
 __global__ void __launch_bounds__(128)
 proj_bf16_kernel(ScaoPlanDev P, int* err) {
     const ScaoPanel pn = P.panels[blockIdx.x];
@@ -1107,6 +1107,10 @@ extern "C" int scao_plan_step(const ScaoPlanDev* P, void* stream) {
                                  (int)apply_tc_smem(128));
             cudaFuncSetAttribute(proj_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)proj_bf16_smem(128));
+            // full shared-memory carveout so several CTAs fit per SM
+            cudaFuncSetAttribute(proj_bf16_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+            cudaFuncSetAttribute(proj_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+            cudaFuncSetAttribute(apply_kron_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
             pattr = true;
         }
         { ProfScope _ps(SLOT_PROJ, st);
