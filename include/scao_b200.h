@@ -283,9 +283,10 @@ SCAO_API int scao_prof_slots(void);
 
 /* Known-answer check of the tensor-core path: C (128 x N fp32) = A (128 x K
  * bf16, row-major) * B^T (B: N x K bf16, row-major); N, K multiples of 16,
- * N <= 256, K <= 128.  *err set to 1 if the MMA completion wait timed out. */
+ * N <= 256, K <= 128.  *err set to 1 if the MMA completion wait timed out.
+ * mn_major=1 stages both operands in the MN-major shared-memory layout.   */
 SCAO_API int scao_tc_selftest(const uint16_t* A, const uint16_t* B, float* C, int N, int K,
-                              int* err, void* stream);
+                              int* err, int mn_major, void* stream);
 
 /* Library identification. */
 SCAO_API const char* scao_version(void);

@@ -102,7 +102,7 @@ SIGNATURES = {
     "scao_plan_prep_factors": (C.c_int, [C.POINTER(PlanDev), _P, C.c_int, _P]),
     "scao_plan_lookahead": (C.c_int, [C.POINTER(PlanDev), C.c_float, C.c_int, _P]),
     "scao_version": (C.c_char_p, []),
-    "scao_tc_selftest": (C.c_int, [_P, _P, _P, C.c_int, C.c_int, _P, _P]),
+    "scao_tc_selftest": (C.c_int, [_P, _P, _P, C.c_int, C.c_int, _P, C.c_int, _P]),
     "scao_launch_count": (C.c_int64, []),
     "scao_prof_enable": (None, [C.c_int]),
     "scao_prof_read": (C.c_int, [_P, _P, C.c_int]),

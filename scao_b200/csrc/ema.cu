@@ -13,6 +13,7 @@
 // tcgen05 tensor-core path used for 16-bit gradients.
 #include "common.cuh"
 #include "prof.cuh"
+#include "tc.cuh"
 
 namespace {
 
@@ -61,11 +62,197 @@ __device__ __forceinline__ float load_a(const Prob& p, int i, int k) {
     return load_dt(p.g, (p.row0 + r) * p.ld + p.col0 + c, p.dt);
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-core gram + EMA for bf16 gradients (tcgen05, fp32 accumulators in
+// TMEM).  One CTA per lower-triangle 128 x 128 output tile; the gradient is
+// streamed by cp.async in 64-deep K blocks (3 stages).  L = G G^T reads
+// gradient rows (K-major operands); R = G^T G reads gradient columns, which
+// are contiguous along the output index, so both operands use the MN-major
+// layout and no transpose is needed.
+// ---------------------------------------------------------------------------
+constexpr int GT = 128, GKB = 64, GSTAGES = 3;
+
+__device__ __forceinline__ bool gram_tc_ok(const Prob& p, const ScaoLeaf& L) {
+    return p.dt == SCAO_BF16 && (L.ld % 8) == 0 && (L.col0 % 8) == 0 && (L.a % 8) == 0 &&
+           (L.b % 8) == 0 && ((reinterpret_cast<uintptr_t>(p.g) & 15) == 0);
+}
+
+__global__ void __launch_bounds__(128)
+gram_ema_tc_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, float* xbuf, int64_t xstride,
+                   float* amnew, float rho_f, float alpha_f, int* err) {
+    const Prob p = get_prob(P, ids, blockIdx.y, xbuf, xstride, amnew);
+    const ScaoLeaf& L = P.leaves[ids[blockIdx.y >> 1]];
+    if (!gram_tc_ok(p, L)) return;
+    const int nt = (p.n + GT - 1) / GT;
+    const int t = blockIdx.x;
+    if (t >= nt * (nt + 1) / 2) return;
+    int ti = 0;
+    while ((ti + 1) * (ti + 2) / 2 <= t) ++ti;
+    const int tj = t - ti * (ti + 1) / 2;
+    const int i0 = ti * GT, j0 = tj * GT;
+    const bool diag = ti == tj;
+    extern __shared__ __align__(1024) unsigned char smx[];
+    constexpr uint32_t OPB = GT * GKB * 2;          // one operand block, 16 KB
+    constexpr uint32_t SB = 2 * OPB;
+    __shared__ uint64_t mbar_m[GSTAGES];
+    __shared__ uint32_t tslot;
+    __shared__ float red[32];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint16_t* g = (const uint16_t*)p.g;
+    const int mn = p.side;    // R = G^T G uses MN-major operands
+    if (warp == 0) tc_alloc(&tslot, GT);
+    if (tid == 0) {
+        for (int i = 0; i < GSTAGES; ++i) mbar_init(&mbar_m[i], 1);
+        fence_async_smem();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tslot;
+    const uint32_t idesc = idesc_bf16(GT, GT, mn, mn);
+    const int nkb = (p.K + GKB - 1) / GKB;
+    auto issue = [&](int kb) {
+        unsigned char* st = smx + (kb % GSTAGES) * SB;
+        const int k0 = kb * GKB;
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {          // 2 operands x 1024 chunks / 128 threads
+            const int ch = tid + (q & 7) * 128;
+            const int opnd = q >> 3;
+            const int base = opnd ? j0 : i0;
+            int r, k;                           // output index r (< 128), depth k (< 64)
+            if (!mn) { r = ch >> 3; k = (ch & 7) * 8; } else { k = ch >> 4; r = (ch & 15) * 8; }
+            const bool in = (base + r < p.n) && (k0 + k < p.K);
+            int64_t off = 0;
+            if (in) off = mn ? (p.row0 + k0 + k) * p.ld + p.col0 + base + r
+                             : (p.row0 + base + r) * p.ld + p.col0 + k0 + k;
+            const uint32_t o = mn ? canon_off_mn(r, k, GT) : canon_off(r, k, GKB);
+            const uint32_t dst = smem_u32(st + opnd * OPB + o);
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;"
+                         :: "r"(dst), "l"(g + off), "r"(in ? 16 : 0) : "memory");
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    for (int kb = 0; kb < GSTAGES - 1; ++kb) {
+        if (kb < nkb) issue(kb);
+        else asm volatile("cp.async.commit_group;" ::: "memory");
+    }
+    bool ok = true;
+    for (int kb = 0; kb < nkb; ++kb) {
+        const int nxt = kb + GSTAGES - 1;
+        if (nxt < nkb) {
+            if (nxt >= GSTAGES)
+                ok = mbar_wait(&mbar_m[nxt % GSTAGES], ((nxt - GSTAGES) / GSTAGES) & 1) && ok;
+            issue(nxt);
+        } else {
+            asm volatile("cp.async.commit_group;" ::: "memory");
+        }
+        asm volatile("cp.async.wait_group %0;" :: "n"(GSTAGES - 1) : "memory");
+        fence_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+        if (tid == 0) {
+            const uint32_t sa = smem_u32(smx + (kb % GSTAGES) * SB), sb = sa + OPB;
+            for (int s = 0; s < GKB / 16; ++s) {
+                uint64_t ad, bd;
+                if (mn) {
+                    ad = smem_desc(sa + s * 2 * 16 * GT, 16 * GT, 128);
+                    bd = smem_desc(sb + s * 2 * 16 * GT, 16 * GT, 128);
+                } else {
+                    ad = smem_desc(sa + s * 256, 128, 16 * GKB);
+                    bd = smem_desc(sb + s * 256, 128, 16 * GKB);
+                }
+                tc_mma_bf16(tmem, ad, bd, idesc, (kb > 0 || s > 0));
+            }
+            tc_commit(&mbar_m[kb % GSTAGES]);
+        }
+    }
+    ok = mbar_wait(&mbar_m[(nkb - 1) % GSTAGES], ((nkb - 1) / GSTAGES) & 1) && ok;
+    if (!ok && err) atomicExch(err, 1);
+    tc_fence_after();
+    __syncthreads();
+    // TMEM (lane i, column j) -> Cs[i][j]
+    constexpr int CLD = GT + 1;
+    float* Cs = (float*)smx;
+    {
+        const int r = warp * 32 + lane;
+        for (int c0 = 0; c0 < GT; c0 += 16) {
+            float v[16];
+            tc_ld16(tmem + ((uint32_t)(warp * 32) << 16) + c0, v);
+#pragma unroll
+            for (int c = 0; c < 16; ++c) Cs[r * CLD + c0 + c] = ok ? v[c] : 0.f;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tc_dealloc(tmem, GT);
+    // EMA epilogue with the reference's separate roundings; rows i, lanes j
+    const int n = p.n;
+    float mx = 0.f;
+    const int jj = tid;
+    const int j = j0 + jj;
+    if (P.int8_ema) {
+        const int8_t* q = (const int8_t*)P.fac + p.fac_off;
+        const float s_old = quant_scale_f(P.absmax[p.pid]);
+        for (int ii = 0; ii < GT; ++ii) {
+            const int i = i0 + ii;
+            if (i >= n || j >= n) continue;
+            float x = 0.f;
+            if (!diag || ii >= jj) {
+                const float deq = __fmul_rn((float)q[(int64_t)i * n + j], s_old);
+                x = __fadd_rn(__fmul_rn(deq, rho_f), __fmul_rn(alpha_f, Cs[ii * CLD + jj]));
+                p.x[(int64_t)i * n + j] = x;
+                mx = fmaxf(mx, fabsf(x));
+            }
+            Cs[ii * CLD + jj] = x;
+        }
+    } else {
+        float* Lm = (float*)P.fac + p.fac_off;
+        for (int ii = 0; ii < GT; ++ii) {
+            const int i = i0 + ii;
+            if (i >= n || j >= n) continue;
+            float x = 0.f;
+            if (!diag || ii >= jj)
+                x = __fadd_rn(__fmul_rn(Lm[(int64_t)i * n + j], rho_f),
+                              __fmul_rn(alpha_f, Cs[ii * CLD + jj]));
+            Cs[ii * CLD + jj] = x;
+        }
+        __syncthreads();    // every old value read before any write
+        for (int ii = 0; ii < GT; ++ii) {
+            const int i = i0 + ii;
+            if (i < n && j < n && (!diag || ii >= jj)) Lm[(int64_t)i * n + j] = Cs[ii * CLD + jj];
+        }
+    }
+    __syncthreads();
+    // mirror: element (j, i) = x(i, j) for the strict lower part
+    {
+        float* dst = P.int8_ema ? p.x : (float*)P.fac + p.fac_off;
+        const int ii = tid;
+        const int i = i0 + ii;
+        for (int jr = 0; jr < GT; ++jr) {
+            const int jm = j0 + jr;
+            if (i >= n || jm >= n) continue;
+            if (diag && ii <= jr) continue;
+            dst[(int64_t)jm * n + i] = Cs[ii * CLD + jr];
+        }
+    }
+    if (P.int8_ema) {
+        mx = block_max(mx, red);
+        if (tid == 0) atomic_max_nonneg(p.am_new, mx);
+    }
+}
+
+size_t gram_tc_smem() {
+    const size_t st = (size_t)GSTAGES * 2 * GT * GKB * 2, cs = (size_t)GT * (GT + 1) * 4;
+    return st > cs ? st : cs;
+}
+
 __global__ void __launch_bounds__(NT)
 gram_ema_simt_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids,
                      float* xbuf, int64_t xstride, float* amnew, float rho_f,
                      float alpha_f) {
     const Prob p = get_prob(P, ids, blockIdx.y, xbuf, xstride, amnew);
+    if (gram_tc_ok(p, P.leaves[ids[blockIdx.y >> 1]])) return;   // tensor-core kernel
     const int nt = (p.n + TM - 1) / TM;
     int t = blockIdx.x;
     if (t >= nt * (nt + 1) / 2) return;
@@ -229,6 +416,21 @@ extern "C" int scao_plan_curvature(const ScaoPlanDev* P, const int32_t* leaf_ids
             return SCAO_ERR_LAUNCH;
         const int32_t* ids = leaf_ids + j0 / 2;
         dim3 grid(tiles, np);
+        {
+            static bool attr = false;
+            if (!attr) {
+                cudaFuncSetAttribute(gram_ema_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)gram_tc_smem());
+                cudaFuncSetAttribute(gram_ema_tc_kernel,
+                                     cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+                attr = true;
+            }
+            const int nt2 = (int)((mx + GT - 1) / GT);
+            ProfScope _ps2(SLOT_GRAM_TC, st);
+            gram_ema_tc_kernel<<<dim3(nt2 * (nt2 + 1) / 2, np), 128, gram_tc_smem(), st>>>(
+                *P, ids, xbuf, xstride, amnew, rho_f, alpha_f, P->err);
+        }
+        SCAO_CHECK_LAUNCH();
         { ProfScope _ps(SLOT_GRAM_EMA, st); gram_ema_simt_kernel<<<grid, NT, 0, st>>>(*P, ids, xbuf, xstride, amnew,
                                                    rho_f, alpha_f); }
         SCAO_CHECK_LAUNCH();

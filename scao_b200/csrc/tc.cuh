@@ -24,6 +24,14 @@ TC_DEV uint32_t canon_off(int r, int k, int K) {
     return (uint32_t)((r >> 3) * (16 * K) + (k >> 3) * 128 + (r & 7) * 16 + (k & 7) * 2);
 }
 
+// byte offset of element (mn, k) in a canonical MN-major no-swizzle tile with
+// MN extent M: 8 consecutive MN elements form a 16-byte core-matrix row, 8 K
+// rows make a 128-byte core matrix; MN groups are adjacent (SBO = 128 B) and
+// K groups of 8 are LBO = 16 * M bytes apart.
+TC_DEV uint32_t canon_off_mn(int mn, int k, int M) {
+    return (uint32_t)((mn >> 3) * 128 + (k >> 3) * (16 * M) + (k & 7) * 16 + (mn & 7) * 2);
+}
+
 // Shared-memory matrix descriptor (sm_100 format, version 1, no swizzle).
 TC_DEV uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
     uint64_t d = 0;
@@ -34,10 +42,11 @@ TC_DEV uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
     return d;                          // base offset 0, lbo mode 0, layout 0 (no swizzle)
 }
 
-// Instruction descriptor: D fp32, A/B bf16, both K-major, M x N.
-__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) |
-           ((uint32_t)(M >> 4) << 24);
+// Instruction descriptor: D fp32, A/B bf16, M x N; a_mn / b_mn select the
+// MN-major layout for that operand (default K-major).
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, int a_mn = 0, int b_mn = 0) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
+           ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
 TC_DEV void tc_mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,

@@ -11,7 +11,7 @@ namespace {
 
 __global__ void __launch_bounds__(128)
 tc_selftest_kernel(const uint16_t* __restrict__ A, const uint16_t* __restrict__ B,
-                   float* __restrict__ C, int N, int K, int* err) {
+                   float* __restrict__ C, int N, int K, int* err, int mn) {
     extern __shared__ __align__(1024) unsigned char sm[];
     unsigned char* sa = sm;                       // 128 x K
     unsigned char* sb = sm + 128 * K * 2;         // N x K
@@ -20,11 +20,11 @@ tc_selftest_kernel(const uint16_t* __restrict__ A, const uint16_t* __restrict__ 
     const int tid = threadIdx.x, warp = tid >> 5;
     for (int e = tid; e < 128 * K; e += 128) {
         const int r = e / K, k = e % K;
-        *(uint16_t*)(sa + canon_off(r, k, K)) = A[e];
+        *(uint16_t*)(sa + (mn ? canon_off_mn(r, k, 128) : canon_off(r, k, K))) = A[e];
     }
     for (int e = tid; e < N * K; e += 128) {
         const int r = e / K, k = e % K;
-        *(uint16_t*)(sb + canon_off(r, k, K)) = B[e];
+        *(uint16_t*)(sb + (mn ? canon_off_mn(r, k, N) : canon_off(r, k, K))) = B[e];
     }
     uint32_t ncols = 32;
     while ((int)ncols < N) ncols <<= 1;
@@ -36,10 +36,16 @@ tc_selftest_kernel(const uint16_t* __restrict__ A, const uint16_t* __restrict__ 
     tc_fence_after();
     const uint32_t tmem = tslot;
     if (tid == 0) {
-        const uint32_t idesc = idesc_bf16(128, N);
+        const uint32_t idesc = idesc_bf16(128, N, mn, mn);
         for (int s = 0; s < K / 16; ++s) {
-            const uint64_t ad = smem_desc(smem_u32(sa) + s * 256, 128, 16 * K);
-            const uint64_t bd = smem_desc(smem_u32(sb) + s * 256, 128, 16 * K);
+            uint64_t ad, bd;
+            if (mn) {   // K step of 16 = two K groups of LBO = 16*M bytes
+                ad = smem_desc(smem_u32(sa) + s * 2 * 16 * 128, 16 * 128, 128);
+                bd = smem_desc(smem_u32(sb) + s * 2 * 16 * N, 16 * N, 128);
+            } else {
+                ad = smem_desc(smem_u32(sa) + s * 256, 128, 16 * K);
+                bd = smem_desc(smem_u32(sb) + s * 256, 128, 16 * K);
+            }
             tc_mma_bf16(tmem, ad, bd, idesc, s > 0);
         }
         tc_commit(&mbar);
@@ -63,13 +69,13 @@ tc_selftest_kernel(const uint16_t* __restrict__ A, const uint16_t* __restrict__ 
 }  // namespace
 
 extern "C" int scao_tc_selftest(const uint16_t* A, const uint16_t* B, float* C, int N, int K,
-                                int* err, void* stream) {
+                                int* err, int mn_major, void* stream) {
     if (!A || !B || !C || N < 16 || N > 256 || N % 16 || K < 16 || K > 128 || K % 16)
         return SCAO_ERR_ARG;
     cudaStream_t st = (cudaStream_t)stream;
     const size_t sm = (size_t)(128 + N) * K * 2;
     cudaFuncSetAttribute(tc_selftest_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-    { ProfScope _ps(SLOT_SEAM, st); tc_selftest_kernel<<<1, 128, sm, st>>>(A, B, C, N, K, err); }
+    { ProfScope _ps(SLOT_SEAM, st); tc_selftest_kernel<<<1, 128, sm, st>>>(A, B, C, N, K, err, mn_major); }
     SCAO_CHECK_LAUNCH();
     return SCAO_OK;
 }
