@@ -156,6 +156,7 @@ typedef struct {
     uint16_t* slow;              /* lookahead slow weights, 16-bit params   */
     float* slow32;               /* lookahead slow weights, fp32 params     */
     uint8_t *ua, *ut, *wa;       /* operand tile arenas (see ScaoLeaf)      */
+    int32_t* counters;           /* 16 device ints of small bookkeeping      */
     int32_t* err;                /* device error flag: set to 1 when a bounded
                                     wait on the tensor core timed out       */
 } ScaoPlanDev;

@@ -61,7 +61,7 @@ class PlanDev(C.Structure):
         ("eig_y", _P), ("eig_x", _P), ("eig_ax", _P), ("eig_h", _P), ("eig_v", _P),
         ("eig_aux", _P), ("w", _P), ("p_part", _P), ("tile_part", _P), ("chunk_part", _P),
         ("upd", _P), ("upd32", _P), ("leaf_nat2", _P), ("param_scalars", _P),
-        ("global_norm_ema", _P), ("slow", _P), ("slow32", _P), ("ua", _P), ("ut", _P), ("wa", _P),
+        ("global_norm_ema", _P), ("slow", _P), ("slow32", _P), ("ua", _P), ("ut", _P), ("wa", _P), ("counters", _P),
         ("err", _P),
     ]
 

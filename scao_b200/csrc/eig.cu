@@ -552,6 +552,21 @@ __global__ void eig_rank_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, 
     }
 }
 
+// number of problems that still need the iterative solver
+__global__ void eig_count_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, int np) {
+    int c = 0;
+    for (int j = threadIdx.x; j < np; j += blockDim.x) {
+        const PInfo p = pinfo(P, ids, j);
+        if (!skip_iter(p)) ++c;
+    }
+    __shared__ int tot;
+    if (threadIdx.x == 0) tot = 0;
+    __syncthreads();
+    atomicAdd(&tot, c);
+    __syncthreads();
+    if (threadIdx.x == 0) P.counters[0] = tot;
+}
+
 size_t jacobi_smem(int s) {
     const int se = s + (s & 1), ld = se + 1;
     return (size_t)(2 * se * ld + 2 * se) * 4 + 32 * 4 + 64;
@@ -573,6 +588,14 @@ extern "C" int scao_plan_eigen(const ScaoPlanDev* P, const int32_t* leaf_ids, in
     const size_t dsm = 4096 * 8;
     { ProfScope _ps(SLOT_EIG_DIAG, st); eig_diag_kernel<<<np, NT, dsm, st>>>(*P, leaf_ids); }
     SCAO_CHECK_LAUNCH();
+    // all factors exactly diagonal (the common int8 case): skip the iterations
+    int n_iter = 0;
+    { ProfScope _ps(SLOT_EIG_PREP, st); eig_count_kernel<<<1, 256, 0, st>>>(*P, leaf_ids, np); }
+    SCAO_CHECK_LAUNCH();
+    if (cudaMemcpyAsync(&n_iter, P->counters, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+        return SCAO_ERR_LAUNCH;
+    if (n_iter == 0) max_iters = 0;
     const size_t jsm = jacobi_smem(smax);
     const size_t csm = (size_t)2 * smax * (smax + 1) * 4;
     static bool attr_done = false;

@@ -232,6 +232,7 @@ class Plan:
         self.param_scalars = z(self.n_params * 8)
         self.global_norm_ema = torch.ones(1, dtype=torch.float64, device=dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.counters = z(16, torch.int32)
         self.ua = z(self._tile_bytes[0], torch.uint8)
         self.ut = z(self._tile_bytes[1], torch.uint8)
         self.wa = z(self._tile_bytes[2], torch.uint8)
@@ -332,4 +333,5 @@ def PlanDev_from(plan):
     d.global_norm_ema = ptr(plan.global_norm_ema)
     d.err = ptr(plan.err)
     d.ua, d.ut, d.wa = ptr(plan.ua), ptr(plan.ut), ptr(plan.wa)
+    d.counters = ptr(plan.counters)
     return d
