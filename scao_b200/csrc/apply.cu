@@ -398,7 +398,37 @@ apply_flat_kernel(ScaoPlanDev P) {
     float usq = 0.f, gsq = 0.f;
     if (phase == 1) {
         const float a1 = round_dt((float)S.alpha1, dt);
-        for (int64_t e = ch.begin + threadIdx.x; e < ch.end; e += NT) {
+        auto adam4 = [&](float g_, float p_, float& m_, float& v_) {
+            const float pd = round_dt(fmul(p_, S.wd_mult), dt);
+            m_ = fmaf(g_, S.c1, fmul(m_, S.beta1));
+            v_ = fmaf(fmul(S.c2, g_), g_, fmul(v_, S.beta2));
+            const float den = fadd(fdiv(sqrtf(v_), S.sqrt_bc2), S.eps);
+            const float u = round_dt(fdiv(m_, den), dt);
+            gsq = fmaf(g_, g_, gsq);
+            return round_dt(fmaf(a1, u, pd), dt);
+        };
+        const bool vec = ((S.g_ptr & 15) == 0) && ((S.p_ptr & 15) == 0) &&
+                         ((pr.offset & 3) == 0) && ((ch.begin & 3) == 0);
+        int64_t vend = ch.begin;
+        if (vec) {
+            const int64_t n4 = (ch.end - ch.begin) >> 2;
+            vend = ch.begin + n4 * 4;
+            for (int64_t q = threadIdx.x; q < n4; q += NT) {
+                const int64_t e = ch.begin + q * 4;
+                const float4 g4 = load4_dt(g, e, dt), p4 = load4_dt(pp, e, dt);
+                float4 m4 = ldg_stream4(M + e), v4 = ldg_stream4(V + e);
+                float4 o;
+                o.x = adam4(g4.x, p4.x, m4.x, v4.x);
+                o.y = adam4(g4.y, p4.y, m4.y, v4.y);
+                o.z = adam4(g4.z, p4.z, m4.z, v4.z);
+                o.w = adam4(g4.w, p4.w, m4.w, v4.w);
+                store4_dt(pp, e, dt, o);
+                stg_stream4(M + e, m4);
+                stg_stream4(V + e, v4);
+                stg_stream4(Pv + e, g4);
+            }
+        }
+        for (int64_t e = vend + threadIdx.x; e < ch.end; e += NT) {
             const float gv = load_dt(g, e, dt);
             const float pd = round_dt(fmul(load_dt(pp, e, dt), S.wd_mult), dt);
             float m = fmaf(gv, S.c1, fmul(M[e], S.beta1));
@@ -554,7 +584,25 @@ lookahead_kernel(ScaoPlanDev P, float alpha, int init) {
     const int dt = pr.dtype;
     void* pp = (void*)S.p_ptr;
     void* sl = dt == SCAO_F32 ? (void*)(P.slow32 + pr.offset) : (void*)(P.slow + pr.offset);
-    for (int64_t e = ch.begin + threadIdx.x; e < ch.end; e += NT) {
+    auto la = [&](float p, float s) {
+        const float diff = round_dt(fsub(p, s), dt);
+        return round_dt(fadd(s, round_dt(fmul(alpha, diff), dt)), dt);
+    };
+    int64_t vend = ch.begin;
+    if (((S.p_ptr & 15) == 0) && ((pr.offset & 3) == 0) && ((ch.begin & 3) == 0)) {
+        const int64_t n4 = (ch.end - ch.begin) >> 2;
+        vend = ch.begin + n4 * 4;
+        for (int64_t q = threadIdx.x; q < n4; q += NT) {
+            const int64_t e = ch.begin + q * 4;
+            const float4 p4 = load4_dt(pp, e, dt);
+            const float4 s4 = init ? p4 : load4_dt(sl, e, dt);
+            const float4 o = make_float4(la(p4.x, s4.x), la(p4.y, s4.y), la(p4.z, s4.z),
+                                         la(p4.w, s4.w));
+            store4_dt(sl, e, dt, o);
+            store4_dt(pp, e, dt, o);
+        }
+    }
+    for (int64_t e = vend + threadIdx.x; e < ch.end; e += NT) {
         const float p = load_dt(pp, e, dt);
         float s = init ? p : load_dt(sl, e, dt);
         const float diff = round_dt(fsub(p, s), dt);
@@ -578,6 +626,32 @@ __device__ __forceinline__ bool proj_fast(const ScaoLeaf& L, const ScaoParamStep
                                           const ScaoParam& pr) {
     return pr.dtype == SCAO_BF16 && ((L.ld & 7) == 0) && ((L.col0 & 7) == 0) &&
            ((L.b & 7) == 0) && ((S.g_ptr & 15) == 0);
+}
+
+// P_part = Ls^T Ts (kp x kp) from two row-major [rows][ld] fp32 tiles in
+// shared memory; each thread accumulates 4 x 4 blocks (16 FMA per two
+// 128-bit shared loads).
+__device__ __forceinline__ void proj_pblock(const float* Ls, const float* Ts, int ld, int kp,
+                                            int nrows, float* out, bool ok) {
+    const int nb = (kp + 3) >> 2;
+    for (int blk = threadIdx.x; blk < nb * nb; blk += blockDim.x) {
+        const int a0 = (blk / nb) * 4, b0 = (blk % nb) * 4;
+        float acc[4][4] = {};
+        for (int r = 0; r < nrows; ++r) {
+            const float4 la = *(const float4*)&Ls[r * ld + a0];
+            const float4 tb = *(const float4*)&Ts[r * ld + b0];
+            const float av[4] = {la.x, la.y, la.z, la.w}, bv[4] = {tb.x, tb.y, tb.z, tb.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                if (a0 + i < kp && b0 + j < kp) out[(a0 + i) * kp + b0 + j] = ok ? acc[i][j] : 0.f;
+    }
 }
 
 // U_r rows -> ua tiles; U_r^T 64-row blocks -> ut tiles
@@ -857,36 +931,31 @@ proj_bf16_kernel(ScaoPlanDev P, int* err) {
     tc_fence_after();
     __syncthreads();
     float* Ts = (float*)smx;
-    float* Ls = Ts + TC_T * (Kp + 1);
+    float* Ls = Ts + TC_T * (Kp + 4);
     {
         const int r = warp * 32 + lane;
         for (int c0 = 0; c0 < Kp; c0 += 16) {
             float v[16];
             tc_ld16(tmem + ((uint32_t)(warp * 32) << 16) + c0, v);
-            for (int c = 0; c < 16; ++c) Ts[r * (Kp + 1) + c0 + c] = ok ? v[c] : 0.f;
+            for (int c = 0; c < 16; ++c) Ts[r * (Kp + 4) + c0 + c] = ok ? v[c] : 0.f;
         }
     }
     for (int e = tid; e < TC_T * Kp; e += 128) {
         const int r = e / Kp, a = e - (e / Kp) * Kp;
-        Ls[r * (Kp + 1) + a] = (r < pn.nrows && a < L.kpad) ? Ul[(int64_t)(pn.row0 + r) * L.sl + a] : 0.f;
+        Ls[r * (Kp + 4) + a] = (r < pn.nrows && a < L.kpad) ? Ul[(int64_t)(pn.row0 + r) * L.sl + a] : 0.f;
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 0) tc_dealloc(tmem, ncols);
     float* out = P.p_part + (int64_t)blockIdx.x * P.p_stride;
     const int kp = L.kpad;
-    for (int e = tid; e < kp * kp; e += 128) {
-        const int a = e / kp, b = e - (e / kp) * kp;
-        float s = 0.f;
-        for (int r = 0; r < pn.nrows; ++r) s = fmaf(Ls[r * (Kp + 1) + a], Ts[r * (Kp + 1) + b], s);
-        out[e] = s;
-    }
+    proj_pblock(Ls, Ts, Kp + 4, kp, pn.nrows, out, true);
 }
 
 size_t proj_bf16_smem(int kpad) {
     const int Kp = (kpad + 15) & ~15;
     const size_t stage = (size_t)128 * 64 * 2 + 2 * (size_t)Kp * 64 * 2;
-    const size_t epi = (size_t)2 * 128 * (Kp + 1) * 4;
+    const size_t epi = (size_t)2 * 128 * (Kp + 4) * 4;
     return PJ_STAGES * stage > epi ? PJ_STAGES * stage : epi;
 }
 
@@ -1050,30 +1119,25 @@ proj_tc_kernel(ScaoPlanDev P, int* err) {
     tc_fence_after();
     __syncthreads();
     float* Ts = (float*)smx;                  // 128 x (Kp+1)
-    float* Ls = Ts + TC_T * (Kp + 1);         // 128 x (Kp+1)
+    float* Ls = Ts + TC_T * (Kp + 4);         // 128 x (Kp+1)
     if (ok) {
         const int r = warp * 32 + lane;
         for (int c0 = 0; c0 < Kp; c0 += 16) {
             float v[16];
             tc_ld16(tmem + ((uint32_t)(warp * 32) << 16) + c0, v);
-            for (int c = 0; c < 16; ++c) Ts[r * (Kp + 1) + c0 + c] = v[c];
+            for (int c = 0; c < 16; ++c) Ts[r * (Kp + 4) + c0 + c] = v[c];
         }
     }
     for (int e = tid; e < TC_T * Kp; e += 128) {
         const int r = e / Kp, a = e - (e / Kp) * Kp;
-        Ls[r * (Kp + 1) + a] = (r < pn.nrows && a < L.kpad) ? Ul[(int64_t)(pn.row0 + r) * L.sl + a] : 0.f;
+        Ls[r * (Kp + 4) + a] = (r < pn.nrows && a < L.kpad) ? Ul[(int64_t)(pn.row0 + r) * L.sl + a] : 0.f;
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 0) tc_dealloc(tmem, ncols);
     float* out = P.p_part + (int64_t)blockIdx.x * P.p_stride;
     const int kp = L.kpad;
-    for (int e = tid; e < kp * kp; e += 128) {
-        const int a = e / kp, b = e - (e / kp) * kp;
-        float s = 0.f;
-        for (int r = 0; r < pn.nrows; ++r) s = fmaf(Ls[r * (Kp + 1) + a], Ts[r * (Kp + 1) + b], s);
-        out[e] = ok ? s : 0.f;
-    }
+    proj_pblock(Ls, Ts, Kp + 4, kp, pn.nrows, out, ok);
     (void)psq;
 }
 
@@ -1085,7 +1149,7 @@ size_t apply_tc_smem(int kpad) {
 size_t proj_tc_smem(int kpad) {
     const int Kp = (kpad + 15) & ~15;
     const size_t stage = (size_t)2 * 128 * 64 * 2 + 2 * (size_t)Kp * 64 * 2;
-    const size_t epi = (size_t)2 * 128 * (Kp + 1) * 4;
+    const size_t epi = (size_t)2 * 128 * (Kp + 4) * 4;
     return 2 * stage > epi ? 2 * stage : epi;
 }
 
