@@ -157,6 +157,10 @@ typedef struct {
     float* slow32;               /* lookahead slow weights, fp32 params     */
     uint8_t *ua, *ut, *wa;       /* operand tile arenas (see ScaoLeaf)      */
     int32_t* counters;           /* 16 device ints of small bookkeeping      */
+    /* chunk id lists: diagonal-mode params (static); params whose flat pass
+     * runs this step (Phase 1, or Phase 2 diagonal); Phase-2 params        */
+    const int32_t *diag_list, *flat_list, *p_list;
+    int32_t n_diag, n_flat, n_p, pad2_;
     int32_t* err;                /* device error flag: set to 1 when a bounded
                                     wait on the tensor core timed out       */
 } ScaoPlanDev;

@@ -49,7 +49,8 @@ def build(force=False, verbose=False):
     procs = []
     for src in sources():
         obj = os.path.join(objdir, os.path.basename(src)[:-3] + ".o")
-        cmd = [nvcc()] + ARCH + FLAGS + ["-c", src, "-o", obj]
+        extra = os.environ.get("SCAO_NVCC_FLAGS", "").split()
+        cmd = [nvcc()] + ARCH + FLAGS + extra + ["-c", src, "-o", obj]
         if verbose:
             print(" ".join(cmd))
         procs.append((src, subprocess.Popen(cmd, stdout=subprocess.PIPE,

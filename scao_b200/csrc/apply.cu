@@ -132,7 +132,8 @@ proj_kernel(ScaoPlanDev P) {
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(NT)
 diag_pre_kernel(ScaoPlanDev P) {
-    const ScaoChunk ch = P.chunks[blockIdx.x];
+    const int cid = P.diag_list[blockIdx.x];
+    const ScaoChunk ch = P.chunks[cid];
     const ScaoParam& pr = P.params[ch.param];
     const ScaoParamStep& S = P.step[ch.param];
     if (S.phase != 2 || pr.mode != 0) return;
@@ -152,8 +153,8 @@ diag_pre_kernel(ScaoPlanDev P) {
     nat = block_sum(nat, red);
     psq = block_sum(psq, red);
     if (threadIdx.x == 0) {
-        P.chunk_part[blockIdx.x * 4 + 2] = nat;
-        P.chunk_part[blockIdx.x * 4 + 3] = psq;
+        P.chunk_part[cid * 4 + 2] = nat;
+        P.chunk_part[cid * 4 + 3] = psq;
     }
 }
 
@@ -382,7 +383,8 @@ apply_kron_kernel(ScaoPlanDev P) {
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(NT)
 apply_flat_kernel(ScaoPlanDev P) {
-    const ScaoChunk ch = P.chunks[blockIdx.x];
+    const int cid = P.flat_list[blockIdx.x];
+    const ScaoChunk ch = P.chunks[cid];
     const ScaoParam& pr = P.params[ch.param];
     const ScaoParamStep& S = P.step[ch.param];
     const int phase = S.phase;
@@ -461,8 +463,8 @@ apply_flat_kernel(ScaoPlanDev P) {
     usq = block_sum(usq, red);
     gsq = block_sum(gsq, red);
     if (threadIdx.x == 0) {
-        P.chunk_part[blockIdx.x * 4 + 0] = usq;
-        P.chunk_part[blockIdx.x * 4 + 1] = gsq;
+        P.chunk_part[cid * 4 + 0] = usq;
+        P.chunk_part[cid * 4 + 1] = gsq;
     }
 }
 
@@ -539,7 +541,8 @@ __global__ void global_norm_kernel(ScaoPlanDev P) {
 // Phase-2 parameter write: p = round(round(p*(1-lr wd)) + alpha*u)
 __global__ void __launch_bounds__(NT)
 apply_p_kernel(ScaoPlanDev P) {
-    const ScaoChunk ch = P.chunks[blockIdx.x];
+    const int cid = P.p_list[blockIdx.x];
+    const ScaoChunk ch = P.chunks[cid];
     const ScaoParam& pr = P.params[ch.param];
     const ScaoParamStep& S = P.step[ch.param];
     if (S.phase != 2) return;
@@ -694,7 +697,13 @@ prep_factors_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids) {
 // TMEM -> shared (corr[i][j]) -> every thread handles 4 consecutive columns
 // of a row (128-bit state accesses, 512 contiguous bytes per warp).  Also
 // accumulates ||round(p*(1-lr wd))||^2 for the LARS ratio.
-__global__ void __launch_bounds__(256, 3)
+#ifndef SCAO_APPLY_NT
+#define SCAO_APPLY_NT 256
+#endif
+#ifndef SCAO_APPLY_MINB
+#define SCAO_APPLY_MINB 3
+#endif
+__global__ void __launch_bounds__(SCAO_APPLY_NT, SCAO_APPLY_MINB)
 apply_kron_tc_kernel(ScaoPlanDev P, int* err) {
     const ScaoTile tl = P.tiles[blockIdx.x];
     const ScaoLeaf& L = P.leaves[tl.leaf];
@@ -748,9 +757,10 @@ apply_kron_tc_kernel(ScaoPlanDev P, int* err) {
     tc_fence_after();
     // the MMA has consumed A/B: reuse the staging area for corr[i][j]
     {
+        constexpr int CPG = TC_T * 4 / (SCAO_APPLY_NT / 32);   // TMEM columns per warp group
         const int q = warp & 3, h = warp >> 2;
         const int jj = q * 32 + lane;
-        for (int c0 = h * 64; c0 < h * 64 + 64; c0 += 16) {
+        for (int c0 = h * CPG; c0 < h * CPG + CPG; c0 += 16) {
             float v[16];
             tc_ld16(tmem + ((uint32_t)(q * 32) << 16) + c0, v);
 #pragma unroll
@@ -776,7 +786,7 @@ apply_kron_tc_kernel(ScaoPlanDev P, int* err) {
     const bool vec = ((L.ld & 3) == 0) && ((L.col0 & 3) == 0) && ((S.g_ptr & 15) == 0) &&
                      ((S.p_ptr & 15) == 0) && ((pr.offset & 3) == 0) && (jcol + 3 < L.b);
     const int nrow = min(TC_T, L.a - i0);
-    for (int rr = tid >> 5; rr < nrow; rr += 8) {
+    for (int rr = tid >> 5; rr < nrow; rr += SCAO_APPLY_NT / 32) {
         const int i = i0 + rr;
         const int64_t o = (int64_t)(L.row0 + i) * L.ld + L.col0 + jcol;
         const float4 cr = *(const float4*)&Cs[rr * CLD + cg];
@@ -1184,7 +1194,7 @@ extern "C" int scao_plan_step(const ScaoPlanDev* P, void* stream) {
         SCAO_CHECK_LAUNCH();
     }
     if (P->n_chunks > 0) {
-        { ProfScope _ps(SLOT_DIAG_PRE, st); diag_pre_kernel<<<P->n_chunks, NT, 0, st>>>(*P); }
+        if (P->n_diag > 0) { ProfScope _ps(SLOT_DIAG_PRE, st); diag_pre_kernel<<<P->n_diag, NT, 0, st>>>(*P); }
         SCAO_CHECK_LAUNCH();
     }
     if (P->n_leaves > 0) {
@@ -1205,11 +1215,11 @@ extern "C" int scao_plan_step(const ScaoPlanDev* P, void* stream) {
     SCAO_CHECK_LAUNCH();
     if (P->n_tiles > 0) {
         { ProfScope _ps(SLOT_APPLY_KRON, st);
-          apply_kron_tc_kernel<<<P->n_tiles, 256, apply_tc_smem(P->kpad_max), st>>>(*P, P->err); }
+          apply_kron_tc_kernel<<<P->n_tiles, SCAO_APPLY_NT, apply_tc_smem(P->kpad_max), st>>>(*P, P->err); }
         SCAO_CHECK_LAUNCH();
     }
     if (P->n_chunks > 0) {
-        { ProfScope _ps(SLOT_APPLY_FLAT, st); apply_flat_kernel<<<P->n_chunks, NT, 0, st>>>(*P); }
+        if (P->n_flat > 0) { ProfScope _ps(SLOT_APPLY_FLAT, st); apply_flat_kernel<<<P->n_flat, NT, 0, st>>>(*P); }
         SCAO_CHECK_LAUNCH();
     }
     { ProfScope _ps(SLOT_PARAM_POST, st); param_post_kernel<<<P->n_params, NT, 0, st>>>(*P); }
@@ -1217,7 +1227,7 @@ extern "C" int scao_plan_step(const ScaoPlanDev* P, void* stream) {
     { ProfScope _ps(SLOT_GLOBAL_NORM, st); global_norm_kernel<<<1, 512, 0, st>>>(*P); }
     SCAO_CHECK_LAUNCH();
     if (P->n_chunks > 0) {
-        { ProfScope _ps(SLOT_APPLY_P, st); apply_p_kernel<<<P->n_chunks, NT, 0, st>>>(*P); }
+        if (P->n_p > 0) { ProfScope _ps(SLOT_APPLY_P, st); apply_p_kernel<<<P->n_p, NT, 0, st>>>(*P); }
         SCAO_CHECK_LAUNCH();
     }
     return SCAO_OK;

@@ -285,6 +285,7 @@ class SCAO(Optimizer):
                                          sp), "scao_plan_eigen")
             self._last_eig_status = status
             keep.append(ids)
+        plan.set_phases(np.array(tab["phase"], dtype=np.int32))
         _lib.check(L.scao_plan_step(pd, sp), "scao_plan_step")
         self._noise_std *= self._noise_anneal
         if self._lookahead_k > 0 and self._global_step % self._lookahead_k == 0:

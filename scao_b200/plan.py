@@ -233,6 +233,17 @@ class Plan:
         self.global_norm_ema = torch.ones(1, dtype=torch.float64, device=dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
         self.counters = z(16, torch.int32)
+        nc = max(len(self.ctab), 1)
+        self.t_diag_list = z(nc, torch.int32)
+        self.t_flat_list = z(nc, torch.int32)
+        self.t_p_list = z(nc, torch.int32)
+        self._chunk_param = self.ctab["param"].astype(np.int64) if len(self.ctab) else np.zeros(0, np.int64)
+        diag = np.nonzero(self.ptab["mode"][self._chunk_param] == 0)[0].astype(np.int32) \
+            if len(self.ctab) else np.zeros(0, np.int32)
+        if len(diag):
+            self.t_diag_list[:len(diag)].copy_(torch.from_numpy(diag))
+        self.n_diag = len(diag)
+        self._phase_key = None
         self.ua = z(self._tile_bytes[0], torch.uint8)
         self.ut = z(self._tile_bytes[1], torch.uint8)
         self.wa = z(self._tile_bytes[2], torch.uint8)
@@ -281,6 +292,27 @@ class Plan:
         self.ev.copy_(ev)
         self.absmax.fill_(float(eye_val))
         self.k.copy_(torch.from_numpy(L["kmin"].astype(np.int32)))
+
+    def set_phases(self, phases):
+        """Chunk lists for the flat passes of this step (re-uploaded only when
+        the per-parameter phase vector changes)."""
+        key = phases.tobytes()
+        if key == self._phase_key:
+            return
+        self._phase_key = key
+        if len(self.ctab):
+            ph = phases[self._chunk_param]
+            mode = self.ptab["mode"][self._chunk_param]
+            flat = np.nonzero((ph == 1) | ((ph == 2) & (mode == 0)))[0].astype(np.int32)
+            pl = np.nonzero(ph == 2)[0].astype(np.int32)
+        else:
+            flat = pl = np.zeros(0, np.int32)
+        if len(flat):
+            self.t_flat_list[:len(flat)].copy_(torch.from_numpy(flat))
+        if len(pl):
+            self.t_p_list[:len(pl)].copy_(torch.from_numpy(pl))
+        self.dev.n_flat = len(flat)
+        self.dev.n_p = len(pl)
 
     def check_error(self):
         """Raise if a kernel recorded a timed-out wait (synchronises)."""
@@ -334,4 +366,6 @@ def PlanDev_from(plan):
     d.err = ptr(plan.err)
     d.ua, d.ut, d.wa = ptr(plan.ua), ptr(plan.ut), ptr(plan.wa)
     d.counters = ptr(plan.counters)
+    d.diag_list, d.flat_list, d.p_list = ptr(plan.t_diag_list), ptr(plan.t_flat_list), ptr(plan.t_p_list)
+    d.n_diag = plan.n_diag
     return d
