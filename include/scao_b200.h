@@ -78,7 +78,7 @@ typedef struct {
     float tau;
     float lars;
     float diag_bias;       /* float(max(1 - rho**precond_step, 1e-8))       */
-    int32_t pad0;
+    float rbc1, rbc2, rbc3;/* reciprocals of bc1..bc3 (division by constant) */
 } ScaoParamStep;
 
 /* One per Kronecker leaf block (static).  Each leaf owns two symmetric
@@ -292,6 +292,12 @@ SCAO_API int scao_prof_slots(void);
  * mn_major=1 stages both operands in the MN-major shared-memory layout.   */
 SCAO_API int scao_tc_selftest(const uint16_t* A, const uint16_t* B, float* C, int N, int K,
                               int* err, int mn_major, void* stream);
+
+/* Check of the division-by-constant rewrite used by the Adan update: counts
+ * x[i] / c[i % 1024] where reciprocal-plus-FMA-correction differs from the
+ * IEEE quotient (adds into *mismatches).                                   */
+SCAO_API int scao_divc_check(const float* x, const float* c, int n, int* mismatches,
+                             void* stream);
 
 /* Library identification. */
 SCAO_API const char* scao_version(void);

@@ -29,7 +29,8 @@ STEP_DT = np.dtype([
     ("beta3", "<f4"), ("c1", "<f4"), ("c2", "<f4"), ("c3", "<f4"),
     ("bc1", "<f4"), ("bc2", "<f4"), ("bc3", "<f4"), ("sqrt_bc2", "<f4"),
     ("eps", "<f4"), ("blend", "<f4"), ("one_minus_blend", "<f4"), ("tau", "<f4"),
-    ("lars", "<f4"), ("diag_bias", "<f4"), ("pad0", "<i4")], align=True)
+    ("lars", "<f4"), ("diag_bias", "<f4"), ("rbc1", "<f4"), ("rbc2", "<f4"),
+    ("rbc3", "<f4")], align=True)
 
 LEAF_DT = np.dtype([
     ("param", "<i4"), ("row0", "<i4"), ("col0", "<i4"), ("a", "<i4"), ("b", "<i4"),
@@ -70,7 +71,7 @@ class PlanDev(C.Structure):
 
 def check_layout():
     assert PARAM_DT.itemsize == 56, PARAM_DT.itemsize
-    assert STEP_DT.itemsize == 120, STEP_DT.itemsize
+    assert STEP_DT.itemsize == 128, STEP_DT.itemsize
     assert LEAF_DT.itemsize == 160, LEAF_DT.itemsize
     assert CHUNK_DT.itemsize == 24, CHUNK_DT.itemsize
 
@@ -104,6 +105,7 @@ SIGNATURES = {
     "scao_plan_prep_factors": (C.c_int, [C.POINTER(PlanDev), _P, C.c_int, _P]),
     "scao_plan_lookahead": (C.c_int, [C.POINTER(PlanDev), C.c_float, C.c_int, _P]),
     "scao_version": (C.c_char_p, []),
+    "scao_divc_check": (C.c_int, [_P, _P, C.c_int, _P, _P]),
     "scao_tc_selftest": (C.c_int, [_P, _P, _P, C.c_int, C.c_int, _P, C.c_int, _P]),
     "scao_launch_count": (C.c_int64, []),
     "scao_prof_enable": (None, [C.c_int]),

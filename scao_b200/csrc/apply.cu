@@ -261,6 +261,15 @@ param_pre_kernel(ScaoPlanDev P) {
 
 // Adan moments + update for one element (optimizer.py:608-633).
 struct AdanOut { float u; };
+// x / c for a per-parameter constant c with r ~= 1/c: quotient from the
+// reciprocal, then one fused residual correction (Markstein); matches the
+// IEEE quotient of __fdiv_rn for normal operands.
+__device__ __forceinline__ float div_c(float x, float c, float r) {
+    const float q = x * r;
+    const float e = fmaf(-q, c, x);
+    return fmaf(e, r, q);
+}
+
 __device__ __forceinline__ float adan_elem(const ScaoParamStep& S, int dt, float g, float gp,
                                            float& m, float& v, float& d, float& prev,
                                            bool clip, float clipmul) {
@@ -272,8 +281,8 @@ __device__ __forceinline__ float adan_elem(const ScaoParamStep& S, int dt, float
     d = fmaf(delta, S.c3, fmul(d, S.beta3));
     const float gad = fadd(geff, fmul(S.c3, delta));
     v = fmaf(fmul(S.c2, gad), gad, fmul(v, S.beta2));
-    const float num = fadd(fdiv(m, S.bc1), fmul(S.c3, fdiv(d, S.bc3)));
-    const float den = fadd(sqrtf(fdiv(v, S.bc2)), S.eps);
+    const float num = fadd(div_c(m, S.bc1, S.rbc1), fmul(S.c3, div_c(d, S.bc3, S.rbc3)));
+    const float den = fadd(sqrtf(div_c(v, S.bc2, S.rbc2)), S.eps);
     return fdiv(num, den);
 }
 
@@ -803,7 +812,12 @@ apply_kron_tc_kernel(ScaoPlanDev P, int* err) {
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
                 const float gp = round_dt(fadd(gv[c], crv[c]), dt);
+#ifdef SCAO_EXP_LIGHT
+                mv[c] += gp; vv[c] += gp * gp; dv[c] -= gp; qv[c] = gv[c];
+                const float u = mv[c];
+#else
                 const float u = adan_elem(S, dt, gv[c], gp, mv[c], vv[c], dv[c], qv[c], clip, clipmul);
+#endif
                 usq = fmaf(u, u, usq);
                 gsq = fmaf(gv[c], gv[c], gsq);
                 const float pd = round_dt(fmul(pv[c], wdm), dt);

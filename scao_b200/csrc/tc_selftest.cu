@@ -79,3 +79,27 @@ extern "C" int scao_tc_selftest(const uint16_t* A, const uint16_t* B, float* C, 
     SCAO_CHECK_LAUNCH();
     return SCAO_OK;
 }
+
+// Check of the division-by-constant rewrite used in the Adan update:
+// counts elements where x*r + one FMA correction differs from IEEE x / c.
+namespace {
+__global__ void divc_check_kernel(const float* x, const float* c, int n, int* mism) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const float cc = c[i & 1023];
+        const float r = 1.0f / cc;
+        const float q = x[i] * r;
+        const float e = fmaf(-q, cc, x[i]);
+        const float a = fmaf(e, r, q);
+        if (__float_as_int(a) != __float_as_int(__fdiv_rn(x[i], cc))) atomicAdd(mism, 1);
+    }
+}
+}  // namespace
+
+extern "C" int scao_divc_check(const float* x, const float* c, int n, int* mismatches,
+                               void* stream) {
+    if (!x || !c || !mismatches || n <= 0) return SCAO_ERR_ARG;
+    cudaStream_t st = (cudaStream_t)stream;
+    { ProfScope _ps(SLOT_SEAM, st); divc_check_kernel<<<256, 256, 0, st>>>(x, c, n, mismatches); }
+    SCAO_CHECK_LAUNCH();
+    return SCAO_OK;
+}

@@ -247,6 +247,9 @@ class SCAO(Optimizer):
             row["blend"] = blend
             row["one_minus_blend"] = 1.0 - blend
             row["bc1"], row["bc2"], row["bc3"] = bc1, bc2, 1.0 - b3 ** step
+            # reciprocals of the float32 constants (x / c = x * r + one FMA correction)
+            for k in ("bc1", "bc2", "bc3"):
+                row["r" + k] = 1.0 / float(row[k])
             tau = g["tau"]
             row["clip"] = 0 if tau is None else 1
             row["tau"] = 0.0 if tau is None else tau

@@ -23,3 +23,20 @@ def test_tc_selftest(N, K, mn):
     torch.cuda.synchronize()
     assert err.item() == 0
     assert (C.double().cpu() - ref).abs().max().item() < 1e-3 * max(1.0, ref.abs().max().item())
+
+
+def test_division_by_constant_is_ieee():
+    """x / c in the Adan update runs as x*r plus one FMA correction; it must
+    give the IEEE quotient for the value ranges the moments take."""
+    L = _lib.lib()
+    g = torch.Generator().manual_seed(7)
+    n = 1 << 22
+    x = (torch.randn(n, generator=g) * torch.exp(torch.randn(n, generator=g) * 8)).cuda()
+    # bias corrections 1 - beta**t for beta in (0.9, 0.999, 0.99), t in 1..1024
+    t = torch.arange(1, 1025, dtype=torch.float64)
+    c = torch.cat([1 - 0.9 ** t[:342], 1 - 0.999 ** t[:341], 1 - 0.99 ** t[:341]]).float().cuda()
+    m = torch.zeros(1, dtype=torch.int32, device="cuda")
+    _lib.check(L.scao_divc_check(x.data_ptr(), c.data_ptr(), n, m.data_ptr(),
+                                 torch.cuda.current_stream().cuda_stream), "divc")
+    torch.cuda.synchronize()
+    assert m.item() == 0
