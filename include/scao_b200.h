@@ -125,7 +125,7 @@ typedef struct {
     int32_t kpad_max;      /* largest leaf kpad (<= 128)                    */
     int32_t p_stride;      /* floats per projection partial: kpad_max^2 + 4 */
     int32_t kron_dtypes;   /* bit mask (1 << dtype) over Kronecker params   */
-    int32_t pad_;
+    int32_t max_leaf_rows_tiles; /* max over leaves of ceil(a / 128)        */
     const ScaoParam* params;
     const ScaoLeaf* leaves;
     const ScaoTile* tiles;

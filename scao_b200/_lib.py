@@ -54,7 +54,7 @@ class PlanDev(C.Structure):
         ("n_params", C.c_int32), ("n_leaves", C.c_int32), ("n_tiles", C.c_int32),
         ("n_panels", C.c_int32), ("n_chunks", C.c_int32), ("int8_ema", C.c_int32),
         ("kpad_max", C.c_int32), ("p_stride", C.c_int32),
-        ("kron_dtypes", C.c_int32), ("pad_", C.c_int32),
+        ("kron_dtypes", C.c_int32), ("max_leaf_rows_tiles", C.c_int32),
         ("params", _P), ("leaves", _P), ("tiles", _P), ("panels", _P), ("chunks", _P),
         ("step", _P),
         ("exp_avg", _P), ("exp_avg_sq", _P), ("exp_avg_diff", _P), ("prev_grad", _P),

@@ -200,26 +200,70 @@ leaf_coef_kernel(ScaoPlanDev P) {
     }
     nat = block_sum(nat, red);
     if (threadIdx.x == 0) P.leaf_nat2[blockIdx.x] = nat;
-    // W = U_l * Delta (a x kp; only the first k columns of U_l contribute),
-    // written as bf16 hi/lo canonical tiles for the tensor-core apply
-    const float* Ul = P.u + L.ul_off;
-    const int Kp = (kp + 15) & ~15;
+    // Delta overwrites the first panel's partial slot (read above by this
+    // same thread for the same element, so no other reader remains)
+    float* Dg = P.p_part + (int64_t)L.panel_begin * P.p_stride;
+    for (int e = threadIdx.x; e < kp * kp; e += NT) Dg[e] = D[e];
+}
+
+__device__ __forceinline__ void stage_ls(float* Ls, const float* Ul, int row0, int nrows, int sl,
+                                         int kpad, int Kp);
+
+// W = U_l Delta (rows [128 t, 128 t + 128) of the leaf; only the first k
+// columns of U_l contribute), written as bf16 hi/lo canonical tiles for the
+// tensor-core apply.  4 x 8 register blocks, 16-byte tile stores.
+__global__ void __launch_bounds__(256)
+leaf_w_kernel(ScaoPlanDev P) {
+    const int leaf = blockIdx.y;
+    const ScaoLeaf& L = P.leaves[leaf];
+    const ScaoParamStep& S = P.step[L.param];
+    if (S.phase != 2) return;
+    const int r0 = blockIdx.x * TC_T;
+    if (r0 >= L.a) return;
+    const int kp = L.kpad, Kp = (kp + 15) & ~15;
+    const int k = P.k[leaf];
+    extern __shared__ float sm[];
+    float* Ds = sm;                       // kp x Kp (zero beyond kp)
+    float* Ls = Ds + kp * Kp;             // 128 x (Kp+4)
+    const float* Dg = P.p_part + (int64_t)L.panel_begin * P.p_stride;
+    for (int e = threadIdx.x; e < kp * Kp; e += blockDim.x) {
+        const int a = e / Kp, bb = e - a * Kp;
+        Ds[e] = bb < kp ? Dg[a * kp + bb] : 0.f;
+    }
+    stage_ls(Ls, P.u + L.ul_off, r0, min(TC_T, L.a - r0), L.sl, kp, Kp);
+    __syncthreads();
     const int64_t tbytes = (int64_t)TC_T * Kp * 2;
-    uint8_t* wa = P.wa + L.wa_off;
-    const int arows = (L.a + TC_T - 1) / TC_T * TC_T;
-    for (int64_t e = threadIdx.x; e < (int64_t)arows * Kp; e += NT) {
-        const int i = (int)(e / Kp), b = (int)(e % Kp);
-        float s = 0.f;
-        if (i < L.a && b < kp) {
-            const float* urow = Ul + (int64_t)i * L.sl;
-            for (int a = 0; a < k; ++a) s = fmaf(urow[a], D[a * kp + b], s);
+    uint8_t* t = P.wa + L.wa_off + (int64_t)blockIdx.x * 2 * tbytes;
+    const int nb = Kp / 8;
+    for (int blk = threadIdx.x; blk < 32 * nb; blk += blockDim.x) {
+        const int rr = (blk / nb) * 4, b0 = (blk % nb) * 8;
+        float acc[4][8] = {};
+        for (int a = 0; a < k; ++a) {
+            const float4 d0 = *(const float4*)&Ds[a * Kp + b0];
+            const float4 d1 = *(const float4*)&Ds[a * Kp + b0 + 4];
+            const float dv[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float u = Ls[(rr + i) * (Kp + 4) + a];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(u, dv[j], acc[i][j]);
+            }
         }
-        uint16_t h, l;
-        split_bf16(s, h, l);
-        uint8_t* t = wa + (int64_t)(i / TC_T) * 2 * tbytes;
-        const uint32_t o = canon_off(i % TC_T, b, Kp);
-        *(uint16_t*)(t + o) = h;
-        *(uint16_t*)(t + tbytes + o) = l;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            uint32_t hw[4], lw[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                uint16_t h0, l0, h1, l1;
+                split_bf16(acc[i][2 * j], h0, l0);
+                split_bf16(acc[i][2 * j + 1], h1, l1);
+                hw[j] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+                lw[j] = (uint32_t)l0 | ((uint32_t)l1 << 16);
+            }
+            const uint32_t o = canon_off(rr + i, b0, Kp);
+            *(uint4*)(t + o) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            *(uint4*)(t + tbytes + o) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        }
     }
 }
 
@@ -640,6 +684,29 @@ __device__ __forceinline__ bool proj_fast(const ScaoLeaf& L, const ScaoParamStep
            ((L.b & 7) == 0) && ((S.g_ptr & 15) == 0);
 }
 
+// U_l rows [row0, row0+128) x [0, Kp) -> shared (row stride Kp+4), zero
+// padded; 16-byte cp.async chunks when the rows are 16-byte aligned.
+__device__ __forceinline__ void stage_ls(float* Ls, const float* Ul, int row0, int nrows, int sl,
+                                         int kpad, int Kp) {
+    const int q4 = Kp >> 2;
+    if ((sl & 3) == 0 && (reinterpret_cast<uintptr_t>(Ul) & 15) == 0) {
+        for (int c = threadIdx.x; c < TC_T * q4; c += blockDim.x) {
+            const int r = c / q4, a = (c - r * q4) * 4;
+            const bool in = r < nrows && a < kpad;
+            const float* src = in ? Ul + (int64_t)(row0 + r) * sl + a : Ul;
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 16, %2;"
+                         :: "r"(smem_u32(Ls + r * (Kp + 4) + a)), "l"(src), "r"(in ? 16 : 0)
+                         : "memory");
+        }
+        asm volatile("cp.async.commit_group;\n\tcp.async.wait_all;" ::: "memory");
+    } else {
+        for (int e = threadIdx.x; e < TC_T * Kp; e += blockDim.x) {
+            const int r = e / Kp, a = e - (e / Kp) * Kp;
+            Ls[r * (Kp + 4) + a] = (r < nrows && a < kpad) ? Ul[(int64_t)(row0 + r) * sl + a] : 0.f;
+        }
+    }
+}
+
 // P_part = Ls^T Ts (kp x kp) from two row-major [rows][ld] fp32 tiles in
 // shared memory; each thread accumulates 4 x 4 blocks (16 FMA per two
 // 128-bit shared loads).
@@ -964,10 +1031,7 @@ proj_bf16_kernel(ScaoPlanDev P, int* err) {
             for (int c = 0; c < 16; ++c) Ts[r * (Kp + 4) + c0 + c] = ok ? v[c] : 0.f;
         }
     }
-    for (int e = tid; e < TC_T * Kp; e += 128) {
-        const int r = e / Kp, a = e - (e / Kp) * Kp;
-        Ls[r * (Kp + 4) + a] = (r < pn.nrows && a < L.kpad) ? Ul[(int64_t)(pn.row0 + r) * L.sl + a] : 0.f;
-    }
+    stage_ls(Ls, Ul, pn.row0, pn.nrows, L.sl, L.kpad, Kp);
     tc_fence_before();
     __syncthreads();
     if (warp == 0) tc_dealloc(tmem, ncols);
@@ -1152,10 +1216,7 @@ proj_tc_kernel(ScaoPlanDev P, int* err) {
             for (int c = 0; c < 16; ++c) Ts[r * (Kp + 4) + c0 + c] = v[c];
         }
     }
-    for (int e = tid; e < TC_T * Kp; e += 128) {
-        const int r = e / Kp, a = e - (e / Kp) * Kp;
-        Ls[r * (Kp + 4) + a] = (r < pn.nrows && a < L.kpad) ? Ul[(int64_t)(pn.row0 + r) * L.sl + a] : 0.f;
-    }
+    stage_ls(Ls, Ul, pn.row0, pn.nrows, L.sl, L.kpad, Kp);
     tc_fence_before();
     __syncthreads();
     if (warp == 0) tc_dealloc(tmem, ncols);
@@ -1223,6 +1284,18 @@ extern "C" int scao_plan_step(const ScaoPlanDev* P, void* stream) {
             attr = true;
         }
         { ProfScope _ps(SLOT_LEAF_COEF, st); leaf_coef_kernel<<<P->n_leaves, NT, sm, st>>>(*P); }
+        SCAO_CHECK_LAUNCH();
+        {
+            const size_t smw = (size_t)(kp * ((kp + 15) & ~15) + TC_T * (((kp + 15) & ~15) + 4)) * 4;
+            static bool wattr = false;
+            if (!wattr) {
+                cudaFuncSetAttribute(leaf_w_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)((128 * 128 + 128 * 132) * 4));
+                wattr = true;
+            }
+            ProfScope _ps(SLOT_LEAF_COEF, st);
+            leaf_w_kernel<<<dim3(P->max_leaf_rows_tiles, P->n_leaves), 256, smw, st>>>(*P);
+        }
         SCAO_CHECK_LAUNCH();
     }
     { ProfScope _ps(SLOT_PARAM_PRE, st); param_pre_kernel<<<P->n_params, NT, 0, st>>>(*P); }

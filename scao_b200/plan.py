@@ -348,6 +348,7 @@ def PlanDev_from(plan):
     d.int8_ema = int(plan.int8_ema)
     d.kpad_max = plan.kpad_max
     d.p_stride = plan.p_stride
+    d.max_leaf_rows_tiles = int((-(-plan.ltab["a"] // 128)).max()) if plan.n_leaves else 0
     d.kron_dtypes = int(np.bitwise_or.reduce(
         [1 << int(r["dtype"]) for r in plan.ptab if int(r["mode"]) == 1] or [0]))
     ptr = lambda t: t.data_ptr() if t is not None else None
