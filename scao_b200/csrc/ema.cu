@@ -194,17 +194,26 @@ gram_ema_tc_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, float* xbuf, 
     if (P.int8_ema) {
         const int8_t* q = (const int8_t*)P.fac + p.fac_off;
         const float s_old = quant_scale_f(P.absmax[p.pid]);
-        for (int ii = 0; ii < GT; ++ii) {
-            const int i = i0 + ii;
-            if (i >= n || j >= n) continue;
-            float x = 0.f;
-            if (!diag || ii >= jj) {
-                const float deq = __fmul_rn((float)q[(int64_t)i * n + j], s_old);
-                x = __fadd_rn(__fmul_rn(deq, rho_f), __fmul_rn(alpha_f, Cs[ii * CLD + jj]));
-                p.x[(int64_t)i * n + j] = x;
-                mx = fmaxf(mx, fabsf(x));
+        for (int ib = 0; ib < GT; ib += 16) {
+            // 16 independent old-code loads in flight, then the arithmetic
+            int8_t qv[16];
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+                const int i = i0 + ib + c;
+                qv[c] = (i < n && j < n) ? q[(int64_t)i * n + j] : (int8_t)0;
             }
-            Cs[ii * CLD + jj] = x;
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+                const int ii = ib + c, i = i0 + ii;
+                float x = 0.f;
+                if (i < n && j < n && (!diag || ii >= jj)) {
+                    const float deq = __fmul_rn((float)qv[c], s_old);
+                    x = __fadd_rn(__fmul_rn(deq, rho_f), __fmul_rn(alpha_f, Cs[ii * CLD + jj]));
+                    p.x[(int64_t)i * n + j] = x;
+                    mx = fmaxf(mx, fabsf(x));
+                }
+                Cs[ii * CLD + jj] = x;
+            }
         }
     } else {
         float* Lm = (float*)P.fac + p.fac_off;
@@ -362,7 +371,16 @@ __global__ void requant_batch_kernel(ScaoPlanDev P, const int32_t* __restrict__ 
     const float s = quant_scale_f(am);
     int8_t* q = (int8_t*)P.fac + (side ? L.rq_off : L.lq_off);
     const float* x = xbuf + (int64_t)j * xstride;
-    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < nn;
+    const int64_t n4 = nn >> 2;
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n4;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        const float4 v = __ldcs((const float4*)x + e);
+        char4 o;
+        o.x = quant_one(v.x, s, zero); o.y = quant_one(v.y, s, zero);
+        o.z = quant_one(v.z, s, zero); o.w = quant_one(v.w, s, zero);
+        ((char4*)q)[e] = o;
+    }
+    for (int64_t e = n4 * 4 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < nn;
          e += (int64_t)gridDim.x * blockDim.x)
         q[e] = quant_one(x[e], s, zero);
     if (blockIdx.x == 0 && threadIdx.x == 0) P.absmax[2 * leaf + side] = am;
