@@ -773,6 +773,29 @@ prep_factors_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids) {
 // TMEM -> shared (corr[i][j]) -> every thread handles 4 consecutive columns
 // of a row (128-bit state accesses, 512 contiguous bytes per warp).  Also
 // accumulates ||round(p*(1-lr wd))||^2 for the LARS ratio.
+#ifndef SCAO_APPLY_PD
+#define SCAO_APPLY_PD 4
+#endif
+// L2 prefetch of one row segment (128 columns) of every array the apply
+// epilogue touches; one request per 128-byte line.
+__device__ __forceinline__ void apply_prefetch_row(const ScaoPlanDev& P, const ScaoLeaf& L,
+                                                   const ScaoParamStep& S, const ScaoParam& pr,
+                                                   int i0, int rr, int nrow, int jcol, int lane) {
+    if (rr >= nrow || jcol >= L.b) return;
+    const int64_t o = (int64_t)(L.row0 + i0 + rr) * L.ld + L.col0 + jcol;
+    if ((lane & 7) == 0) {
+        asm volatile("prefetch.global.L2 [%0];" :: "l"(P.exp_avg + pr.offset + o));
+        asm volatile("prefetch.global.L2 [%0];" :: "l"(P.exp_avg_sq + pr.offset + o));
+        asm volatile("prefetch.global.L2 [%0];" :: "l"(P.exp_avg_diff + pr.offset + o));
+        asm volatile("prefetch.global.L2 [%0];" :: "l"(P.prev_grad + pr.offset + o));
+    }
+    const int es = pr.dtype == SCAO_F32 ? 4 : 2;
+    if ((lane & (es == 4 ? 7 : 15)) == 0) {
+        asm volatile("prefetch.global.L2 [%0];" :: "l"((const char*)S.g_ptr + o * es));
+        asm volatile("prefetch.global.L2 [%0];" :: "l"((const char*)S.p_ptr + o * es));
+    }
+}
+
 #ifndef SCAO_APPLY_NT
 #define SCAO_APPLY_NT 256
 #endif
@@ -807,6 +830,11 @@ apply_kron_tc_kernel(ScaoPlanDev P, int* err) {
         bulk_g2s(A, P.ua + L.ua_off + (int64_t)(j0 / TC_T) * 2 * tb, 2 * tb, &mbar_ld);
         bulk_g2s(B, P.wa + L.wa_off + (int64_t)(i0 / TC_T) * 2 * tb, 2 * tb, &mbar_ld);
     }
+    // start pulling this thread's first state rows into L2 while the
+    // correction is built on the tensor core
+    for (int d = 0; d < SCAO_APPLY_PD; ++d)
+        apply_prefetch_row(P, L, S, pr, i0, (tid >> 5) + d * (SCAO_APPLY_NT / 32),
+                           min(TC_T, L.a - i0), j0 + (tid & 31) * 4, lane);
     if (warp == 0) tc_alloc(&tslot, TC_T);
     tc_fence_before();
     __syncthreads();
@@ -863,6 +891,7 @@ apply_kron_tc_kernel(ScaoPlanDev P, int* err) {
                      ((S.p_ptr & 15) == 0) && ((pr.offset & 3) == 0) && (jcol + 3 < L.b);
     const int nrow = min(TC_T, L.a - i0);
     for (int rr = tid >> 5; rr < nrow; rr += SCAO_APPLY_NT / 32) {
+        apply_prefetch_row(P, L, S, pr, i0, rr + SCAO_APPLY_PD * (SCAO_APPLY_NT / 32), nrow, jcol, lane);
         const int i = i0 + rr;
         const int64_t o = (int64_t)(L.row0 + i) * L.ld + L.col0 + jcol;
         const float4 cr = *(const float4*)&Cs[rr * CLD + cg];
