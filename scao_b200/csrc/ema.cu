@@ -77,7 +77,7 @@ __device__ __forceinline__ bool gram_tc_ok(const Prob& p, const ScaoLeaf& L) {
            (L.b % 8) == 0 && ((reinterpret_cast<uintptr_t>(p.g) & 15) == 0);
 }
 
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(256, 2)
 gram_ema_tc_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, float* xbuf, int64_t xstride,
                    float* amnew, float rho_f, float alpha_f, int* err) {
     const Prob p = get_prob(P, ids, blockIdx.y, xbuf, xstride, amnew);
@@ -115,9 +115,10 @@ gram_ema_tc_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, float* xbuf, 
         unsigned char* st = smx + (kb % GSTAGES) * SB;
         const int k0 = kb * GKB;
 #pragma unroll
-        for (int q = 0; q < 16; ++q) {          // 2 operands x 1024 chunks / 128 threads
-            const int ch = tid + (q & 7) * 128;
-            const int opnd = q >> 3;
+        for (int q = 0; q < 8; ++q) {           // 2 operands x 1024 chunks / 256 threads
+            const int cq = tid + q * 256;
+            const int ch = cq & 1023;
+            const int opnd = cq >> 10;
             const int base = opnd ? j0 : i0;
             int r, k;                           // output index r (< 128), depth k (< 64)
             if (!mn) { r = ch >> 3; k = (ch & 7) * 8; } else { k = ch >> 4; r = (ch & 15) * 8; }
@@ -175,10 +176,11 @@ gram_ema_tc_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, float* xbuf, 
     constexpr int CLD = GT + 1;
     float* Cs = (float*)smx;
     {
-        const int r = warp * 32 + lane;
-        for (int c0 = 0; c0 < GT; c0 += 16) {
+        const int qd = warp & 3, hf = warp >> 2;
+        const int r = qd * 32 + lane;
+        for (int c0 = hf * 64; c0 < hf * 64 + 64; c0 += 16) {
             float v[16];
-            tc_ld16(tmem + ((uint32_t)(warp * 32) << 16) + c0, v);
+            tc_ld16(tmem + ((uint32_t)(qd * 32) << 16) + c0, v);
 #pragma unroll
             for (int c = 0; c < 16; ++c) Cs[r * CLD + c0 + c] = ok ? v[c] : 0.f;
         }
@@ -189,12 +191,13 @@ gram_ema_tc_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, float* xbuf, 
     // EMA epilogue with the reference's separate roundings; rows i, lanes j
     const int n = p.n;
     float mx = 0.f;
-    const int jj = tid;
+    const int jj = tid & 127;
     const int j = j0 + jj;
+    const int rlo = (tid >> 7) * 64, rhi = rlo + 64;   // this thread's row half
     if (P.int8_ema) {
         const int8_t* q = (const int8_t*)P.fac + p.fac_off;
         const float s_old = quant_scale_f(P.absmax[p.pid]);
-        for (int ib = 0; ib < GT; ib += 16) {
+        for (int ib = rlo; ib < rhi; ib += 16) {
             // 16 independent old-code loads in flight, then the arithmetic
             int8_t qv[16];
 #pragma unroll
@@ -217,7 +220,7 @@ gram_ema_tc_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, float* xbuf, 
         }
     } else {
         float* Lm = (float*)P.fac + p.fac_off;
-        for (int ii = 0; ii < GT; ++ii) {
+        for (int ii = rlo; ii < rhi; ++ii) {
             const int i = i0 + ii;
             if (i >= n || j >= n) continue;
             float x = 0.f;
@@ -227,7 +230,7 @@ gram_ema_tc_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, float* xbuf, 
             Cs[ii * CLD + jj] = x;
         }
         __syncthreads();    // every old value read before any write
-        for (int ii = 0; ii < GT; ++ii) {
+        for (int ii = rlo; ii < rhi; ++ii) {
             const int i = i0 + ii;
             if (i < n && j < n && (!diag || ii >= jj)) Lm[(int64_t)i * n + j] = Cs[ii * CLD + jj];
         }
@@ -236,9 +239,9 @@ gram_ema_tc_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, float* xbuf, 
     // mirror: element (j, i) = x(i, j) for the strict lower part
     {
         float* dst = P.int8_ema ? p.x : (float*)P.fac + p.fac_off;
-        const int ii = tid;
+        const int ii = tid & 127;
         const int i = i0 + ii;
-        for (int jr = 0; jr < GT; ++jr) {
+        for (int jr = rlo; jr < rhi; ++jr) {
             const int jm = j0 + jr;
             if (i >= n || jm >= n) continue;
             if (diag && ii <= jr) continue;
@@ -445,7 +448,7 @@ extern "C" int scao_plan_curvature(const ScaoPlanDev* P, const int32_t* leaf_ids
             }
             const int nt2 = (int)((mx + GT - 1) / GT);
             ProfScope _ps2(SLOT_GRAM_TC, st);
-            gram_ema_tc_kernel<<<dim3(nt2 * (nt2 + 1) / 2, np), 128, gram_tc_smem(), st>>>(
+            gram_ema_tc_kernel<<<dim3(nt2 * (nt2 + 1) / 2, np), 256, gram_tc_smem(), st>>>(
                 *P, ids, xbuf, xstride, amnew, rho_f, alpha_f, P->err);
         }
         SCAO_CHECK_LAUNCH();
