@@ -130,9 +130,26 @@ __global__ void eig_prep_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids,
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
     if (P.int8_ema) {
         const int8_t* q = (const int8_t*)P.fac + p.facoff;
-        for (int i = wid; i < p.n; i += nw)
-            for (int k = lane; k < p.n; k += 32)
-                if (i != k && q[(int64_t)i * p.n + k] != 0) nz = 1;
+        if ((p.n & 15) == 0) {
+            // 16 codes per load; the diagonal byte is masked out
+            const int nc = p.n >> 4;
+            for (int i = wid; i < p.n; i += nw) {
+                const uint4* row = (const uint4*)(q + (int64_t)i * p.n);
+                for (int c = lane; c < nc; c += 32) {
+                    uint4 v = row[c];
+                    if (c == (i >> 4)) {
+                        const int b = i & 15;
+                        uint32_t* w = (uint32_t*)&v;
+                        w[b >> 2] &= ~(0xFFu << ((b & 3) * 8));
+                    }
+                    if (v.x | v.y | v.z | v.w) nz = 1;
+                }
+            }
+        } else {
+            for (int i = wid; i < p.n; i += nw)
+                for (int k = lane; k < p.n; k += 32)
+                    if (i != k && q[(int64_t)i * p.n + k] != 0) nz = 1;
+        }
     } else {
         const float* q = (const float*)P.fac + p.facoff;
         for (int i = wid; i < p.n; i += nw)

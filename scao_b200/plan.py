@@ -58,6 +58,17 @@ def split_blocks(m, n, mpd):
     return out
 
 
+def split_tree(m, n, mpd):
+    """Nesting of the block split: an int count of leaves for a Kronecker
+    block, or a list of sub-trees for a block-diagonal one (the reference's
+    ``_blocks`` hierarchy, preconditioner.py:163-194)."""
+    if max(m, n) <= mpd:
+        return 1
+    large, small = (m, n) if m >= n else (n, m)
+    sizes = [mpd] * (large // mpd) + ([large % mpd] if large % mpd else [])
+    return [split_tree(*((bs, small) if m >= n else (small, bs)), mpd) for bs in sizes]
+
+
 def _round_up(x, k):
     return (x + k - 1) // k * k
 
@@ -87,6 +98,7 @@ class Plan:
         ptab = np.zeros(self.n_params, PARAM_DT)
         leaves, tiles, panels, chunks = [], [], [], []
         self.param_leaves = []
+        self.param_trees = []
         off = 0
         fac_off = 0
         u_off = 0
@@ -167,6 +179,7 @@ class Plan:
                     self.eps_sparse.append(g["epsilon_sparse"])
                     self.rho_leaf.append(g["rho"])
             self.param_leaves.append(mine)
+            self.param_trees.append(split_tree(m, n, g["max_precond_dim"]) if kron else 0)
             r["leaf_end"] = len(leaves)
             r["tile_end"] = len(tiles)
             for c0 in range(0, numel, CHUNK):

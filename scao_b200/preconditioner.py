@@ -143,32 +143,50 @@ class PrecondView:
     def k(self):
         if not self._leaves:
             return 1
-        ks = self.plan.k[self.plan.param_leaves[self.pi]].tolist()
-        if self.use_block_diagonal:
-            return sum(ks) // max(len(ks), 1)
-        return ks[0]
+        ks = iter(self.plan.k[self.plan.param_leaves[self.pi]].tolist())
+
+        def walk(t):
+            # block-diagonal k = integer mean of the sub-blocks' k
+            # (preconditioner.py:329), applied at every nesting level
+            if t == 1:
+                return next(ks)
+            sub = [walk(c) for c in t]
+            if self.precond_step == 0:      # initialised as the first block's k (:194)
+                return sub[0]
+            return sum(sub) // max(len(sub), 1)
+        return walk(self.plan.param_trees[self.pi])
 
     @property
     def diag_ema(self):
         return self.plan.state_view(self.plan.diag_ema, self.pi)
 
+    def _tree_state(self, t, leaves):
+        if t == 1:
+            return next(leaves).state_dict()
+        blocks = [self._tree_state(c, leaves) for c in t]
+        k = blocks[0]["k"] if self.precond_step == 0 else \
+            sum(b["k"] for b in blocks) // max(len(blocks), 1)
+        return {"precond_step": self.precond_step, "k": k, "use_kronecker": False,
+                "use_block_diagonal": True, "blocks": blocks}
+
+    def _tree_load(self, t, st, leaves):
+        if t == 1:
+            next(leaves).load_state_dict(st)
+            return
+        for c, bs in zip(t, st["blocks"]):
+            self._tree_load(c, bs, leaves)
+
     def state_dict(self):
-        if self.use_block_diagonal:
-            d = {"precond_step": self.precond_step, "k": self.k, "use_kronecker": False,
-                 "use_block_diagonal": True}
-            d["blocks"] = [lf.state_dict() for lf in self._leaves]
-            return d
-        if self.use_kronecker:
-            return self._leaves[0].state_dict()
+        """Same schema as preconditioner.py:570-600, nested like the
+        reference's ``_blocks`` hierarchy."""
+        if self.use_block_diagonal or self.use_kronecker:
+            return self._tree_state(self.plan.param_trees[self.pi], iter(self._leaves))
         return {"precond_step": self.precond_step, "k": 1, "use_kronecker": False,
                 "use_block_diagonal": False, "diag_ema": self.diag_ema.clone()}
 
     def load_state_dict(self, st):
         self.precond_step = int(st["precond_step"])
-        if self.use_block_diagonal:
-            for lf, bs in zip(self._leaves, st["blocks"]):
-                lf.load_state_dict(bs)
-        elif self.use_kronecker:
-            self._leaves[0].load_state_dict(st)
+        if self.use_block_diagonal or self.use_kronecker:
+            self._tree_load(self.plan.param_trees[self.pi], st, iter(self._leaves))
         else:
             self.diag_ema.copy_(st["diag_ema"])
