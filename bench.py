@@ -193,6 +193,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--json-out", default=None)
+    ap.add_argument("--profile-range", action="store_true",
+                    help="cudaProfilerStart/Stop around the timed steps (ncu --profile-from-start off)")
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3)
 
@@ -273,6 +275,8 @@ def main():
     torch.cuda.synchronize()
     clocks.start()
     time.sleep(0.3)
+    if a.profile_range:
+        torch.cuda.profiler.start()
     ev[0].record(stream)
     for k in range(a.steps):
         gstep = opt._global_step + 1 if world == 1 else opt.global_step + 1
@@ -281,6 +285,8 @@ def main():
         opt.step()
         ev[k + 1].record(stream)
     torch.cuda.synchronize()
+    if a.profile_range:
+        torch.cuda.profiler.stop()
     if world > 1:
         torch.distributed.barrier()
     clk = clocks.stop()

@@ -43,32 +43,59 @@ def _round_up(x, k):
 
 
 class FlatLayout:
-    """Owner-major flat layout: rank r's parameters (in model order) occupy
-    [r*shard, (r+1)*shard) of a flat buffer."""
+    """Bucket-major owner layout of a flat buffer.  Each rank's parameters (in
+    model order) are cut into ``buckets`` contiguous groups of similar size;
+    bucket b occupies [base_b, base_b + world * seg_b) with rank r's part at
+    base_b + r * seg_b, so one reduce-scatter / all-gather per bucket works on
+    a contiguous range and the buckets can be pipelined."""
 
-    def __init__(self, numels, owner, world):
+    def __init__(self, numels, owner, world, buckets=1):
         self.world = world
         self.owner = owner
-        self.offsets = [0] * len(numels)
-        fill = [0] * world
-        for i, n in enumerate(numels):
-            r = owner[i]
-            self.offsets[i] = fill[r]
-            fill[r] += _round_up(n, ALIGN)
-        self.shard = max(max(fill), ALIGN)
         self.numels = numels
+        n = len(numels)
+        self.bucket = [0] * n
+        self.offsets = [0] * n
+        fill = {}
+        for r in range(world):
+            mine = [i for i in range(n) if owner[i] == r]
+            tot = sum(_round_up(numels[i], ALIGN) for i in mine)
+            acc = 0
+            for i in mine:
+                b = min(buckets - 1, int(acc * buckets // max(tot, 1)))
+                self.bucket[i] = b
+                self.offsets[i] = fill.get((r, b), 0)
+                fill[(r, b)] = self.offsets[i] + _round_up(numels[i], ALIGN)
+                acc += _round_up(numels[i], ALIGN)
+        self.nb = buckets
+        self.seg = [max([fill.get((r, b), 0) for r in range(world)] + [ALIGN])
+                    for b in range(buckets)]
+        self.base = [0] * buckets
+        self.gbase = [0] * buckets      # bucket start inside a rank's own shard
+        for b in range(1, buckets):
+            self.base[b] = self.base[b - 1] + world * self.seg[b - 1]
+            self.gbase[b] = self.gbase[b - 1] + self.seg[b - 1]
+        self.total = self.base[-1] + world * self.seg[-1]
+        self.shard = sum(self.seg)
 
     def global_offset(self, i):
-        return self.owner[i] * self.shard + self.offsets[i]
+        b = self.bucket[i]
+        return self.base[b] + self.owner[i] * self.seg[b] + self.offsets[i]
+
+    def shard_offset(self, i):
+        return self.gbase[self.bucket[i]] + self.offsets[i]
 
 
 class ShardedSCAO:
     """Owner-compute wrapper.  ``make_inner(list of (param, spec))`` builds the
-    per-rank optimizer over the owned parameters (a ``scao_b200.SCAO`` on GPUs;
-    tests inject CPU stand-ins).  Parameters are re-pointed into one flat
-    buffer so the all-gather writes them in place."""
+    per-rank optimizer over the owned parameters of one bucket (a
+    ``scao_b200.SCAO`` on GPUs; tests inject CPU stand-ins).  Parameters are
+    re-pointed into one flat buffer so the all-gather writes them in place.
+    On NCCL the buckets are pipelined: all reduce-scatters are queued on a
+    communication stream, bucket b's step runs as soon as its gradients have
+    arrived, and its all-gather is queued right after its step."""
 
-    def __init__(self, params, workload, make_inner, group=None, costs=None):
+    def __init__(self, params, workload, make_inner, group=None, costs=None, buckets=4):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -76,37 +103,48 @@ class ShardedSCAO:
         self.specs = list(workload.params)
         numels = [p.numel() for p in self.params]
         self.owner = partition(costs or numels, self.world)
-        self.layout = FlatLayout(numels, self.owner, self.world)
+        self.layout = lay = FlatLayout(numels, self.owner, self.world, buckets)
         p0 = self.params[0]
         self.dtype, self.device = p0.dtype, p0.device
-        n = self.layout.shard * self.world
-        self.flat_p = torch.zeros(n, dtype=self.dtype, device=self.device)
+        self.flat_p = torch.zeros(lay.total, dtype=self.dtype, device=self.device)
         for i, p in enumerate(self.params):
-            o = self.layout.global_offset(i)
+            o = lay.global_offset(i)
             view = self.flat_p[o:o + p.numel()].view_as(p)
             view.copy_(p.data)
             p.data = view
         self.my = [i for i in range(len(self.params)) if self.owner[i] == self.rank]
-        s0 = self.rank * self.layout.shard
-        self.my_p = self.flat_p[s0:s0 + self.layout.shard]
-        self.my_g = torch.zeros(self.layout.shard, dtype=self.dtype, device=self.device)
+        self.my_g = torch.zeros(lay.shard, dtype=self.dtype, device=self.device)
         for i in self.my:
-            o = self.layout.offsets[i]
+            o = lay.shard_offset(i)
             self.params[i].grad = self.my_g[o:o + numels[i]].view_as(self.params[i])
-        self.inner = make_inner([(self.params[i], self.specs[i]) for i in self.my])
+        self.inner = []
+        for b in range(lay.nb):
+            mine = [i for i in self.my if lay.bucket[i] == b]
+            self.inner.append(make_inner([(self.params[i], self.specs[i]) for i in mine])
+                              if mine else None)
         self.global_step = 0
         self.grad_sets = []
         self.cur = None
         self.nccl = dist.get_backend(group) == "nccl"
+        self.comm = torch.cuda.Stream(self.device) if self.nccl else None
 
     def owned_specs(self):
         return [self.specs[i] for i in self.my]
 
+    # bucket views ------------------------------------------------------------
+    def _views(self, flat, b):
+        lay = self.layout
+        full = flat[lay.base[b]:lay.base[b] + self.world * lay.seg[b]]
+        mine_p = self.flat_p[lay.base[b] + self.rank * lay.seg[b]:
+                             lay.base[b] + (self.rank + 1) * lay.seg[b]]
+        mine_g = self.my_g[lay.gbase[b]:lay.gbase[b] + lay.seg[b]]
+        return full, mine_p, mine_g
+
     # gradients ------------------------------------------------------------
     def stage_grads(self, full_grads):
-        """Lay a full (per-rank) gradient list out as one owner-major flat
-        buffer; returns its index for ``use_grads``."""
-        flat = torch.zeros(self.layout.shard * self.world, dtype=self.dtype, device=self.device)
+        """Lay a full (per-rank) gradient list out as one flat buffer in the
+        bucket-major owner layout; returns its index."""
+        flat = torch.zeros(self.layout.total, dtype=self.dtype, device=self.device)
         for i, g in enumerate(full_grads):
             o = self.layout.global_offset(i)
             flat[o:o + g.numel()].copy_(g.reshape(-1))
@@ -123,8 +161,8 @@ class ShardedSCAO:
 
     def flat_grad_from_params(self):
         """Training-loop entry: gather every parameter's local .grad (as left
-        by backward) into the owner-major flat buffer."""
-        flat = torch.zeros(self.layout.shard * self.world, dtype=self.dtype, device=self.device)
+        by backward) into the flat buffer."""
+        flat = torch.zeros(self.layout.total, dtype=self.dtype, device=self.device)
         for i, p in enumerate(self.params):
             if p.grad is None:
                 continue
@@ -137,22 +175,42 @@ class ShardedSCAO:
         self.global_step += 1
         if self.cur is None:
             raise RuntimeError("no gradients staged (load_grads / flat_grad_from_params)")
-        if self.nccl:
-            dist.reduce_scatter_tensor(self.my_g, self.cur, op=dist.ReduceOp.AVG,
-                                       group=self.group)
-        else:
-            tmp = self.cur.clone()
-            dist.all_reduce(tmp, group=self.group)
-            s0 = self.rank * self.layout.shard
-            self.my_g.copy_(tmp[s0:s0 + self.layout.shard] / self.world)
-        if self.my:
-            self.inner.step()
-        if self.nccl:
-            dist.all_gather_into_tensor(self.flat_p, self.my_p, group=self.group)
-        else:
-            parts = list(self.flat_p.chunk(self.world))
-            dist.all_gather(parts, self.my_p.clone(), group=self.group)
-            self.flat_p.copy_(torch.cat(parts))
+        nb = self.layout.nb
+        if not self.nccl:
+            for b in range(nb):
+                full_g, mine_p, mine_g = self._views(self.cur, b)
+                tmp = full_g.clone()
+                dist.all_reduce(tmp, group=self.group)
+                seg = self.layout.seg[b]
+                mine_g.copy_(tmp[self.rank * seg:(self.rank + 1) * seg] / self.world)
+                if self.inner[b] is not None:
+                    self.inner[b].step()
+                full_p, _, _ = self._views(self.flat_p, b)
+                parts = list(full_p.chunk(self.world))
+                dist.all_gather(parts, mine_p.clone(), group=self.group)
+                full_p.copy_(torch.cat(parts))
+            return
+        D = torch.cuda.current_stream(self.device)
+        C = self.comm
+        C.wait_stream(D)
+        ev_rs = [torch.cuda.Event() for _ in range(nb)]
+        with torch.cuda.stream(C):
+            for b in range(nb):
+                full_g, _, mine_g = self._views(self.cur, b)
+                dist.reduce_scatter_tensor(mine_g, full_g, op=dist.ReduceOp.AVG,
+                                           group=self.group)
+                ev_rs[b].record(C)
+        for b in range(nb):
+            D.wait_event(ev_rs[b])
+            if self.inner[b] is not None:
+                self.inner[b].step()
+            ev = torch.cuda.Event()
+            ev.record(D)
+            full_p, mine_p, _ = self._views(self.flat_p, b)
+            with torch.cuda.stream(C):
+                C.wait_event(ev)
+                dist.all_gather_into_tensor(full_p, mine_p, group=self.group)
+        D.wait_stream(C)
 
     @property
     def _global_step(self):

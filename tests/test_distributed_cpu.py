@@ -21,14 +21,20 @@ def test_partition_balanced_and_deterministic():
 
 
 def test_flat_layout_disjoint_aligned():
-    numels = [10, 300, 64, 1, 1000]
+    numels = [10, 300, 64, 1, 1000, 77, 5000, 3]
     owner = partition(numels, 2)
-    lay = FlatLayout(numels, owner, 2)
-    spans = sorted((lay.global_offset(i), lay.global_offset(i) + n) for i, n in enumerate(numels))
-    for (a0, a1), (b0, _) in zip(spans, spans[1:]):
-        assert a1 <= b0
-    assert all(lay.offsets[i] % 64 == 0 for i in range(len(numels)))
-    assert all(lay.offsets[i] + numels[i] <= lay.shard for i in range(len(numels)))
+    for nb in (1, 3):
+        lay = FlatLayout(numels, owner, 2, nb)
+        spans = sorted((lay.global_offset(i), lay.global_offset(i) + n)
+                       for i, n in enumerate(numels))
+        for (a0, a1), (b0, _) in zip(spans, spans[1:]):
+            assert a1 <= b0
+        assert spans[-1][1] <= lay.total
+        assert all(lay.offsets[i] % 64 == 0 for i in range(len(numels)))
+        assert all(lay.offsets[i] + numels[i] <= lay.seg[lay.bucket[i]]
+                   for i in range(len(numels)))
+        # a rank's bucket segments tile its own shard
+        assert lay.shard == sum(lay.seg)
 
 
 class _SGD:
@@ -54,7 +60,7 @@ def _worker(rank, world, port, q):
         # per-rank gradients differ; the owner update must use their average
         grads = [torch.full(s.shape, float(rank + 1)) * (i + 1) for i, s in enumerate(w.params)]
         avg = [torch.full(s.shape, (1 + world) / 2.0) * (i + 1) for i, s in enumerate(w.params)]
-        opt = ShardedSCAO(params, w, _SGD)
+        opt = ShardedSCAO(params, w, _SGD, buckets=2)
         opt.load_grads(grads)
         opt.step()
         errs = [float((p - (r - 0.1 * g)).abs().max()) for p, r, g in zip(params, ref, avg)]
