@@ -303,6 +303,84 @@ class OraclePreconditioner:
 # optimizer.py
 # ---------------------------------------------------------------------------
 
+# ---------------------------------------------------------------------------
+# gradient filter (optimizer.py:40-97)
+# ---------------------------------------------------------------------------
+
+QUANTILE_CAP = 1 << 24   # torch.quantile refuses larger inputs
+
+
+def quantile_f32(x, q):
+    """``torch.quantile(x, q)`` (linear interpolation) for a float32 vector,
+    as ATen computes it: rank = float32(q) * (n - 1) in float32, the two
+    neighbouring order statistics, and ``lerp`` with the weight
+    rank - floor(rank) (fused multiply-add form, weight < 0.5 from below).
+    Any NaN gives NaN.  Beyond torch's 2^24-element cap (where the reference
+    raises) the rank is formed in float64 instead."""
+    x = np.ascontiguousarray(x, dtype=F32).ravel()
+    n = x.size
+    if n == 0:
+        return F32(np.nan)
+    if np.isnan(x).any():
+        return F32(np.nan)
+    if n <= QUANTILE_CAP:
+        rank = F32(F32(q) * F32(n - 1))
+        lo = int(math.floor(rank))
+        w = F32(rank - F32(lo))
+    else:
+        rank = float(F32(q)) * (n - 1)
+        lo = int(math.floor(rank))
+        w = F32(rank - lo)
+    hi = min(lo + (1 if w > 0 else 0), n - 1)
+    part = np.partition(x, (lo, hi)) if hi != lo else np.partition(x, lo)
+    a, b = part[lo], part[hi]
+    return lerp_f32(a, b, w)
+
+
+def lerp_f32(a, b, w):
+    """ATen ``lerp`` (Lerp.h) with its multiply-add contracted: exact
+    products in float64, one rounding to float32."""
+    a, b, w = F32(a), F32(b), F32(w)
+    d = F32(b - a)
+    if abs(w) < 0.5:
+        return F32(float(w) * float(d) + float(a))
+    return F32(float(b) - float(d) * float(F32(F32(1.0) - w)))
+
+
+class OracleSparseFilter:
+    """``_SparseGradFilter`` (optimizer.py:40-56) and, with ``dynamic``,
+    ``_DynamicSparseFilter`` (:59-97)."""
+
+    def __init__(self, sparsity=0.7, dynamic=False, ema=0.99, min_sparsity=0.3,
+                 max_sparsity=0.9, norm_ema=0.95):
+        self.base = sparsity
+        self.sparsity = sparsity
+        self.dynamic = dynamic
+        self.ema = ema
+        self.min_s, self.max_s, self.norm_coeff = min_sparsity, max_sparsity, norm_ema
+        self.norm_ema = 1.0
+        self.global_ref = 1.0
+        self.mag = None
+
+    def set_global_norm_ref(self, g):
+        self.global_ref = max(g, 1e-8)
+
+    def __call__(self, grad):
+        if self.dynamic:
+            layer = float(norm_f32(grad))
+            self.norm_ema = self.norm_coeff * self.norm_ema + (1.0 - self.norm_coeff) * layer
+            ratio = self.norm_ema / self.global_ref
+            margin = 0.2 * (1.0 - min(ratio, 2.0) / 2.0)
+            self.sparsity = float(max(self.min_s, min(self.max_s, self.base + margin)))
+        mag = np.abs(grad).astype(F32)
+        if self.mag is None:
+            self.mag = mag.copy()
+        else:
+            self.mag = (self.mag * F32(self.ema)) + F32(1.0 - self.ema) * mag
+        thr = quantile_f32(self.mag, self.sparsity)
+        return grad * (self.mag >= thr).astype(F32)
+
+
 _DEFAULTS = dict(lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01,
                  precond_freq=20, epsilon_sparse=0.05, k_min=8, k_max=128,
                  rho=0.999, tau=1.0, warmup_steps=100, blend_steps=50,
@@ -311,8 +389,9 @@ _DEFAULTS = dict(lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01,
 
 
 class OracleSCAO:
-    """optimizer.py:221-645 restricted to the deterministic path
-    (sparsity=0, noise_std_init=0, no R1-R5 extensions), numpy float32.
+    """optimizer.py:221-645 restricted to the deterministic path (no gradient
+    noise, no R1/R3-R5 extensions; the sparse filter and its R2 dynamic form
+    are included), numpy float32.
 
     ``params`` is a list of float32 arrays holding parameter-dtype values;
     ``groups`` is a list of dicts {"params": [indices], **overrides}.
@@ -323,7 +402,12 @@ class OracleSCAO:
         self.dtype = dtype
         self.params = [round_to(np.array(p, dtype=F32), dtype) for p in params]
         d = dict(_DEFAULTS)
-        for k in ("sparsity", "noise_std_init", "async_precond", "noise_anneal"):
+        self.sparsity = float(kw.pop("sparsity", 0.0))
+        self.dynamic_sparsity = bool(kw.pop("dynamic_sparsity", False))
+        self.filters = {}
+        # gradient noise (optimizer.py:544-545) draws from torch's generator and
+        # is not restated: the oracle is the noise-free path
+        for k in ("noise_std_init", "async_precond", "noise_anneal"):
             kw.pop(k, None)
         d.update(kw)
         if groups is None:
@@ -365,6 +449,9 @@ class OracleSCAO:
         if norms:
             avg = sum(norms) / len(norms)
             self.global_norm_ema = 0.95 * self.global_norm_ema + 0.05 * avg
+        if self.dynamic_sparsity:
+            for f in self.filters.values():
+                f.set_global_norm_ref(self.global_norm_ema)
         for group in self.groups:
             self._step_group(group, grads)
         if self.lookahead_k > 0 and self.global_step % self.lookahead_k == 0:
@@ -412,6 +499,10 @@ class OracleSCAO:
             step = st["step"]
             raw = np.asarray(gr, dtype=F32)       # p.grad (param dtype values)
             grad = raw
+            if self.sparsity > 0.0:              # optimizer.py:536-542
+                if i not in self.filters:
+                    self.filters[i] = OracleSparseFilter(self.sparsity, self.dynamic_sparsity)
+                grad = self.filters[i](grad)
             p = self.params[i]
             if wd != 0.0:
                 p = round_to(p * F32(1.0 - lr * wd), dt)

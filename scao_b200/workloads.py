@@ -83,18 +83,19 @@ def _llama_layers(n_layers, d, n_q, n_kv, head_dim, d_ff):
 
 
 def tiny(dtype="float32", max_precond_dim=4096, steps=40, grad_scale=1e-2,
-         int8=True) -> Workload:
+         int8=True, extra=None) -> Workload:
     """Small GPT-like set used for committed golden fixtures and CPU tests.
 
     With the default gradient scale the int8 EMA never leaves its 1e-4*I
     initialisation (the degenerate regime of the benchmark configs);
     ``grad_scale=1`` gives well-separated curvature spectra."""
     ps = _gpt_layers(1, 32, 128)
+    kw = dict(lr=1e-3, betas=(0.9, 0.999), precond_freq=5, warmup_steps=8,
+              blend_steps=10, min_precond_updates=1, k_min=4, k_max=8,
+              use_int8_ema=int8, max_precond_dim=max_precond_dim, **_PARITY)
+    kw.update(extra or {})
     return Workload(
-        "tiny", ps,
-        dict(lr=1e-3, betas=(0.9, 0.999), precond_freq=5, warmup_steps=8,
-             blend_steps=10, min_precond_updates=1, k_min=4, k_max=8,
-             use_int8_ema=int8, max_precond_dim=max_precond_dim, **_PARITY),
+        "tiny", ps, kw,
         grad_rank=4, grad_decay=0.7, param_dtype=dtype, steps=steps,
         grad_scale=grad_scale)
 

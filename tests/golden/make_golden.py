@@ -38,6 +38,15 @@ CASES = {
     "f32_spec": ("float32", 4096, 30, 1.0, False),
     "int8_spec": ("float32", 48, 30, 1.0, True),
     "bf16_spec": ("bfloat16", 48, 30, 1.0, True),
+    "f32_sparse": ("float32", 4096, 30, 1.0, True),
+    "bf16_dyn": ("bfloat16", 48, 30, 1.0, True),
+}
+
+# optimizer keyword overrides of a case (the gradient filter of
+# optimizer.py:40-97, static and R2-dynamic)
+EXTRA = {
+    "f32_sparse": dict(sparsity=0.7),
+    "bf16_dyn": dict(sparsity=0.6, dynamic_sparsity=True),
 }
 
 
@@ -50,7 +59,7 @@ def grad_digest(grads):
 
 def run_case(scao_mod, name, dtype, mpd, steps, gs, int8):
     w = workloads.tiny(dtype=dtype, max_precond_dim=mpd, steps=steps,
-                       grad_scale=gs, int8=int8)
+                       grad_scale=gs, int8=int8, extra=EXTRA.get(name))
     params0 = synthetic.init_params(w, seed=0)
     params = [torch.nn.Parameter(p.clone()) for p in params0]
     opt = scao_mod.SCAO(params, **w.scao_kwargs)
@@ -140,15 +149,18 @@ def rank_cases(utils):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="reference checkout root")
+    ap.add_argument("--only", nargs="*", help="regenerate only these run cases")
     a = ap.parse_args()
     sys.path.insert(0, a.ref)
     import scao  # noqa: E402  (the reference package)
     from scao import utils  # noqa: E402
     torch.set_num_threads(min(8, os.cpu_count() or 1))
-    quant_cases(utils)
-    rank_cases(utils)
+    if not a.only:
+        quant_cases(utils)
+        rank_cases(utils)
     for name, args in CASES.items():
-        run_case(scao, name, *args)
+        if not a.only or name in a.only:
+            run_case(scao, name, *args)
 
 
 if __name__ == "__main__":

@@ -13,6 +13,15 @@ CASES = {
     "f32_spec": ("float32", 4096, 30, 1.0, False),
     "int8_spec": ("float32", 48, 30, 1.0, True),
     "bf16_spec": ("bfloat16", 48, 30, 1.0, True),
+    "f32_sparse": ("float32", 4096, 30, 1.0, True),
+    "bf16_dyn": ("bfloat16", 48, 30, 1.0, True),
+}
+
+# optimizer keyword overrides of a case (the gradient filter of
+# optimizer.py:40-97, static and R2-dynamic)
+EXTRA = {
+    "f32_sparse": dict(sparsity=0.7),
+    "bf16_dyn": dict(sparsity=0.6, dynamic_sparsity=True),
 }
 
 

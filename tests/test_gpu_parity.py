@@ -10,7 +10,7 @@ import numpy as np
 import pytest
 import torch
 
-from golden_util import CASES, load, principal_angle, rel_err, subspace_angle
+from golden_util import CASES, EXTRA, load, principal_angle, rel_err, subspace_angle
 from oracle import scao_oracle as O
 from scao_b200 import SCAO, _lib, synthetic, workloads
 
@@ -132,7 +132,8 @@ def test_low_rank_precond_mm(left):
 def run_gpu(name, steps=None):
     dt, mpd, nsteps, gs, i8 = CASES[name]
     steps = steps or nsteps
-    w = workloads.tiny(dtype=dt, max_precond_dim=mpd, steps=steps, grad_scale=gs, int8=i8)
+    w = workloads.tiny(dtype=dt, max_precond_dim=mpd, steps=steps, grad_scale=gs, int8=i8,
+                       extra=EXTRA.get(name))
     p0 = synthetic.init_params(w)
     params = [torch.nn.Parameter(p.clone().to(DEV)) for p in p0]
     opt = SCAO(params, **w.scao_kwargs)

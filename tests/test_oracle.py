@@ -3,7 +3,7 @@ package itself (tests/golden/make_golden.py).  CPU only."""
 import numpy as np
 import pytest
 
-from golden_util import CASES, load, principal_angle, rel_err, subspace_angle
+from golden_util import CASES, EXTRA, load, principal_angle, rel_err, subspace_angle
 from oracle import scao_oracle as O
 from scao_b200 import synthetic, workloads
 
@@ -36,7 +36,7 @@ def test_bf16_rounding_matches_torch():
 def run_oracle(name):
     dt, mpd, steps, gs, i8 = CASES[name]
     w = workloads.tiny(dtype=dt, max_precond_dim=mpd, steps=steps,
-                       grad_scale=gs, int8=i8)
+                       grad_scale=gs, int8=i8, extra=EXTRA.get(name))
     p0 = [p.float().numpy() for p in synthetic.init_params(w)]
     opt = O.OracleSCAO(p0, dtype=dt, **w.scao_kwargs)
     gen = synthetic.LowRankGradients(w)
@@ -93,3 +93,23 @@ def test_grad_generator_is_reproducible():
             for g in gen.next():
                 h.update(g.float().contiguous().numpy().tobytes())
             assert h.hexdigest() == str(G["digests"][t])
+
+
+def test_quantile_matches_torch():
+    """The oracle's quantile (optimizer.py:56 calls torch.quantile) against
+    torch itself: random, tied and wide-range inputs, q at the edges."""
+    import torch
+    rng = np.random.default_rng(1)
+    for t in range(600):
+        n = int(rng.integers(1, 5000))
+        kind = t % 3
+        if kind == 0:
+            x = (rng.random(n) ** 4).astype(np.float32)
+        elif kind == 1:
+            x = (np.round(rng.random(n) * 20) / 7).astype(np.float32)
+        else:
+            x = (np.abs(rng.standard_normal(n)) * 10.0 ** rng.integers(-8, 3)).astype(np.float32)
+        q = float(rng.random()) if t % 5 else [0.0, 1.0, 0.5, 0.7, 0.3][t // 5 % 5]
+        ref = np.float32(torch.quantile(torch.from_numpy(x), q).item())
+        assert O.quantile_f32(x, q) == ref, (t, n, q)
+    assert np.isnan(O.quantile_f32(np.array([1, np.nan, 2], np.float32), 0.5))
