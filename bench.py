@@ -195,11 +195,18 @@ def main():
     ap.add_argument("--json-out", default=None)
     ap.add_argument("--profile-range", action="store_true",
                     help="cudaProfilerStart/Stop around the timed steps (ncu --profile-from-start off)")
+    ap.add_argument("--sparsity", type=float, default=0.0,
+                    help="gradient filter level (the reference default is 0.7; the headline "
+                         "configuration runs the deterministic path, 0)")
+    ap.add_argument("--dynamic-sparsity", action="store_true")
+    ap.add_argument("--noise", type=float, default=0.0, help="noise_std_init")
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3)
 
     from scao_b200 import workloads
     workload = workloads.c4(n_layers=a.layers)
+    workload.scao_kwargs.update(sparsity=a.sparsity, noise_std_init=a.noise,
+                                dynamic_sparsity=a.dynamic_sparsity)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -207,7 +214,9 @@ def main():
            "param_dtype": workload.param_dtype, "state_dtype": "float32",
            "int8_ema": True, "max_precond_dim": 1024, "k_max": 64, "precond_freq": 10,
            "warmup_steps": 20, "blend_steps": 50, "grad_rank": workload.grad_rank,
-           "l2": "inputs larger than L2 (2.1 GB grads, 16.6 GB fp32 state per step)"}
+           "l2": "inputs larger than L2 (2.1 GB grads, 16.6 GB fp32 state per step)",
+           "sparsity": a.sparsity, "dynamic_sparsity": a.dynamic_sparsity,
+           "noise_std_init": a.noise}
 
     if a.impl == "reference":
         if rank != 0:
@@ -308,11 +317,16 @@ def main():
     hbm = float(pk.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
     apply_slots = ["proj", "diag_pre", "leaf_coef", "param_pre", "apply_kron", "apply_flat",
                    "param_post", "global_norm", "apply_p"]
+    if a.sparsity > 0:
+        apply_slots.append("filter")
     apply_ms = sum(prof.get(s, (0.0, 0))[0] for s in apply_slots) / a.steps
     owned = opt.owned_specs() if world > 1 else workload.params
     wl_local = type(workload)(workload.name, owned, workload.scao_kwargs, workload.grad_rank,
                               workload.grad_decay, workload.param_dtype)
     abytes = algorithmic_bytes(wl_local, lambda s: 1 if s.adam_only else 2)
+    if a.sparsity > 0:
+        # filter: magnitude EMA read + write and one read for the selection
+        abytes += 12 * sum(int(np.prod(s.shape)) for s in wl_local.params)
     achieved = abytes / (apply_ms * 1e-3) / 1e9 if apply_ms > 0 else 0.0
     kern = {k: {"ms_total": round(v[0], 3), "launches": v[1]} for k, v in sorted(prof.items())}
 

@@ -118,6 +118,43 @@ typedef struct { int32_t leaf, row0, nrows, pad0; } ScaoPanel;
 /* Flat chunk of a parameter (element range).                               */
 typedef struct { int32_t param, pad0; int64_t begin, end; } ScaoChunk;
 
+/* Gradient filter (scao/optimizer.py:40-97, applied at :536-542) and
+ * gradient noise (:544-545).  The filtered gradient
+ *     grad * (mag_ema >= quantile(mag_ema, sparsity))
+ * feeds the moments and prev_grad; the preconditioner keeps the raw grad.
+ * The quantile is an exact radix selection of two order statistics on the
+ * float32 bit patterns (3 levels: bits 31-20, 19-8, 7-0).                   */
+typedef struct {
+    double norm_ema;       /* R2 layer-norm EMA (starts at 1.0)              */
+    double global_ref;     /* R2 global-norm reference (starts at 1.0)       */
+    double sparsity;       /* quantile level of this step                     */
+    int64_t rem_lo, rem_hi;/* rank left inside the radix prefix found so far */
+    uint32_t pre_lo, pre_hi; /* radix prefixes (float32 bit patterns)        */
+    float w;               /* lerp weight: rank - floor(rank)                */
+    float thr;             /* threshold of this step                          */
+    float gsq;             /* sum of raw grad^2 of this step                  */
+    int32_t first;         /* 1 until the parameter's first filter call      */
+    int32_t nan;           /* 1 if the magnitude EMA holds a NaN             */
+    int32_t sel_begin, sel_end; /* selection chunks of this parameter        */
+    int32_t pad0;
+} ScaoFilterParam;
+
+typedef struct {
+    int32_t mode;          /* 0 off, 1 static sparsity, 2 dynamic (R2)        */
+    int32_t n_sel;         /* number of selection chunks                      */
+    const ScaoChunk* sel;  /* <= 65536-element pieces of every parameter      */
+    float* mag_ema;        /* magnitude EMA, numel total (state arena offsets) */
+    ScaoFilterParam* fp;   /* n_params                                        */
+    uint32_t* hist;        /* n_params x 2 x 4096 radix histograms            */
+    float* sel_part;       /* per selection chunk: sum of raw grad^2          */
+    double base, min_s, max_s, norm_coeff; /* sparsity, 0.3, 0.9, 0.95 (R2)   */
+    float ema, ema_c;      /* float32(ema), float32(1 - ema)                  */
+    int32_t noise_on;      /* 1 if noise_std > 1e-9 this step                 */
+    float noise_std;       /* float32(noise_std)                              */
+    uint64_t noise_seed;   /* Philox-4x32-10 key                              */
+    uint64_t noise_step;   /* counter word: global step                       */
+} ScaoFilterDev;
+
 /* Device-side plan: pointers to the tables and arenas above.              */
 typedef struct {
     int32_t n_params, n_leaves, n_tiles, n_panels, n_chunks;
@@ -163,6 +200,7 @@ typedef struct {
     int32_t n_diag, n_flat, n_p, pad2_;
     int32_t* err;                /* device error flag: set to 1 when a bounded
                                     wait on the tensor core timed out       */
+    ScaoFilterDev filt;          /* gradient filter and noise (mode 0: off) */
 } ScaoPlanDev;
 
 /* ---------------------------------------------------------------------- */

@@ -49,6 +49,24 @@ CHUNK_DT = np.dtype([("param", "<i4"), ("pad0", "<i4"), ("begin", "<i8"), ("end"
 _P = C.c_void_p
 
 
+class FilterDev(C.Structure):
+    _fields_ = [
+        ("mode", C.c_int32), ("n_sel", C.c_int32), ("sel", _P), ("mag_ema", _P),
+        ("fp", _P), ("hist", _P), ("sel_part", _P),
+        ("base", C.c_double), ("min_s", C.c_double), ("max_s", C.c_double),
+        ("norm_coeff", C.c_double), ("ema", C.c_float), ("ema_c", C.c_float),
+        ("noise_on", C.c_int32), ("noise_std", C.c_float),
+        ("noise_seed", C.c_uint64), ("noise_step", C.c_uint64),
+    ]
+
+
+FILTER_PARAM_DT = np.dtype([
+    ("norm_ema", "<f8"), ("global_ref", "<f8"), ("sparsity", "<f8"),
+    ("rem_lo", "<i8"), ("rem_hi", "<i8"), ("pre_lo", "<u4"), ("pre_hi", "<u4"),
+    ("w", "<f4"), ("thr", "<f4"), ("gsq", "<f4"), ("first", "<i4"), ("nan", "<i4"),
+    ("sel_begin", "<i4"), ("sel_end", "<i4"), ("pad0", "<i4")])
+
+
 class PlanDev(C.Structure):
     _fields_ = [
         ("n_params", C.c_int32), ("n_leaves", C.c_int32), ("n_tiles", C.c_int32),
@@ -66,6 +84,7 @@ class PlanDev(C.Structure):
         ("diag_list", _P), ("flat_list", _P), ("p_list", _P),
         ("n_diag", C.c_int32), ("n_flat", C.c_int32), ("n_p", C.c_int32), ("pad2_", C.c_int32),
         ("err", _P),
+        ("filt", FilterDev),
     ]
 
 
@@ -74,6 +93,8 @@ def check_layout():
     assert STEP_DT.itemsize == 128, STEP_DT.itemsize
     assert LEAF_DT.itemsize == 160, LEAF_DT.itemsize
     assert CHUNK_DT.itemsize == 24, CHUNK_DT.itemsize
+    assert FILTER_PARAM_DT.itemsize == 80, FILTER_PARAM_DT.itemsize
+    assert C.sizeof(FilterDev) == 112, C.sizeof(FilterDev)
 
 
 check_layout()

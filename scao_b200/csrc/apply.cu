@@ -4,14 +4,16 @@
 // and the curvature clip (optimizer.py:667-678, preconditioner.py:527-564).
 //
 // Kernel sequence of one step (scao_plan_step):
-//   proj       P_panel = U_l[rows]^T (G[rows] U_r)      per 64-row panel
-//              + sum p_dec^2 per panel (LARS, optimizer.py:373)
+//   filter     (sparsity > 0) magnitude EMA + exact quantile threshold,
+//              filter.cu
+//   proj       P_panel = U_l[rows]^T (G[rows] U_r)      per 128-row panel
 //   diag_pre   natural-norm^2 and p_dec^2 of diagonal-mode params
-//   leaf_coef  P = sum of panels; nat^2; Delta = (s_l s_r^T - 1) o P;
-//              W = U_l Delta                            per leaf
+//   leaf_coef  P = sum of panels; nat^2; Delta = (s_l s_r^T - 1) o P
+//   leaf_w     W = U_l Delta as bf16 hi/lo operand tiles
 //   param_pre  clip factor tau / nat  per param
-//   apply_kron per 64x64 tile: corr = W U_r^T, g_prec = round(G + corr),
-//              clip, blend, Adan moments, update u (rounded to param dtype)
+//   apply_kron per 128x128 tile: corr = W U_r^T on the tensor core,
+//              g_prec = round(G + corr), clip, blend, Adan moments,
+//              update u (rounded to param dtype), sum p_dec^2
 //   apply_flat Phase-1 Adam (full update) and Phase-2 diagonal params
 //   param_post LARS trust ratio -> alpha = -(lr * trust) per param
 //   global     global grad-norm EMA (optimizer.py:439-446)
@@ -24,14 +26,13 @@
 #include "common.cuh"
 #include "prof.cuh"
 #include "tc.cuh"
+#include "filter.cuh"
 
 namespace {
 
 constexpr int NT = 256;
-constexpr int TT = 64;       // apply tile edge
 constexpr int TC_T = 128;    // tensor-core tile edge (rows and columns)
 
-enum { PS_CLIPMUL = 0, PS_CLIP, PS_PNORM2, PS_UNORM2, PS_GNORM2, PS_ALPHA, PS_NAT, PS_TRUST };
 
 __device__ __forceinline__ float fmul(float a, float b) { return __fmul_rn(a, b); }
 __device__ __forceinline__ float fadd(float a, float b) { return __fadd_rn(a, b); }
@@ -41,90 +42,6 @@ __device__ __forceinline__ float fdiv(float a, float b) { return __fdiv_rn(a, b)
 // S^(-1/4) and S^(-1/2) with the clamp of utils.py:113 / preconditioner.py:558
 __device__ __forceinline__ float s_inv4(float s) { return powf(fmaxf(s, 1e-8f), -0.25f); }
 __device__ __forceinline__ float s_inv2(float s) { return powf(fmaxf(s, 1e-8f), -0.5f); }
-
-// ---------------------------------------------------------------------------
-// projection: T = G_panel * U_r (rows x kpad), P_part = U_l[rows]^T T
-// ---------------------------------------------------------------------------
-template <int KP>
-__global__ void __launch_bounds__(NT)
-proj_kernel(ScaoPlanDev P) {
-    const ScaoPanel pn = P.panels[blockIdx.x];
-    const ScaoLeaf& L = P.leaves[pn.leaf];
-    const ScaoParamStep& S = P.step[L.param];
-    if (S.phase != 2) return;
-    const ScaoParam& pr = P.params[L.param];
-    const int dt = pr.dtype;
-    const void* g = (const void*)S.g_ptr;
-    const void* pp = (const void*)S.p_ptr;
-    const int kp = L.kpad;
-    const float* Ul = P.u + L.ul_off;
-    const float* Ur = P.u + L.ur_off;
-    constexpr int TKK = 16;
-    constexpr int CPT = KP / 16;         // columns per thread
-    extern __shared__ float psm[];
-    float (*Gs)[TT + 4] = (float (*)[TT + 4])psm;                  // [TKK][TT+4]
-    float (*Us)[KP + 4] = (float (*)[KP + 4])(psm + TKK * (TT + 4)); // [TKK][KP+4]
-    float (*Ts)[KP + 4] = Us + TKK;                                 // [TT][KP+4]
-    float (*Ls)[KP + 4] = Ts + TT;                                  // [TT][KP+4]
-    __shared__ float red[32];
-    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
-    float acc[4][CPT] = {};
-    float psq = 0.f;
-    const float wdm = S.wd_mult;
-    for (int c0 = 0; c0 < L.b; c0 += TKK) {
-        for (int e = tid; e < TT * TKK; e += NT) {
-            const int r = e >> 4, c = e & 15;
-            float v = 0.f;
-            if (r < pn.nrows && c0 + c < L.b) {
-                const int64_t off = (int64_t)(L.row0 + pn.row0 + r) * L.ld + L.col0 + c0 + c;
-                v = load_dt(g, off, dt);
-                const float pd = round_dt(fmul(load_dt(pp, off, dt), wdm), dt);
-                psq = fmaf(pd, pd, psq);
-            }
-            Gs[c][r] = v;
-        }
-        for (int e = tid; e < TKK * KP; e += NT) {
-            const int c = e / KP, b = e % KP;
-            Us[c][b] = (c0 + c < L.b && b < kp) ? Ur[(int64_t)(c0 + c) * L.sr + b] : 0.f;
-        }
-        __syncthreads();
-#pragma unroll
-        for (int c = 0; c < TKK; ++c) {
-            float4 a = *(const float4*)&Gs[c][ty * 4];
-            float av[4] = {a.x, a.y, a.z, a.w};
-            float bv[CPT];
-#pragma unroll
-            for (int q = 0; q < CPT; q += 4) {
-                float4 b = *(const float4*)&Us[c][tx * CPT + q];
-                bv[q] = b.x; bv[q + 1] = b.y; bv[q + 2] = b.z; bv[q + 3] = b.w;
-            }
-#pragma unroll
-            for (int r = 0; r < 4; ++r)
-#pragma unroll
-                for (int q = 0; q < CPT; ++q) acc[r][q] = fmaf(av[r], bv[q], acc[r][q]);
-        }
-        __syncthreads();
-    }
-    // second stage: P_part[a][b] = sum_r U_l[row0+r][a] * T[r][b]
-#pragma unroll
-    for (int r = 0; r < 4; ++r)
-#pragma unroll
-        for (int q = 0; q < CPT; ++q) Ts[ty * 4 + r][tx * CPT + q] = acc[r][q];
-    for (int e = tid; e < TT * KP; e += NT) {
-        const int r = e / KP, a = e % KP;
-        Ls[r][a] = (r < pn.nrows && a < kp) ? Ul[(int64_t)(pn.row0 + r) * L.sl + a] : 0.f;
-    }
-    __syncthreads();
-    float* out = P.p_part + (int64_t)blockIdx.x * P.p_stride;
-    for (int e = tid; e < kp * kp; e += NT) {
-        const int a = e / kp, b = e % kp;
-        float s = 0.f;
-        for (int r = 0; r < pn.nrows; ++r) s = fmaf(Ls[r][a], Ts[r][b], s);
-        out[e] = s;
-    }
-    psq = block_sum(psq, red);
-    if (tid == 0) out[P.p_stride - 4] = psq;
-}
 
 // ---------------------------------------------------------------------------
 // diagonal-mode Phase-2 params: natural-norm^2 and p_dec^2 per chunk
@@ -331,109 +248,10 @@ __device__ __forceinline__ float adan_elem(const ScaoParamStep& S, int dt, float
 }
 
 // ---------------------------------------------------------------------------
-// Kronecker Phase-2 tiles
-// ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(NT)
-apply_kron_kernel(ScaoPlanDev P) {
-    const ScaoTile tl = P.tiles[blockIdx.x];
-    const ScaoLeaf& L = P.leaves[tl.leaf];
-    const ScaoParamStep& S = P.step[L.param];
-    if (S.phase != 2) return;
-    const ScaoParam& pr = P.params[L.param];
-    const int dt = pr.dtype;
-    const int kp = L.kpad;
-    extern __shared__ float sm[];
-    float* Ws = sm;                       // kp x (TT+4): Ws[b][i]
-    float* Us = Ws + kp * (TT + 4);       // kp x (TT+4): Us[b][j]
-    __shared__ float red[32];
-    const float* W = P.w + L.w_off;
-    const float* Ur = P.u + L.ur_off;
-    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
-    for (int e = tid; e < TT * kp; e += NT) {
-        const int r = e / kp, b = e % kp;
-        const int i = tl.row0 + r, j = tl.col0 + r;
-        Ws[b * (TT + 4) + r] = i < L.a ? W[(int64_t)i * kp + b] : 0.f;
-        Us[b * (TT + 4) + r] = j < L.b ? Ur[(int64_t)j * L.sr + b] : 0.f;
-    }
-    __syncthreads();
-    float acc[4][4] = {};
-    for (int b = 0; b < kp; ++b) {
-        const float4 a = *(const float4*)&Ws[b * (TT + 4) + ty * 4];
-        const float4 u = *(const float4*)&Us[b * (TT + 4) + tx * 4];
-        const float av[4] = {a.x, a.y, a.z, a.w}, uv[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-        for (int r = 0; r < 4; ++r)
-#pragma unroll
-            for (int c = 0; c < 4; ++c) acc[r][c] = fmaf(av[r], uv[c], acc[r][c]);
-    }
-    const float* ps = P.param_scalars + L.param * 8;
-    const bool clip = ps[PS_CLIP] != 0.f;
-    const float clipmul = ps[PS_CLIPMUL];
-    const void* g = (const void*)S.g_ptr;
-    float* M = P.exp_avg + pr.offset;
-    float* V = P.exp_avg_sq + pr.offset;
-    float* Dd = P.exp_avg_diff + pr.offset;
-    float* Pv = P.prev_grad + pr.offset;
-    float usq = 0.f, gsq = 0.f;
-    const bool vec = ((L.ld & 3) == 0) && ((L.col0 & 3) == 0) &&
-                     ((S.g_ptr & 15) == 0) && ((pr.offset & 3) == 0);
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-        const int i = tl.row0 + ty * 4 + r;
-        const int j0 = tl.col0 + tx * 4;
-        if (i >= L.a) continue;
-        const int64_t off = (int64_t)(L.row0 + i) * L.ld + L.col0 + j0;
-        if (vec && j0 + 3 < L.b) {
-            const float4 gg = load4_dt(g, off, dt);
-            float4 m4 = ldg_stream4(M + off), v4 = ldg_stream4(V + off);
-            float4 d4 = ldg_stream4(Dd + off), p4 = ldg_stream4(Pv + off);
-            float gv[4] = {gg.x, gg.y, gg.z, gg.w};
-            float mv[4] = {m4.x, m4.y, m4.z, m4.w}, vv[4] = {v4.x, v4.y, v4.z, v4.w};
-            float dv[4] = {d4.x, d4.y, d4.z, d4.w}, pv[4] = {p4.x, p4.y, p4.z, p4.w};
-            float uo[4];
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                const float gp = round_dt(fadd(gv[c], acc[r][c]), dt);
-                const float u = adan_elem(S, dt, gv[c], gp, mv[c], vv[c], dv[c], pv[c], clip, clipmul);
-                usq = fmaf(u, u, usq);
-                gsq = fmaf(gv[c], gv[c], gsq);
-                uo[c] = round_dt(u, dt);
-            }
-            stg_stream4(M + off, make_float4(mv[0], mv[1], mv[2], mv[3]));
-            stg_stream4(V + off, make_float4(vv[0], vv[1], vv[2], vv[3]));
-            stg_stream4(Dd + off, make_float4(dv[0], dv[1], dv[2], dv[3]));
-            stg_stream4(Pv + off, make_float4(pv[0], pv[1], pv[2], pv[3]));
-            if (dt == SCAO_F32) store4_dt(P.upd32 + pr.offset, off, dt, make_float4(uo[0], uo[1], uo[2], uo[3]));
-            else store4_dt(P.upd + pr.offset, off, dt, make_float4(uo[0], uo[1], uo[2], uo[3]));
-        } else {
-            for (int c = 0; c < 4; ++c) {
-                const int j = j0 + c;
-                if (j >= L.b) break;
-                const int64_t o = off + c;
-                const float gv = load_dt(g, o, dt);
-                float mv = M[o], vv = V[o], dv = Dd[o], pv = Pv[o];
-                const float gp = round_dt(fadd(gv, acc[r][c]), dt);
-                const float u = adan_elem(S, dt, gv, gp, mv, vv, dv, pv, clip, clipmul);
-                usq = fmaf(u, u, usq);
-                gsq = fmaf(gv, gv, gsq);
-                M[o] = mv; V[o] = vv; Dd[o] = dv; Pv[o] = pv;
-                if (dt == SCAO_F32) P.upd32[pr.offset + o] = u;
-                else store_dt(P.upd + pr.offset, o, dt, u);
-            }
-        }
-    }
-    usq = block_sum(usq, red);
-    gsq = block_sum(gsq, red);
-    if (tid == 0) {
-        P.tile_part[blockIdx.x * 4 + 0] = usq;
-        P.tile_part[blockIdx.x * 4 + 1] = gsq;
-    }
-}
-
-// ---------------------------------------------------------------------------
 // flat chunks: Phase-1 Adam (optimizer.py:561-578) and Phase-2 diagonal
 // params (preconditioner.py:506-510 + the Adan step)
 // ---------------------------------------------------------------------------
+template <bool FN>
 __global__ void __launch_bounds__(NT)
 apply_flat_kernel(ScaoPlanDev P) {
     const int cid = P.flat_list[blockIdx.x];
@@ -451,15 +269,25 @@ apply_flat_kernel(ScaoPlanDev P) {
     float* Dd = P.exp_avg_diff + pr.offset;
     float* Pv = P.prev_grad + pr.offset;
     float usq = 0.f, gsq = 0.f;
+    const ScaoFilterDev& FD = P.filt;
+    const float* MG = FD.mode ? FD.mag_ema + pr.offset : nullptr;
+    const float thr = FD.mode ? FD.fp[ch.param].thr : 0.f;
+    constexpr bool fl = FN;
+    // filtered / noised gradient of element e (optimizer.py:536-545)
+    auto gfilt = [&](float g_, int64_t e) {
+        return filt_grad(FD, g_, FD.mode ? MG[e] : 0.f, thr,
+                         FD.noise_on ? f4_get(noise_normal4(FD.noise_seed, ch.param, FD.noise_step,
+                                                            e >> 2), (int)(e & 3)) : 0.f);
+    };
     if (phase == 1) {
         const float a1 = round_dt((float)S.alpha1, dt);
-        auto adam4 = [&](float g_, float p_, float& m_, float& v_) {
+        auto adam4 = [&](float graw, float g_, float p_, float& m_, float& v_) {
             const float pd = round_dt(fmul(p_, S.wd_mult), dt);
             m_ = fmaf(g_, S.c1, fmul(m_, S.beta1));
             v_ = fmaf(fmul(S.c2, g_), g_, fmul(v_, S.beta2));
             const float den = fadd(fdiv(sqrtf(v_), S.sqrt_bc2), S.eps);
             const float u = round_dt(fdiv(m_, den), dt);
-            gsq = fmaf(g_, g_, gsq);
+            gsq = fmaf(graw, graw, gsq);
             return round_dt(fmaf(a1, u, pd), dt);
         };
         const bool vec = ((S.g_ptr & 15) == 0) && ((S.p_ptr & 15) == 0) &&
@@ -472,19 +300,30 @@ apply_flat_kernel(ScaoPlanDev P) {
                 const int64_t e = ch.begin + q * 4;
                 const float4 g4 = load4_dt(g, e, dt), p4 = load4_dt(pp, e, dt);
                 float4 m4 = ldg_stream4(M + e), v4 = ldg_stream4(V + e);
+                float4 f4 = g4;
+                if (fl) {
+                    const float4 mg4 = FD.mode ? *(const float4*)(MG + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    const float4 z4 = FD.noise_on ? noise_normal4(FD.noise_seed, ch.param, FD.noise_step, e >> 2)
+                                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+                    f4.x = filt_grad(FD, g4.x, mg4.x, thr, z4.x);
+                    f4.y = filt_grad(FD, g4.y, mg4.y, thr, z4.y);
+                    f4.z = filt_grad(FD, g4.z, mg4.z, thr, z4.z);
+                    f4.w = filt_grad(FD, g4.w, mg4.w, thr, z4.w);
+                }
                 float4 o;
-                o.x = adam4(g4.x, p4.x, m4.x, v4.x);
-                o.y = adam4(g4.y, p4.y, m4.y, v4.y);
-                o.z = adam4(g4.z, p4.z, m4.z, v4.z);
-                o.w = adam4(g4.w, p4.w, m4.w, v4.w);
+                o.x = adam4(g4.x, f4.x, p4.x, m4.x, v4.x);
+                o.y = adam4(g4.y, f4.y, p4.y, m4.y, v4.y);
+                o.z = adam4(g4.z, f4.z, p4.z, m4.z, v4.z);
+                o.w = adam4(g4.w, f4.w, p4.w, m4.w, v4.w);
                 store4_dt(pp, e, dt, o);
                 stg_stream4(M + e, m4);
                 stg_stream4(V + e, v4);
-                stg_stream4(Pv + e, g4);
+                stg_stream4(Pv + e, f4);
             }
         }
         for (int64_t e = vend + threadIdx.x; e < ch.end; e += NT) {
-            const float gv = load_dt(g, e, dt);
+            const float graw = load_dt(g, e, dt);
+            const float gv = fl ? gfilt(graw, e) : graw;
             const float pd = round_dt(fmul(load_dt(pp, e, dt), S.wd_mult), dt);
             float m = fmaf(gv, S.c1, fmul(M[e], S.beta1));
             float v = fmaf(fmul(S.c2, gv), gv, fmul(V[e], S.beta2));
@@ -492,7 +331,7 @@ apply_flat_kernel(ScaoPlanDev P) {
             const float u = round_dt(fdiv(m, den), dt);
             store_dt(pp, e, dt, round_dt(fmaf(a1, u, pd), dt));
             M[e] = m; V[e] = v; Pv[e] = gv;
-            gsq = fmaf(gv, gv, gsq);
+            gsq = fmaf(graw, graw, gsq);
         }
     } else {
         // Phase 2, diagonal mode
@@ -505,7 +344,7 @@ apply_flat_kernel(ScaoPlanDev P) {
             const float den = fadd(powf(fdiv(de[e], S.diag_bias), 0.25f), 1e-8f);
             const float gp = round_dt(fdiv(gv, den), dt);
             float m = M[e], v = V[e], d = Dd[e], pv = Pv[e];
-            const float u = adan_elem(S, dt, gv, gp, m, v, d, pv, clip, clipmul);
+            const float u = adan_elem(S, dt, fl ? gfilt(gv, e) : gv, gp, m, v, d, pv, clip, clipmul);
             usq = fmaf(u, u, usq);
             gsq = fmaf(gv, gv, gsq);
             M[e] = m; V[e] = v; Dd[e] = d; Pv[e] = pv;
@@ -570,25 +409,29 @@ param_post_kernel(ScaoPlanDev P) {
     ps[PS_ALPHA] = round_dt((float)(-(S.lr * trust)), dt);
 }
 
-// global grad-norm EMA (optimizer.py:439-446): mean of fp32 per-param norms
+// global grad-norm EMA (optimizer.py:439-446): mean of the fp32 per-param
+// norms, summed in parameter order like Python's sum, then the EMA in
+// double without contraction.
 __global__ void global_norm_kernel(ScaoPlanDev P) {
-    __shared__ double red[32];
-    double s = 0.0, c = 0.0;
-    for (int pi = threadIdx.x; pi < P.n_params; pi += blockDim.x) {
-        if (P.step[pi].phase == 0) continue;
-        s += (double)sqrtf(P.param_scalars[pi * 8 + PS_GNORM2]);
-        c += 1.0;
+    __shared__ float nrm[1024];
+    __shared__ int live[1024];
+    double s = 0.0;
+    int c = 0;
+    for (int p0 = 0; p0 < P.n_params; p0 += 1024) {
+        const int m = min(1024, P.n_params - p0);
+        for (int i = threadIdx.x; i < m; i += blockDim.x) {
+            live[i] = P.step[p0 + i].phase != 0;
+            nrm[i] = sqrtf(P.param_scalars[(p0 + i) * 8 + PS_GNORM2]);
+        }
+        __syncthreads();
+        if (threadIdx.x == 0)
+            for (int i = 0; i < m; ++i)
+                if (live[i]) { s = __dadd_rn(s, (double)nrm[i]); ++c; }
+        __syncthreads();
     }
-    s = warp_sum_d(s);
-    c = warp_sum_d(c);
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    if (lane == 0) { red[wid] = s; red[16 + wid] = c; }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        double ts = 0.0, tc = 0.0;
-        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) { ts += red[w]; tc += red[16 + w]; }
-        if (tc > 0.0) *P.global_norm_ema = 0.95 * (*P.global_norm_ema) + 0.05 * (ts / tc);
-    }
+    if (threadIdx.x == 0 && c > 0)
+        *P.global_norm_ema = __dadd_rn(__dmul_rn(0.95, *P.global_norm_ema),
+                                       __dmul_rn(0.05, s / (double)c));
 }
 
 // Phase-2 parameter write: p = round(round(p*(1-lr wd)) + alpha*u)
@@ -802,6 +645,9 @@ __device__ __forceinline__ void apply_prefetch_row(const ScaoPlanDev& P, const S
 #ifndef SCAO_APPLY_MINB
 #define SCAO_APPLY_MINB 3
 #endif
+// FN: the gradient filter or noise is on this step (a separate
+// instantiation keeps the plain epilogue's register budget).
+template <bool FN>
 __global__ void __launch_bounds__(SCAO_APPLY_NT, SCAO_APPLY_MINB)
 apply_kron_tc_kernel(ScaoPlanDev P, int* err) {
     const ScaoTile tl = P.tiles[blockIdx.x];
@@ -885,6 +731,9 @@ apply_kron_tc_kernel(ScaoPlanDev P, int* err) {
     float* Dd = P.exp_avg_diff + pr.offset;
     float* Pv = P.prev_grad + pr.offset;
     const float wdm = S.wd_mult;
+    const ScaoFilterDev& FD = P.filt;
+    const float* MG = FD.mag_ema + pr.offset;
+    const float thr = FD.mode ? FD.fp[L.param].thr : 0.f;
     const int cg = (tid & 31) * 4;          // 4 columns
     const int jcol = j0 + cg;
     const bool vec = ((L.ld & 3) == 0) && ((L.col0 & 3) == 0) && ((S.g_ptr & 15) == 0) &&
@@ -904,6 +753,15 @@ apply_kron_tc_kernel(ScaoPlanDev P, int* err) {
             float gv[4] = {gg.x, gg.y, gg.z, gg.w}, pv[4] = {p4.x, p4.y, p4.z, p4.w};
             float mv[4] = {m4.x, m4.y, m4.z, m4.w}, vv[4] = {v4.x, v4.y, v4.z, v4.w};
             float dv[4] = {d4.x, d4.y, d4.z, d4.w}, qv[4] = {q4.x, q4.y, q4.z, q4.w};
+            float gf[4] = {gv[0], gv[1], gv[2], gv[3]};
+            if (FN) {
+                const float4 mg4 = FD.mode ? *(const float4*)(MG + o) : make_float4(0.f, 0.f, 0.f, 0.f);
+                const float4 z4 = FD.noise_on ? noise_normal4(FD.noise_seed, L.param, FD.noise_step, o >> 2)
+                                              : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    gf[c] = filt_grad(FD, gv[c], f4_get(mg4, c), thr, f4_get(z4, c));
+            }
             float uo[4];
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
@@ -912,7 +770,7 @@ apply_kron_tc_kernel(ScaoPlanDev P, int* err) {
                 mv[c] += gp; vv[c] += gp * gp; dv[c] -= gp; qv[c] = gv[c];
                 const float u = mv[c];
 #else
-                const float u = adan_elem(S, dt, gv[c], gp, mv[c], vv[c], dv[c], qv[c], clip, clipmul);
+                const float u = adan_elem(S, dt, gf[c], gp, mv[c], vv[c], dv[c], qv[c], clip, clipmul);
 #endif
                 usq = fmaf(u, u, usq);
                 gsq = fmaf(gv[c], gv[c], gsq);
@@ -933,7 +791,13 @@ apply_kron_tc_kernel(ScaoPlanDev P, int* err) {
                 const float gv = load_dt(g, oc, dt);
                 float mv = M[oc], vv = V[oc], dv = Dd[oc], qv = Pv[oc];
                 const float gp = round_dt(fadd(gv, crv[c]), dt);
-                const float u = adan_elem(S, dt, gv, gp, mv, vv, dv, qv, clip, clipmul);
+                float gf = gv;
+                if (FN)
+                    gf = filt_grad(FD, gv, FD.mode ? MG[oc] : 0.f, thr,
+                                   FD.noise_on ? f4_get(noise_normal4(FD.noise_seed, L.param,
+                                                                      FD.noise_step, oc >> 2), (int)(oc & 3))
+                                               : 0.f);
+                const float u = adan_elem(S, dt, gf, gp, mv, vv, dv, qv, clip, clipmul);
                 usq = fmaf(u, u, usq);
                 gsq = fmaf(gv, gv, gsq);
                 const float pd = round_dt(fmul(load_dt(pp, oc, dt), wdm), dt);
@@ -1148,7 +1012,6 @@ proj_tc_kernel(ScaoPlanDev P, int* err) {
     const uint32_t sbytes = 2 * abytes + 2 * bbytes;   // [A hi][A lo][B hi][B lo]
     __shared__ uint64_t mbar_b[2], mbar_m[2];
     __shared__ uint32_t tslot;
-    __shared__ float red[32];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const void* g = (const void*)S.g_ptr;
     const void* pp = (const void*)S.p_ptr;
@@ -1267,28 +1130,34 @@ size_t proj_tc_smem(int kpad) {
     return 2 * stage > epi ? 2 * stage : epi;
 }
 
-size_t proj_smem(int kp) {
-    return (size_t)(16 * (TT + 4) + (16 + 2 * TT) * (kp + 4)) * 4;
-}
-
 }  // namespace
 
 extern "C" int scao_plan_step(const ScaoPlanDev* P, void* stream) {
     if (!P || P->kpad_max > 128 || P->kpad_max < 0) return SCAO_ERR_ARG;
     cudaStream_t st = (cudaStream_t)stream;
+    // the gradient filter also folds the global grad-norm EMA (its R2 form
+    // reads it before the moments are updated)
+    {
+        const int rc = scao_filter_run(P, st);
+        if (rc != SCAO_OK) return rc;
+    }
+    const bool fn = P->filt.mode != 0 || P->filt.noise_on != 0;
     if (P->n_panels > 0) {
         static bool pattr = false;
         if (!pattr) {
             cudaFuncSetAttribute(proj_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)proj_tc_smem(128));
-            cudaFuncSetAttribute(apply_kron_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            cudaFuncSetAttribute(apply_kron_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)apply_tc_smem(128));
+            cudaFuncSetAttribute(apply_kron_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)apply_tc_smem(128));
+            cudaFuncSetAttribute(apply_kron_tc_kernel<true>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
             cudaFuncSetAttribute(proj_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)proj_bf16_smem(128));
             // full shared-memory carveout so several CTAs fit per SM
             cudaFuncSetAttribute(proj_bf16_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
             cudaFuncSetAttribute(proj_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-            cudaFuncSetAttribute(apply_kron_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+            cudaFuncSetAttribute(apply_kron_tc_kernel<false>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
             pattr = true;
         }
         { ProfScope _ps(SLOT_PROJ, st);
@@ -1308,8 +1177,6 @@ extern "C" int scao_plan_step(const ScaoPlanDev* P, void* stream) {
         if (!attr) {
             cudaFuncSetAttribute(leaf_coef_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (128 * 128 + 4 * 128) * 4);
-            cudaFuncSetAttribute(apply_kron_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 2 * 128 * (TT + 4) * 4);
             attr = true;
         }
         { ProfScope _ps(SLOT_LEAF_COEF, st); leaf_coef_kernel<<<P->n_leaves, NT, sm, st>>>(*P); }
@@ -1331,17 +1198,24 @@ extern "C" int scao_plan_step(const ScaoPlanDev* P, void* stream) {
     SCAO_CHECK_LAUNCH();
     if (P->n_tiles > 0) {
         { ProfScope _ps(SLOT_APPLY_KRON, st);
-          apply_kron_tc_kernel<<<P->n_tiles, SCAO_APPLY_NT, apply_tc_smem(P->kpad_max), st>>>(*P, P->err); }
+          if (fn) apply_kron_tc_kernel<true><<<P->n_tiles, SCAO_APPLY_NT, apply_tc_smem(P->kpad_max), st>>>(*P, P->err);
+          else apply_kron_tc_kernel<false><<<P->n_tiles, SCAO_APPLY_NT, apply_tc_smem(P->kpad_max), st>>>(*P, P->err); }
         SCAO_CHECK_LAUNCH();
     }
     if (P->n_chunks > 0) {
-        if (P->n_flat > 0) { ProfScope _ps(SLOT_APPLY_FLAT, st); apply_flat_kernel<<<P->n_flat, NT, 0, st>>>(*P); }
+        if (P->n_flat > 0) {
+            ProfScope _ps(SLOT_APPLY_FLAT, st);
+            if (fn) apply_flat_kernel<true><<<P->n_flat, NT, 0, st>>>(*P);
+            else apply_flat_kernel<false><<<P->n_flat, NT, 0, st>>>(*P);
+        }
         SCAO_CHECK_LAUNCH();
     }
     { ProfScope _ps(SLOT_PARAM_POST, st); param_post_kernel<<<P->n_params, NT, 0, st>>>(*P); }
     SCAO_CHECK_LAUNCH();
-    { ProfScope _ps(SLOT_GLOBAL_NORM, st); global_norm_kernel<<<1, 512, 0, st>>>(*P); }
-    SCAO_CHECK_LAUNCH();
+    if (P->filt.mode == 0) {
+        { ProfScope _ps(SLOT_GLOBAL_NORM, st); global_norm_kernel<<<1, 256, 0, st>>>(*P); }
+        SCAO_CHECK_LAUNCH();
+    }
     if (P->n_chunks > 0) {
         if (P->n_p > 0) { ProfScope _ps(SLOT_APPLY_P, st); apply_p_kernel<<<P->n_p, NT, 0, st>>>(*P); }
         SCAO_CHECK_LAUNCH();

@@ -9,6 +9,9 @@
 
 #define SCAO_DEV __device__ __forceinline__
 
+// per-parameter scalar slots of ScaoPlanDev::param_scalars (8 floats each)
+enum { PS_CLIPMUL = 0, PS_CLIP, PS_PNORM2, PS_UNORM2, PS_GNORM2, PS_ALPHA, PS_NAT, PS_TRUST };
+
 // ---------------------------------------------------------------------------
 // parameter-dtype load / round / store.  All arithmetic is fp32 ("opmath"),
 // values are rounded to the parameter dtype where the reference stores a

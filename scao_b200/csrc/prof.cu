@@ -11,7 +11,7 @@ const char* kNames[SLOT_COUNT] = {
     "proj", "diag_pre", "leaf_coef", "param_pre", "apply_kron", "apply_flat", "param_post",
     "global_norm", "apply_p", "lookahead", "gram_ema", "requant", "diag_ema", "eig_prep",
     "eig_diag", "eig_gemm", "eig_jacobi", "eig_residual", "eig_cholinv", "eig_rank", "quant",
-    "seam", "gram_tc", "transpose"};
+    "seam", "gram_tc", "transpose", "filter"};
 
 std::atomic<int64_t> g_launches{0};
 std::atomic<int> g_enabled{0};

@@ -12,7 +12,7 @@ enum ScaoSlot {
     SLOT_APPLY_FLAT, SLOT_PARAM_POST, SLOT_GLOBAL_NORM, SLOT_APPLY_P, SLOT_LOOKAHEAD,
     SLOT_GRAM_EMA, SLOT_REQUANT, SLOT_DIAG_EMA, SLOT_EIG_PREP, SLOT_EIG_DIAG,
     SLOT_EIG_GEMM, SLOT_EIG_JACOBI, SLOT_EIG_RESIDUAL, SLOT_EIG_CHOLINV, SLOT_EIG_RANK,
-    SLOT_QUANT, SLOT_SEAM, SLOT_GRAM_TC, SLOT_TRANSPOSE, SLOT_COUNT
+    SLOT_QUANT, SLOT_SEAM, SLOT_GRAM_TC, SLOT_TRANSPOSE, SLOT_FILTER, SLOT_COUNT
 };
 
 void scao_prof_begin(int slot, cudaStream_t st);

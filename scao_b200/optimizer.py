@@ -22,10 +22,6 @@ from . import _lib
 from .plan import Plan
 from .preconditioner import PrecondView
 
-_UNSUPPORTED = {
-    "dynamic_sparsity": False, "adaptive_warmup": False, "lazy_precond": False,
-    "use_gsnr_clip": False, "adaptive_rank": False,
-}
 
 
 class SCAO(Optimizer):
@@ -99,9 +95,9 @@ class SCAO(Optimizer):
         self._lookahead_alpha = lookahead_alpha
         self._lookahead_init = False
         self._sparsity = sparsity
-        self._opts = dict(dynamic_sparsity=dynamic_sparsity, adaptive_warmup=adaptive_warmup,
-                          lazy_precond=lazy_precond, use_gsnr_clip=use_gsnr_clip,
-                          adaptive_rank=adaptive_rank)
+        self._dynamic_sparsity = bool(dynamic_sparsity)
+        self._opts = dict(adaptive_warmup=adaptive_warmup, lazy_precond=lazy_precond,
+                          use_gsnr_clip=use_gsnr_clip, adaptive_rank=adaptive_rank)
         self._warmup_cfg = (warmup_steps, warmup_stability_threshold, warmup_patience)
         self._in_warmup_global = True
         self._eig_max_iters = int(eig_max_iters)
@@ -136,6 +132,13 @@ class SCAO(Optimizer):
         _lib.lib()
         with torch.cuda.device(dev):
             self._plan = Plan(ps, gs, dev, int8.pop())
+            if self._sparsity > 0.0:
+                self._plan.setup_filter(2 if self._dynamic_sparsity else 1, self._sparsity)
+        # noise stream key: the device generator's seed (consumes no draws)
+        gen = torch.cuda.default_generators[dev.index if dev.index is not None
+                                            else torch.cuda.current_device()]
+        self._plan.dev.filt.noise_seed = (int(gen.initial_seed()) * 0x9E3779B97F4A7C15 + 1) \
+            & 0xFFFFFFFFFFFFFFFF
         for i, (p, g) in enumerate(zip(ps, gs)):
             st = self.state[p]
             st["step"] = 0
@@ -147,14 +150,6 @@ class SCAO(Optimizer):
             st["preconditioner"] = PrecondView(self._plan, i, g)
 
     def _check_supported(self):
-        if self._sparsity > 0.0:
-            raise NotImplementedError(
-                "scao_b200: sparsity > 0 (the magnitude-EMA quantile mask, optimizer.py:42-57) "
-                "is not implemented on the device yet; pass sparsity=0")
-        if self._noise_std > 1e-9:
-            raise NotImplementedError(
-                "scao_b200: gradient noise (noise_std_init > 0, optimizer.py:544-545) is not "
-                "implemented on the device yet; pass noise_std_init=0")
         for k, v in self._opts.items():
             if v:
                 raise NotImplementedError(f"scao_b200: {k}=True is not implemented yet")
@@ -289,6 +284,10 @@ class SCAO(Optimizer):
             self._last_eig_status = status
             keep.append(ids)
         plan.set_phases(np.array(tab["phase"], dtype=np.int32))
+        f = plan.dev.filt
+        f.noise_on = 1 if self._noise_std > 1e-9 else 0     # optimizer.py:544
+        f.noise_std = float(np.float32(self._noise_std))
+        f.noise_step = self._global_step
         _lib.check(L.scao_plan_step(pd, sp), "scao_plan_step")
         self._noise_std *= self._noise_anneal
         if self._lookahead_k > 0 and self._global_step % self._lookahead_k == 0:

@@ -19,6 +19,7 @@ from ._lib import CHUNK_DT, LEAF_DT, PANEL_DT, PARAM_DT, STEP_DT, TILE_DT
 TILE = 128       # apply tile edge (apply.cu TC_T)
 PANEL = 128      # projection panel rows
 CHUNK = 4096     # flat chunk length
+SEL = 65536      # elements per chunk of the gradient filter's selection passes
 SMAX = 160       # largest eigen subspace width (eig.cu SMAX)
 
 DTYPE_CODE = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16, torch.float16: _lib.F16}
@@ -326,6 +327,44 @@ class Plan:
             self.t_p_list[:len(pl)].copy_(torch.from_numpy(pl))
         self.dev.n_flat = len(flat)
         self.dev.n_p = len(pl)
+
+    def setup_filter(self, mode, sparsity, ema=0.99):
+        """Device state of the sparse gradient filter (optimizer.py:40-97):
+        magnitude-EMA arena, selection chunks of <= SEL elements per param,
+        per-param radix-selection state.  ``mode`` 1 static, 2 dynamic (R2)."""
+        f = self.dev.filt
+        if f.mode:
+            return
+        sel = []
+        fp = np.zeros(self.n_params, _lib.FILTER_PARAM_DT)
+        for i in range(self.n_params):
+            n = int(self.ptab[i]["numel"])
+            fp[i]["sel_begin"] = len(sel)
+            for c0 in range(0, n, SEL):
+                sel.append((i, 0, c0, min(n, c0 + SEL)))
+            fp[i]["sel_end"] = len(sel)
+        fp["norm_ema"] = 1.0
+        fp["global_ref"] = 1.0
+        fp["first"] = 1
+        dev = self.device
+        self.t_sel = self._dev(np.array(sel, CHUNK_DT))
+        self.t_fp = self._dev(fp)
+        self.mag_ema = torch.zeros(max(self.numel_total, 1), dtype=torch.float32, device=dev)
+        self.filt_hist = torch.zeros(self.n_params * 2 * 4096, dtype=torch.int32, device=dev)
+        self.sel_part = torch.zeros(max(len(sel), 1), dtype=torch.float32, device=dev)
+        f.mode = int(mode)
+        f.n_sel = len(sel)
+        f.sel, f.mag_ema, f.fp = self.t_sel.data_ptr(), self.mag_ema.data_ptr(), self.t_fp.data_ptr()
+        f.hist, f.sel_part = self.filt_hist.data_ptr(), self.sel_part.data_ptr()
+        f.base, f.min_s, f.max_s, f.norm_coeff = float(sparsity), 0.3, 0.9, 0.95
+        f.ema = float(np.float32(ema))
+        f.ema_c = float(np.float32(1.0 - ema))
+
+    def filter_params(self):
+        """Per-parameter filter state (numpy copy; synchronises)."""
+        if not self.dev.filt.mode:
+            return None
+        return self.t_fp.cpu().numpy().view(_lib.FILTER_PARAM_DT)
 
     def check_error(self):
         """Raise if a kernel recorded a timed-out wait (synchronises)."""

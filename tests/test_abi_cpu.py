@@ -42,3 +42,49 @@ def test_host_only_queries():
     assert L.scao_fused_precond_scratch_bytes(64, 48, 8) > 0
     assert L.scao_int8_ema_update_noalloc_max_n() == 1 << 20
     assert b"sm_100a" in L.scao_version()
+
+
+def test_struct_layouts_match_header(tmp_path):
+    """Compile a probe against include/scao_b200.h with the host C compiler
+    and compare every struct size and the PlanDev / FilterDev field offsets
+    with the ctypes / numpy mirrors."""
+    import shutil
+    import subprocess
+    import numpy as np
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        import pytest
+        pytest.skip("no host C compiler")
+    fields_plan = [f for f, _ in _lib.PlanDev._fields_]
+    fields_filt = [f for f, _ in _lib.FilterDev._fields_]
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "scao_b200.h"',
+             'int main(void) {']
+    for t in ("ScaoParam", "ScaoParamStep", "ScaoLeaf", "ScaoChunk", "ScaoFilterParam",
+              "ScaoFilterDev", "ScaoPlanDev"):
+        lines.append(f'printf("size {t} %zu\\n", sizeof({t}));')
+    for f in fields_plan:
+        lines.append(f'printf("plan {f} %zu\\n", offsetof(ScaoPlanDev, {f}));')
+    for f in fields_filt:
+        lines.append(f'printf("filt {f} %zu\\n", offsetof(ScaoFilterDev, {f}));')
+    for f in _lib.FILTER_PARAM_DT.names:
+        lines.append(f'printf("fparam {f} %zu\\n", offsetof(ScaoFilterParam, {f}));')
+    lines.append("return 0; }")
+    src = tmp_path / "probe.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "probe"
+    subprocess.check_call([cc, "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)])
+    out = subprocess.check_output([str(exe)]).decode().split("\n")
+    got = {tuple(l.split()[:2]): int(l.split()[2]) for l in out if l.strip()}
+    assert got[("size", "ScaoParam")] == _lib.PARAM_DT.itemsize
+    assert got[("size", "ScaoParamStep")] == _lib.STEP_DT.itemsize
+    assert got[("size", "ScaoLeaf")] == _lib.LEAF_DT.itemsize
+    assert got[("size", "ScaoChunk")] == _lib.CHUNK_DT.itemsize
+    assert got[("size", "ScaoFilterParam")] == _lib.FILTER_PARAM_DT.itemsize
+    assert got[("size", "ScaoFilterDev")] == ctypes.sizeof(_lib.FilterDev)
+    assert got[("size", "ScaoPlanDev")] == ctypes.sizeof(_lib.PlanDev)
+    for f in fields_plan:
+        assert got[("plan", f)] == getattr(_lib.PlanDev, f).offset, f
+    for f in fields_filt:
+        assert got[("filt", f)] == getattr(_lib.FilterDev, f).offset, f
+    for f in _lib.FILTER_PARAM_DT.names:
+        assert got[("fparam", f)] == _lib.FILTER_PARAM_DT.fields[f][1], f

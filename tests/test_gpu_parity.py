@@ -182,8 +182,11 @@ def test_optimizer_matches_reference_run(name):
                 assert rel_err(lf["L_ema"].cpu().numpy(), G[pre + "L"]) < 1e-5
             assert subspace_angle(lf["U_l"].cpu().numpy(), G[pre + "U_l"], G[pre + "S_l"]) < 1e-3
             assert subspace_angle(lf["U_r"].cpu().numpy(), G[pre + "U_r"], G[pre + "S_r"]) < 1e-3
-            assert rel_err(lf["S_l"].cpu().numpy(), G[pre + "S_l"]) < 1e-4
-            assert rel_err(lf["S_r"].cpu().numpy(), G[pre + "S_r"]) < 1e-4
+            # eigenvalues: 1e-4 on fp32 factors; an int8 factor carries its
+            # rare +-1 code flips (one code = absmax / 127) into them
+            stol = 1e-3 if "L_ema_q" in lf else 1e-4
+            assert rel_err(lf["S_l"].cpu().numpy(), G[pre + "S_l"]) < stol
+            assert rel_err(lf["S_r"].cpu().numpy(), G[pre + "S_r"]) < stol
 
 
 def test_bf16_degenerate_run_is_bit_exact():
