@@ -200,6 +200,8 @@ typedef struct {
     int32_t n_diag, n_flat, n_p, pad2_;
     int32_t* err;                /* device error flag: set to 1 when a bounded
                                     wait on the tensor core timed out       */
+    uint8_t* tmaps;              /* n_params x 2 TMA tensor maps (128 B each,
+                                    written by scao_plan_curvature)         */
     ScaoFilterDev filt;          /* gradient filter and noise (mode 0: off) */
 } ScaoPlanDev;
 
@@ -271,10 +273,15 @@ SCAO_API int scao_dequantize_sym_int8(const int8_t* q, double scale, int64_t n,
 /* Curvature EMA for the leaves listed in leaf_ids (device int32, n ids):
  * L <- rho*L + (1-rho) G G^T, R <- rho*R + (1-rho) G^T G
  * (preconditioner.py:341-353), int8 requant fused (utils.py:170-203).
- * scratch: scao_ema_scratch_bytes(...) bytes.                              */
+ * scratch: scao_ema_scratch_bytes(...) bytes.  params_host / step_host:
+ * host copies of the parameter and step tables (may be NULL); with them the
+ * bf16 factor GEMMs run on the TMA-fed persistent tensor-core kernel, whose
+ * per-gradient tensor maps are written to plan_host->tmaps.                 */
 SCAO_API int scao_plan_curvature(const ScaoPlanDev* plan_host, const int32_t* leaf_ids,
                         int n_ids, int max_a, int max_b, double rho,
-                        void* scratch, int64_t scratch_bytes, void* stream);
+                        void* scratch, int64_t scratch_bytes,
+                        const ScaoParam* params_host, const ScaoParamStep* step_host,
+                        void* stream);
 SCAO_API int64_t scao_ema_scratch_bytes(int n_ids, int max_a, int max_b);
 
 /* Diagonal-mode curvature EMA for the params in param_ids

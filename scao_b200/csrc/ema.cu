@@ -11,6 +11,11 @@
 // Only the lower triangle of tiles is computed; the epilogue mirrors it.
 // This file holds the portable SIMT-FMA tile kernel; see gram_tc.cu for the
 // tcgen05 tensor-core path used for 16-bit gradients.
+#include <cuda.h>
+#include <stdlib.h>
+#include <string.h>
+#include <vector>
+
 #include "common.cuh"
 #include "prof.cuh"
 #include "tc.cuh"
@@ -77,12 +82,20 @@ __device__ __forceinline__ bool gram_tc_ok(const Prob& p, const ScaoLeaf& L) {
            (L.b % 8) == 0 && ((reinterpret_cast<uintptr_t>(p.g) & 15) == 0);
 }
 
+// TMA path (gram_tma_kernel): whole 64-deep K blocks, 16-byte aligned rows
+__device__ __forceinline__ bool gram_tma_ok(const ScaoLeaf& L, int side, int dt) {
+    const int K = side ? L.a : L.b;
+    return dt == SCAO_BF16 && (K % 64) == 0 && (L.a % 64) == 0 && (L.b % 64) == 0 &&
+           (L.ld % 8) == 0 && (L.col0 % 8) == 0;
+}
+
 __global__ void __launch_bounds__(256, 2)
 gram_ema_tc_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, float* xbuf, int64_t xstride,
-                   float* amnew, float rho_f, float alpha_f, int* err) {
+                   float* amnew, float rho_f, float alpha_f, int* err, int tma_on) {
     const Prob p = get_prob(P, ids, blockIdx.y, xbuf, xstride, amnew);
     const ScaoLeaf& L = P.leaves[ids[blockIdx.y >> 1]];
     if (!gram_tc_ok(p, L)) return;
+    if (tma_on && gram_tma_ok(L, p.side, p.dt)) return;     // gram_tma_kernel
     const int nt = (p.n + GT - 1) / GT;
     const int t = blockIdx.x;
     if (t >= nt * (nt + 1) / 2) return;
@@ -259,6 +272,348 @@ size_t gram_tc_smem() {
     return st > cs ? st : cs;
 }
 
+// ---------------------------------------------------------------------------
+// Persistent, warp-specialised tensor-core gram + EMA (bf16 gradients whose
+// leaf block allows whole 64-deep K blocks).  Operands arrive by TMA tensor
+// copies (cp.async.bulk.tensor, 128-byte swizzle, no multicast) from one 2-D
+// tensor map per parameter gradient; the leaf block is selected by the copy
+// coordinates.  Roles per CTA (one CTA per SM, 192 threads):
+//   warp 0      TMA producer over a GST-stage shared-memory ring
+//   warp 1      TMEM owner and MMA issuer (one thread), 2 accumulators
+//   warps 2-5   epilogue: TMEM -> dequant*rho + alpha*gram -> fp32 staging
+// The epilogue of tile t overlaps the main loop of tile t+1 (double-buffered
+// TMEM accumulators).  L = G G^T uses K-major operands (gradient rows);
+// R = G^T G uses MN-major operands (gradient columns) -- no transpose.
+// Every wait is bounded; on a timeout the CTA records an error and stops.
+// ---------------------------------------------------------------------------
+constexpr int GN = 256;                 // output tile: 128 rows x GN columns
+constexpr int GST = 4;                  // pipeline stages
+constexpr uint32_t GOPB = 128 * 64 * 2; // one 128 x 64 operand block, 16 KB
+constexpr uint32_t GSTAGE = GOPB + (GN / 128) * GOPB;
+constexpr int GEPI = 256;                // epilogue threads (8 warps)
+constexpr int GTHREADS = 64 + GEPI;
+constexpr int GTRI = GT * GT;           // floats per staged 128 x 128 sub-tile
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* map, int x, int y,
+                                            uint64_t* mbar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3}], [%4];"
+        :: "r"(dst), "l"(map), "r"(x), "r"(y), "r"(smem_u32(mbar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* mbar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(smem_u32(mbar)) : "memory");
+}
+
+// 128-byte-swizzle shared-memory descriptor (layout type 2 in bits 61-63)
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    return smem_desc(saddr, lbo, sbo) | ((uint64_t)2 << 61);
+}
+
+// work tiles of one factor problem: row block ti (128 rows), column block
+// tc (GN columns) for every tc * GN <= 128 ti + 127 (lower triangle)
+__device__ __forceinline__ int gram_row_tiles(int ti) { return (128 * ti + 127) / GN + 1; }
+__host__ __device__ inline int gram_work_tiles(int n) {
+    const int nt = (n + 127) / 128;
+    int c = 0;
+    for (int ti = 0; ti < nt; ++ti) c += (128 * ti + 127) / GN + 1;
+    return c;
+}
+
+struct GTile {
+    int j, leaf, side, n, K, ti, tc, param;
+    int64_t row0, col0;
+};
+
+// decode work item T of the persistent loop; false when it is padding
+__device__ __forceinline__ bool gram_tile(const ScaoPlanDev& P, const int32_t* ids, int tpp,
+                                          int T, GTile& w) {
+    w.j = T / tpp;
+    int t = T - w.j * tpp;
+    w.leaf = ids[w.j >> 1];
+    w.side = w.j & 1;
+    const ScaoLeaf& L = P.leaves[w.leaf];
+    w.param = L.param;
+    if (!gram_tma_ok(L, w.side, P.params[L.param].dtype)) return false;
+    w.n = w.side ? L.b : L.a;
+    w.K = w.side ? L.a : L.b;
+    const int nt = (w.n + 127) / 128;
+    int ti = 0;
+    for (; ti < nt; ++ti) {
+        const int c = gram_row_tiles(ti);
+        if (t < c) break;
+        t -= c;
+    }
+    if (ti >= nt) return false;
+    w.ti = ti;
+    w.tc = t;
+    w.row0 = L.row0;
+    w.col0 = L.col0;
+    return true;
+}
+
+__global__ void __launch_bounds__(GTHREADS, 1)
+gram_tma_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, int nprob, int tpp,
+                float* xbuf, int64_t xstride, float* amnew, float rho_f, float alpha_f, int* err) {
+    extern __shared__ unsigned char gsm_raw[];
+    unsigned char* gsm = (unsigned char*)(((uintptr_t)gsm_raw + 1023) & ~(uintptr_t)1023);
+    __shared__ uint64_t full[GST], empty[GST], accf[2], acce[2], fin;
+    __shared__ uint32_t tslot;
+    __shared__ volatile int abort_flag;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {
+        for (int i = 0; i < GST; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
+        for (int i = 0; i < 2; ++i) { mbar_init(&accf[i], 1); mbar_init(&acce[i], GEPI); }
+        mbar_init(&fin, 1);
+        abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) tc_alloc(&tslot, 2 * GN);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tslot;
+    const int total = nprob * tpp;
+    const unsigned char* maps = P.tmaps;
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer ----------------
+            int stage = 0;
+            uint32_t ph = 0, issued = 0, last_ph = 0;
+            GTile w;
+            for (int T = blockIdx.x; T < total && !abort_flag; T += gridDim.x) {
+                if (!gram_tile(P, ids, tpp, T, w)) continue;
+                const void* map = maps + ((size_t)w.param * 2 + w.side) * 128;
+                const int i0 = w.ti * 128, j0 = w.tc * GN;
+                const int x0 = (int)w.col0, y0 = (int)w.row0;
+                for (int kb = 0; kb < w.K / 64; ++kb) {
+                    if (!mbar_wait(&empty[stage], ph ^ 1)) { abort_flag = 1; atomicExch(err, 2); break; }
+                    mbar_expect_tx(&full[stage], GSTAGE);
+                    const uint32_t a = smem_u32(gsm + (size_t)stage * GSTAGE), b = a + GOPB;
+                    const int k0 = kb * 64;
+                    if (w.side == 0) {
+                        // K-major: x = K (gradient column), y = output index (row)
+                        tma_load_2d(a, map, x0 + k0, y0 + i0, &full[stage]);
+#pragma unroll
+                        for (int h = 0; h < GN / 128; ++h)
+                            tma_load_2d(b + h * GOPB, map, x0 + k0, y0 + j0 + 128 * h, &full[stage]);
+                    } else {
+                        // MN-major: x = output index (gradient column), y = K (row)
+#pragma unroll
+                        for (int h = 0; h < 2; ++h)
+                            tma_load_2d(a + h * (GOPB / 2), map, x0 + i0 + 64 * h, y0 + k0, &full[stage]);
+#pragma unroll
+                        for (int h = 0; h < GN / 64; ++h)
+                            tma_load_2d(b + h * (GOPB / 2), map, x0 + j0 + 64 * h, y0 + k0, &full[stage]);
+                    }
+                    issued |= 1u << stage;
+                    last_ph = (last_ph & ~(1u << stage)) | (ph << stage);
+                    if (++stage == GST) { stage = 0; ph ^= 1; }
+                }
+            }
+            // no copy may still be landing when the CTA exits
+            for (int s2 = 0; s2 < GST; ++s2)
+                if ((issued >> s2) & 1u)
+                    if (!mbar_wait(&full[s2], (last_ph >> s2) & 1u)) atomicExch(err, 2);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer ----------------
+            int stage = 0, acc = 0;
+            uint32_t ph = 0, aph = 0;
+            GTile w;
+            for (int T = blockIdx.x; T < total && !abort_flag; T += gridDim.x) {
+                if (!gram_tile(P, ids, tpp, T, w)) continue;
+                if (!mbar_wait(&acce[acc], aph ^ 1)) { abort_flag = 1; atomicExch(err, 2); break; }
+                tc_fence_after();
+                const uint32_t d = tmem + acc * GN;
+                const uint32_t idesc = idesc_bf16(128, GN, w.side, w.side);
+                bool ok = true;
+                for (int kb = 0; kb < w.K / 64; ++kb) {
+                    if (!mbar_wait(&full[stage], ph)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a = smem_u32(gsm + (size_t)stage * GSTAGE), b = a + GOPB;
+#pragma unroll
+                    for (int s = 0; s < 4; ++s) {
+                        uint64_t ad, bd;
+                        if (w.side == 0) {          // K-major: 16 K = 32 bytes along the row
+                            ad = smem_desc_sw128(a + s * 32, 16, 1024);
+                            bd = smem_desc_sw128(b + s * 32, 16, 1024);
+                        } else {                    // MN-major: 16 K rows = 2 x 1024 bytes
+                            ad = smem_desc_sw128(a + s * 2048, GOPB / 2, 1024);
+                            bd = smem_desc_sw128(b + s * 2048, GOPB / 2, 1024);
+                        }
+                        tc_mma_bf16(d, ad, bd, idesc, (kb > 0 || s > 0) ? 1u : 0u);
+                    }
+                    tc_commit(&empty[stage]);
+                    if (++stage == GST) { stage = 0; ph ^= 1; }
+                }
+                if (!ok) { abort_flag = 1; atomicExch(err, 2); break; }
+                tc_commit(&accf[acc]);
+                acc ^= 1;
+                if (acc == 0) aph ^= 1;
+            }
+            // every issued MMA has completed before TMEM is released
+            tc_commit(&fin);
+            if (!mbar_wait(&fin, 0)) atomicExch(err, 2);
+        }
+    } else {
+        // ---------------- epilogue (warps 2..9) ----------------
+        const int q = warp & 3;                 // TMEM lane quarter of this warp
+        const int h = (warp - 2) >> 2;          // column half of the tile
+        const int r = q * 32 + lane;            // tile row
+        int acc = 0;
+        uint32_t aph = 0;
+        GTile w;
+        for (int T = blockIdx.x; T < total; T += gridDim.x) {
+            if (abort_flag) break;
+            if (!gram_tile(P, ids, tpp, T, w)) continue;
+            if (!mbar_wait(&accf[acc], aph)) { abort_flag = 1; atomicExch(err, 2); break; }
+            tc_fence_after();
+            const int n = w.n;
+            const int i0 = w.ti * 128, j0 = w.tc * GN + h * (GN / 2);
+            const int i = i0 + r;
+            const int pid = 2 * w.leaf + w.side;
+            const ScaoLeaf& L = P.leaves[w.leaf];
+            const int64_t fo = w.side ? L.rq_off : L.lq_off;
+            float mx = 0.f;
+            const uint32_t tbase = tmem + acc * GN + h * (GN / 2) + ((uint32_t)(q * 32) << 16);
+            int cend = min(GN / 2, n - j0);
+            // columns above the diagonal sub-tile are not needed
+            cend = min(cend, ((w.ti + 1) << 7) - j0);
+            if (P.int8_ema) {
+                const int8_t* qo = (const int8_t*)P.fac + fo;
+                const float s_old = quant_scale_f(P.absmax[pid]);
+                // all old codes of this thread's row segment in flight at once
+                int4 q4[GN / 32];
+#pragma unroll
+                for (int u = 0; u < GN / 32; ++u)
+                    q4[u] = (i < n && u * 16 < cend) ? *(const int4*)(qo + (int64_t)i * n + j0 + u * 16)
+                                                    : make_int4(0, 0, 0, 0);
+#pragma unroll
+                for (int u = 0; u < GN / 32; ++u) {
+                    const int c0 = u * 16;
+                    if (c0 >= cend) break;
+                    const int tj = (j0 + c0) >> 7;          // 128-sub-tile of these columns
+                    const bool diag = tj == w.ti;
+                    float v[16];
+                    tc_ld16(tbase + c0, v);
+                    const int8_t* qv = (const int8_t*)&q4[u];
+                    float xo[16];
+#pragma unroll
+                    for (int c = 0; c < 16; ++c) {
+                        const int jc = j0 + c0 + c;
+                        float x = 0.f;
+                        if (i < n && (!diag || jc <= i)) {
+                            const float deq = __fmul_rn((float)qv[c], s_old);
+                            x = __fadd_rn(__fmul_rn(deq, rho_f), __fmul_rn(alpha_f, v[c]));
+                            mx = fmaxf(mx, fabsf(x));
+                        }
+                        xo[c] = x;
+                    }
+                    float* xt = xbuf + (int64_t)w.j * xstride +
+                                (int64_t)(w.ti * (w.ti + 1) / 2 + tj) * GTRI + r * GT + ((j0 + c0) & 127);
+#pragma unroll
+                    for (int c = 0; c < 16; c += 4)
+                        __stcs((float4*)(xt + c), make_float4(xo[c], xo[c + 1], xo[c + 2], xo[c + 3]));
+                }
+            } else {
+                float* Lm = (float*)P.fac + fo;
+                for (int c0 = 0; c0 < cend; c0 += 16) {
+                    float v[16];
+                    tc_ld16(tbase + c0, v);
+#pragma unroll
+                    for (int c = 0; c < 16; ++c) {
+                        const int jc = j0 + c0 + c;
+                        if (i < n && jc <= i) {
+                            const int64_t o = (int64_t)i * n + jc;
+                            const float x = __fadd_rn(__fmul_rn(Lm[o], rho_f), __fmul_rn(alpha_f, v[c]));
+                            Lm[o] = x;
+                            if (jc != i) Lm[(int64_t)jc * n + i] = x;
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&acce[acc]);
+            acc ^= 1;
+            if (acc == 0) aph ^= 1;
+            if (P.int8_ema) {
+                mx = warp_max(mx);
+                if (lane == 0) atomic_max_nonneg(amnew + w.j, mx);
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tc_dealloc(tmem, 2 * GN);
+}
+
+size_t gram_tma_smem() { return (size_t)GST * GSTAGE + 1024; }
+
+// Requantise the tile-major staging of gram_tma_kernel (lower-triangle
+// tiles only) into both triangles of the int8 factor (utils.py:170-189).
+__global__ void __launch_bounds__(256)
+requant_tile_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, const float* __restrict__ xbuf,
+                    int64_t xstride, const float* __restrict__ amnew) {
+    const int j = blockIdx.y;
+    const int leaf = ids[j >> 1], side = j & 1;
+    const ScaoLeaf& L = P.leaves[leaf];
+    if (!gram_tma_ok(L, side, P.params[L.param].dtype)) return;
+    const int n = side ? L.b : L.a;
+    const int nt = (n + GT - 1) / GT;
+    const int t = blockIdx.x;
+    if (t >= nt * (nt + 1) / 2) return;
+    int ti = 0;
+    while ((ti + 1) * (ti + 2) / 2 <= t) ++ti;
+    const int tj = t - ti * (ti + 1) / 2;
+    const int i0 = ti * GT, j0 = tj * GT;
+    const bool diag = ti == tj;
+    const float am = amnew[j];
+    const bool zero = (double)am < 1e-30;
+    const float s = quant_scale_f(am);
+    int8_t* qd = (int8_t*)P.fac + (side ? L.rq_off : L.lq_off);
+    const float* x = xbuf + (int64_t)j * xstride + (int64_t)t * GTRI;
+    __shared__ int8_t tq[GT][GT + 4];
+    for (int e = threadIdx.x; e < GTRI / 4; e += 256) {
+        const float4 v = __ldcs((const float4*)x + e);
+        const int rr = (e * 4) / GT, cc = (e * 4) % GT;
+        tq[rr][cc + 0] = quant_one(v.x, s, zero);
+        tq[rr][cc + 1] = quant_one(v.y, s, zero);
+        tq[rr][cc + 2] = quant_one(v.z, s, zero);
+        tq[rr][cc + 3] = quant_one(v.w, s, zero);
+    }
+    __syncthreads();
+    // rows i0+rr, columns j0..j0+127 (diagonal tile: upper part mirrored)
+    for (int e = threadIdx.x; e < GT * GT / 4; e += 256) {
+        const int rr = (e * 4) / GT, cc = (e * 4) % GT;
+        if (i0 + rr >= n || j0 + cc >= n) continue;
+        char4 o;
+        if (!diag) {
+            o = make_char4(tq[rr][cc], tq[rr][cc + 1], tq[rr][cc + 2], tq[rr][cc + 3]);
+        } else {
+            const int8_t a0 = cc + 0 <= rr ? tq[rr][cc + 0] : tq[cc + 0][rr];
+            const int8_t a1 = cc + 1 <= rr ? tq[rr][cc + 1] : tq[cc + 1][rr];
+            const int8_t a2 = cc + 2 <= rr ? tq[rr][cc + 2] : tq[cc + 2][rr];
+            const int8_t a3 = cc + 3 <= rr ? tq[rr][cc + 3] : tq[cc + 3][rr];
+            o = make_char4(a0, a1, a2, a3);
+        }
+        *(char4*)(qd + (int64_t)(i0 + rr) * n + j0 + cc) = o;
+    }
+    if (!diag) {
+        // transposed copy: rows j0+cc, columns i0..i0+127
+        for (int e = threadIdx.x; e < GT * GT / 4; e += 256) {
+            const int cc = (e * 4) / GT, rr = (e * 4) % GT;
+            if (j0 + cc >= n || i0 + rr >= n) continue;
+            *(char4*)(qd + (int64_t)(j0 + cc) * n + i0 + rr) =
+                make_char4(tq[rr][cc], tq[rr + 1][cc], tq[rr + 2][cc], tq[rr + 3][cc]);
+        }
+    }
+    if (t == 0 && threadIdx.x == 0) P.absmax[2 * leaf + side] = am;
+}
+
 __global__ void __launch_bounds__(NT)
 gram_ema_simt_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids,
                      float* xbuf, int64_t xstride, float* amnew, float rho_f,
@@ -363,10 +718,11 @@ gram_ema_simt_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids,
 
 __global__ void requant_batch_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids,
                                      const float* __restrict__ xbuf, int64_t xstride,
-                                     const float* __restrict__ amnew) {
+                                     const float* __restrict__ amnew, int tma_on) {
     const int j = blockIdx.y;
     const int leaf = ids[j >> 1], side = j & 1;
     const ScaoLeaf& L = P.leaves[leaf];
+    if (tma_on && gram_tma_ok(L, side, P.params[L.param].dtype)) return;   // requant_tile_kernel
     const int n = side ? L.b : L.a;
     const int64_t nn = (int64_t)n * n;
     const float am = amnew[j];
@@ -407,20 +763,98 @@ __global__ void diag_ema_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids,
 
 }  // namespace
 
+namespace {
+
+int64_t ntri_tiles(int64_t n) {
+    const int64_t nt = (n + GT - 1) / GT;
+    return nt * (nt + 1) / 2;
+}
+
+// floats of fp32 staging per factor problem: the full n x n square (SIMT
+// and cp.async kernels) or the lower-triangle tiles (TMA kernel)
+int64_t xstride_floats(int64_t mx) {
+    const int64_t a = mx * mx, b = ntri_tiles(mx) * GTRI;
+    return ((a > b ? a : b) + 63) / 64 * 64;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess && q == cudaDriverEntryPointSuccess)
+            fn = (EncodeTiledFn)p;
+    }
+    return fn;
+}
+
+// Two maps per 2-D bf16 gradient (row-major rows x cols): [0] boxes of
+// 128 rows x 64 columns (K-major operands of L), [1] boxes of 64 x 64
+// (MN-major operands of R); 128-byte swizzle, zero fill out of bounds.
+bool build_tensor_maps(const ScaoPlanDev* P, const ScaoParam* ph, const ScaoParamStep* sh,
+                       cudaStream_t st) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc || !P->tmaps) return false;
+    std::vector<CUtensorMap> maps((size_t)P->n_params * 2);
+    memset(maps.data(), 0, maps.size() * sizeof(CUtensorMap));
+    for (int i = 0; i < P->n_params; ++i) {
+        if (ph[i].mode != 1 || ph[i].dtype != SCAO_BF16 || sh[i].phase == 0 || !sh[i].g_ptr)
+            continue;
+        if ((ph[i].cols % 8) != 0 || (sh[i].g_ptr & 15) != 0) continue;
+        const cuuint64_t dims[2] = {(cuuint64_t)ph[i].cols, (cuuint64_t)ph[i].rows};
+        const cuuint64_t strides[1] = {(cuuint64_t)ph[i].cols * 2};
+        const cuuint32_t es[2] = {1, 1};
+        const cuuint32_t box0[2] = {64, 128}, box1[2] = {64, 64};
+        if (enc(&maps[2 * i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void*)sh[i].g_ptr, dims,
+                strides, box0, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return false;
+        if (enc(&maps[2 * i + 1], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void*)sh[i].g_ptr, dims,
+                strides, box1, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return false;
+    }
+    // pageable source: the copy is staged before cudaMemcpyAsync returns
+    return cudaMemcpyAsync(P->tmaps, maps.data(), maps.size() * sizeof(CUtensorMap),
+                           cudaMemcpyHostToDevice, st) == cudaSuccess;
+}
+
+int sm_count() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
+}  // namespace
+
 extern "C" int64_t scao_ema_scratch_bytes(int n_ids, int max_a, int max_b) {
     const int64_t mx = max_a > max_b ? max_a : max_b;
-    return 2 * (int64_t)n_ids * (mx * mx * 4 + 256) + 256 * 4;
+    return 2 * (int64_t)n_ids * (xstride_floats(mx) * 4 + 256) + 256 * 4;
 }
 
 extern "C" int scao_plan_curvature(const ScaoPlanDev* P, const int32_t* leaf_ids,
                                    int n_ids, int max_a, int max_b, double rho,
                                    void* scratch, int64_t scratch_bytes,
+                                   const ScaoParam* params_host, const ScaoParamStep* step_host,
                                    void* stream) {
     if (!P || n_ids < 0 || !scratch) return SCAO_ERR_ARG;
     if (n_ids == 0) return SCAO_OK;
     cudaStream_t st = (cudaStream_t)stream;
     const int64_t mx = max_a > max_b ? max_a : max_b;
-    const int64_t xstride = ((mx * mx + 63) / 64) * 64;          // floats
+    const int64_t xstride = xstride_floats(mx);                   // floats
     const int64_t per_prob = xstride * 4 + 4;                    // bytes
     int64_t cap = (scratch_bytes - 1024) / per_prob;             // problems
     cap &= ~int64_t(1);
@@ -429,6 +863,12 @@ extern "C" int scao_plan_curvature(const ScaoPlanDev* P, const int32_t* leaf_ids
     const float alpha_f = (float)(1.0 - rho);   // Python-float 1 - rho, then cast
     const int nt = (int)((mx + TM - 1) / TM);
     const int tiles = nt * (nt + 1) / 2;
+    const int tpp = gram_work_tiles((int)mx);   // work tiles per problem (upper bound)
+    // SCAO_NO_TMA=1 selects the cp.async kernel for every problem (the
+    // tests compare both paths)
+    const char* no_tma = getenv("SCAO_NO_TMA");
+    const int tma_on = (params_host && step_host && !(no_tma && no_tma[0] == '1') &&
+                        build_tensor_maps(P, params_host, step_host, st)) ? 1 : 0;
     for (int64_t j0 = 0; j0 < 2 * (int64_t)n_ids; j0 += cap) {
         const int np = (int)((2 * (int64_t)n_ids - j0) < cap ? (2 * (int64_t)n_ids - j0) : cap);
         float* xbuf = (float*)scratch;
@@ -437,6 +877,20 @@ extern "C" int scao_plan_curvature(const ScaoPlanDev* P, const int32_t* leaf_ids
             return SCAO_ERR_LAUNCH;
         const int32_t* ids = leaf_ids + j0 / 2;
         dim3 grid(tiles, np);
+        if (tma_on) {
+            static bool tattr = false;
+            if (!tattr) {
+                cudaFuncSetAttribute(gram_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)gram_tma_smem());
+                tattr = true;
+            }
+            const int64_t work = (int64_t)np * tpp;
+            const int g = (int)(work < sm_count() ? work : sm_count());
+            ProfScope _ps(SLOT_GRAM_TC, st);
+            gram_tma_kernel<<<g, GTHREADS, gram_tma_smem(), st>>>(*P, ids, np, tpp, xbuf, xstride,
+                                                                  amnew, rho_f, alpha_f, P->err);
+        }
+        SCAO_CHECK_LAUNCH();
         {
             static bool attr = false;
             if (!attr) {
@@ -447,9 +901,9 @@ extern "C" int scao_plan_curvature(const ScaoPlanDev* P, const int32_t* leaf_ids
                 attr = true;
             }
             const int nt2 = (int)((mx + GT - 1) / GT);
-            ProfScope _ps2(SLOT_GRAM_TC, st);
+            ProfScope _ps2(SLOT_GRAM_EMA, st);
             gram_ema_tc_kernel<<<dim3(nt2 * (nt2 + 1) / 2, np), 256, gram_tc_smem(), st>>>(
-                *P, ids, xbuf, xstride, amnew, rho_f, alpha_f, P->err);
+                *P, ids, xbuf, xstride, amnew, rho_f, alpha_f, P->err, tma_on);
         }
         SCAO_CHECK_LAUNCH();
         { ProfScope _ps(SLOT_GRAM_EMA, st); gram_ema_simt_kernel<<<grid, NT, 0, st>>>(*P, ids, xbuf, xstride, amnew,
@@ -457,7 +911,12 @@ extern "C" int scao_plan_curvature(const ScaoPlanDev* P, const int32_t* leaf_ids
         SCAO_CHECK_LAUNCH();
         if (P->int8_ema) {
             dim3 g2((int)((mx * mx + 255) / 256 < 64 ? (mx * mx + 255) / 256 : 64), np);
-            { ProfScope _ps(SLOT_REQUANT, st); requant_batch_kernel<<<g2, 256, 0, st>>>(*P, ids, xbuf, xstride, amnew); }
+            { ProfScope _ps(SLOT_REQUANT, st); requant_batch_kernel<<<g2, 256, 0, st>>>(*P, ids, xbuf, xstride, amnew, tma_on); }
+            SCAO_CHECK_LAUNCH();
+            if (tma_on) {
+                ProfScope _ps(SLOT_REQUANT, st);
+                requant_tile_kernel<<<dim3((int)ntri_tiles(mx), np), 256, 0, st>>>(*P, ids, xbuf, xstride, amnew);
+            }
             SCAO_CHECK_LAUNCH();
         }
     }

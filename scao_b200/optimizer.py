@@ -263,7 +263,8 @@ class SCAO(Optimizer):
             need = L.scao_ema_scratch_bytes(len(leaves), ma, mb)
             scratch = self._get_ema_scratch(need)
             _lib.check(L.scao_plan_curvature(pd, ids.data_ptr(), len(leaves), ma, mb, rho,
-                                             scratch.data_ptr(), scratch.numel(), sp),
+                                             scratch.data_ptr(), scratch.numel(),
+                                             plan.ptab.ctypes.data, plan.step_host.data_ptr(), sp),
                        "scao_plan_curvature")
             keep.append(ids)
         for rho, pids in curv_diag.items():

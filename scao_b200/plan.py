@@ -246,6 +246,7 @@ class Plan:
         self.param_scalars = z(self.n_params * 8)
         self.global_norm_ema = torch.ones(1, dtype=torch.float64, device=dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.tmaps = torch.zeros(self.n_params * 256, dtype=torch.uint8, device=dev)
         self.counters = z(16, torch.int32)
         nc = max(len(self.ctab), 1)
         self.t_diag_list = z(nc, torch.int32)
@@ -417,6 +418,7 @@ def PlanDev_from(plan):
     d.leaf_nat2, d.param_scalars = ptr(plan.leaf_nat2), ptr(plan.param_scalars)
     d.global_norm_ema = ptr(plan.global_norm_ema)
     d.err = ptr(plan.err)
+    d.tmaps = ptr(plan.tmaps)
     d.ua, d.ut, d.wa = ptr(plan.ua), ptr(plan.ut), ptr(plan.wa)
     d.counters = ptr(plan.counters)
     d.diag_list, d.flat_list, d.p_list = ptr(plan.t_diag_list), ptr(plan.t_flat_list), ptr(plan.t_p_list)
