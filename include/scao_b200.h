@@ -201,7 +201,10 @@ typedef struct {
     int32_t* err;                /* device error flag: set to 1 when a bounded
                                     wait on the tensor core timed out       */
     uint8_t* tmaps;              /* n_params x 2 TMA tensor maps (128 B each,
-                                    written by scao_plan_curvature)         */
+                                    written by scao_plan_tensor_maps and
+                                    scao_plan_curvature)                    */
+    int32_t tmaps_ok;            /* 1: tmaps describe this step's gradients */
+    int32_t pad3_;
     ScaoFilterDev filt;          /* gradient filter and noise (mode 0: off) */
 } ScaoPlanDev;
 
@@ -273,14 +276,16 @@ SCAO_API int scao_dequantize_sym_int8(const int8_t* q, double scale, int64_t n,
 /* Curvature EMA for the leaves listed in leaf_ids (device int32, n ids):
  * L <- rho*L + (1-rho) G G^T, R <- rho*R + (1-rho) G^T G
  * (preconditioner.py:341-353), int8 requant fused (utils.py:170-203).
- * scratch: scao_ema_scratch_bytes(...) bytes.  params_host / step_host:
- * host copies of the parameter and step tables (may be NULL); with them the
- * bf16 factor GEMMs run on the TMA-fed persistent tensor-core kernel, whose
- * per-gradient tensor maps are written to plan_host->tmaps.                 */
+ * scratch: scao_ema_scratch_bytes(...) bytes.  params_host / step_host /
+ * leaves_host / leaf_ids_host: host copies of the parameter, step and leaf
+ * tables and of leaf_ids (may be NULL); with them the bf16 factor GEMMs run on the TMA-fed persistent
+ * tensor-core kernel, whose per-gradient tensor maps are written to
+ * plan_host->tmaps, and the fallback kernels launch only when needed.      */
 SCAO_API int scao_plan_curvature(const ScaoPlanDev* plan_host, const int32_t* leaf_ids,
                         int n_ids, int max_a, int max_b, double rho,
                         void* scratch, int64_t scratch_bytes,
                         const ScaoParam* params_host, const ScaoParamStep* step_host,
+                        const ScaoLeaf* leaves_host, const int32_t* leaf_ids_host,
                         void* stream);
 SCAO_API int64_t scao_ema_scratch_bytes(int n_ids, int max_a, int max_b);
 
@@ -289,6 +294,13 @@ SCAO_API int64_t scao_ema_scratch_bytes(int n_ids, int max_a, int max_b);
 SCAO_API int scao_plan_curvature_diag(const ScaoPlanDev* plan_host,
                              const int32_t* param_ids, int n_ids, double rho,
                              void* stream);
+
+/* TMA tensor maps of this step's gradients into plan_host->tmaps (host
+ * tables: params_host = the plan's ScaoParam table, step_host = this step's
+ * ScaoParamStep table).  The per-step kernels use them only when
+ * plan_host->tmaps_ok is 1, which the caller sets after SCAO_OK.           */
+SCAO_API int scao_plan_tensor_maps(const ScaoPlanDev* plan_host, const ScaoParam* params_host,
+                          const ScaoParamStep* step_host, void* stream);
 
 /* Eigen update of the listed leaves (preconditioner.py:363-451):
  * debias, Tikhonov eps = max(1e-8, 1e-4 tr/m), top-kmax eigenpairs by

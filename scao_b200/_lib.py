@@ -84,7 +84,7 @@ class PlanDev(C.Structure):
         ("diag_list", _P), ("flat_list", _P), ("p_list", _P),
         ("n_diag", C.c_int32), ("n_flat", C.c_int32), ("n_p", C.c_int32), ("pad2_", C.c_int32),
         ("err", _P),
-        ("tmaps", _P),
+        ("tmaps", _P), ("tmaps_ok", C.c_int32), ("pad3_", C.c_int32),
         ("filt", FilterDev),
     ]
 
@@ -118,8 +118,9 @@ SIGNATURES = {
     "scao_quantize_sym_int8": (C.c_int, [_P, C.c_int64, _P, _P, _P, _P]),
     "scao_dequantize_sym_int8": (C.c_int, [_P, C.c_double, C.c_int64, _P, _P]),
     "scao_plan_curvature": (C.c_int, [C.POINTER(PlanDev), _P, C.c_int, C.c_int, C.c_int,
-                                      C.c_double, _P, C.c_int64, _P, _P, _P]),
+                                      C.c_double, _P, C.c_int64, _P, _P, _P, _P, _P]),
     "scao_ema_scratch_bytes": (C.c_int64, [C.c_int, C.c_int, C.c_int]),
+    "scao_plan_tensor_maps": (C.c_int, [C.POINTER(PlanDev), _P, _P, _P]),
     "scao_plan_curvature_diag": (C.c_int, [C.POINTER(PlanDev), _P, C.c_int, C.c_double, _P]),
     "scao_plan_eigen": (C.c_int, [C.POINTER(PlanDev), _P, C.c_int, _P, _P, C.c_int,
                                   C.c_float, _P, C.c_int, C.c_int, _P]),

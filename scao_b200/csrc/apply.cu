@@ -27,6 +27,7 @@
 #include "prof.cuh"
 #include "tc.cuh"
 #include "filter.cuh"
+#include "tmap.cuh"
 
 namespace {
 
@@ -818,6 +819,222 @@ apply_kron_tc_kernel(ScaoPlanDev P, int* err) {
     }
 }
 
+// ---------------------------------------------------------------------------
+// Persistent, warp-specialised projection for bf16 gradients with a TMA
+// tensor map: one work item per 128-row panel of a Kronecker leaf.
+//   warp 0     TMA producer: G panel block (128 rows x 64 columns, 128-byte
+//              swizzle) + U_r^T block (bf16 hi/lo, bulk copy) per stage
+//   warp 1     TMEM owner + MMA issuer: T = G_panel U_r (hi and lo
+//              products, fp32 accumulators, two TMEM buffers)
+//   warps 2-5  epilogue: T -> shared, P_part = U_l[rows]^T T (FFMA, U_l
+//              rows read through L1), overlapping the next panel's loads
+// Panels whose leaf width is not a multiple of 64 stay on proj_bf16_kernel.
+// ---------------------------------------------------------------------------
+constexpr int PT_MAXST = 4;
+constexpr int PT_EPI = 256;                // epilogue threads (8 warps)
+constexpr int PT_THREADS = 64 + PT_EPI;
+
+__device__ __forceinline__ bool proj_tma_use(const ScaoPlanDev& P, const ScaoLeaf& L) {
+    const ScaoParam& pr = P.params[L.param];
+    const ScaoParamStep& S = P.step[L.param];
+    return P.tmaps_ok && S.phase == 2 && proj_fast(L, S, pr) && scao_tmap_ok(pr, S) &&
+           (L.b % 64) == 0;
+}
+
+__host__ __device__ inline int proj_tma_stages(int kpmax) { return kpmax > 64 ? 3 : 4; }
+__host__ __device__ inline uint32_t proj_tma_stage_bytes(int kpmax) {
+    return 128 * 64 * 2 + 2 * (uint32_t)kpmax * 64 * 2;
+}
+// U_l panel rows are staged in shared memory when they fit (Kp <= 64)
+__host__ __device__ inline bool proj_tma_ls_smem(int kpmax) { return kpmax <= 64; }
+size_t proj_tma_smem(int kpad_max) {
+    const int Kp = (kpad_max + 15) & ~15;
+    return (size_t)proj_tma_stages(Kp) * proj_tma_stage_bytes(Kp) +
+           (size_t)(proj_tma_ls_smem(Kp) ? 2 : 1) * 128 * (Kp + 4) * 4 + 1024;
+}
+
+__global__ void __launch_bounds__(PT_THREADS, 1)
+proj_tma_kernel(ScaoPlanDev P, int* err) {
+    extern __shared__ unsigned char psm_raw[];
+    unsigned char* psm = (unsigned char*)(((uintptr_t)psm_raw + 1023) & ~(uintptr_t)1023);
+    const int Kpm = (P.kpad_max + 15) & ~15;
+    const int nst = proj_tma_stages(Kpm);
+    const uint32_t SB = proj_tma_stage_bytes(Kpm);
+    float* Ts = (float*)(psm + (size_t)nst * SB);
+    float* Ls = Ts + 128 * (Kpm + 4);            // used when proj_tma_ls_smem(Kpm)
+    const bool ls_sm = proj_tma_ls_smem(Kpm);
+    __shared__ uint64_t full[PT_MAXST], empty[PT_MAXST], accf[2], acce[2], fin;
+    __shared__ uint32_t tslot;
+    __shared__ volatile int abort_flag, ep_go;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {
+        for (int i = 0; i < PT_MAXST; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
+        for (int i = 0; i < 2; ++i) { mbar_init(&accf[i], 1); mbar_init(&acce[i], PT_EPI); }
+        mbar_init(&fin, 1);
+        abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) tc_alloc(&tslot, 256);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tslot;
+    const int total = P.n_panels;
+    if (warp == 0) {
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t ph = 0, issued = 0, last_ph = 0;
+            for (int T = blockIdx.x; T < total && !abort_flag; T += gridDim.x) {
+                const ScaoPanel pn = P.panels[T];
+                const ScaoLeaf& L = P.leaves[pn.leaf];
+                if (!proj_tma_use(P, L)) continue;
+                const int Kp = (L.kpad + 15) & ~15;
+                const uint32_t bb = (uint32_t)Kp * 64 * 2;
+                const void* map = P.tmaps + (size_t)L.param * 2 * 128;
+                for (int kb = 0; kb < L.b / 64; ++kb) {
+                    if (!mbar_wait(&empty[stage], ph ^ 1)) { abort_flag = 1; atomicExch(err, 2); break; }
+                    mbar_expect_tx(&full[stage], 128 * 64 * 2 + 2 * bb);
+                    unsigned char* st = psm + (size_t)stage * SB;
+                    tma_load_2d(smem_u32(st), map, L.col0 + kb * 64, L.row0 + pn.row0, &full[stage]);
+                    bulk_g2s(st + 128 * 64 * 2, P.ut + L.ut_off + (int64_t)kb * 2 * bb, 2 * bb, &full[stage]);
+                    issued |= 1u << stage;
+                    last_ph = (last_ph & ~(1u << stage)) | (ph << stage);
+                    if (++stage == nst) { stage = 0; ph ^= 1; }
+                }
+            }
+            for (int s2 = 0; s2 < nst; ++s2)
+                if ((issued >> s2) & 1u)
+                    if (!mbar_wait(&full[s2], (last_ph >> s2) & 1u)) atomicExch(err, 2);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            int stage = 0, acc = 0;
+            uint32_t ph = 0, aph = 0;
+            for (int T = blockIdx.x; T < total && !abort_flag; T += gridDim.x) {
+                const ScaoPanel pn = P.panels[T];
+                const ScaoLeaf& L = P.leaves[pn.leaf];
+                if (!proj_tma_use(P, L)) continue;
+                const int Kp = (L.kpad + 15) & ~15;
+                const uint32_t bb = (uint32_t)Kp * 64 * 2;
+                if (!mbar_wait(&acce[acc], aph ^ 1)) { abort_flag = 1; atomicExch(err, 2); break; }
+                tc_fence_after();
+                const uint32_t d = tmem + acc * 128;
+                const uint32_t idesc = idesc_bf16(128, Kp);
+                bool ok = true;
+                for (int kb = 0; kb < L.b / 64; ++kb) {
+                    if (!mbar_wait(&full[stage], ph)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a = smem_u32(psm + (size_t)stage * SB);
+                    const uint32_t bh = a + 128 * 64 * 2, bl = bh + bb;
+#pragma unroll
+                    for (int s = 0; s < 4; ++s) {
+                        const uint64_t ad = smem_desc_sw128(a + s * 32, 16, 1024);
+                        tc_mma_bf16(d, ad, smem_desc(bh + s * 256, 128, 16 * 64), idesc,
+                                    (kb > 0 || s > 0) ? 1u : 0u);
+                        tc_mma_bf16(d, ad, smem_desc(bl + s * 256, 128, 16 * 64), idesc, 1u);
+                    }
+                    tc_commit(&empty[stage]);
+                    if (++stage == nst) { stage = 0; ph ^= 1; }
+                }
+                if (!ok) { abort_flag = 1; atomicExch(err, 2); break; }
+                tc_commit(&accf[acc]);
+                acc ^= 1;
+                if (acc == 0) aph ^= 1;
+            }
+            tc_commit(&fin);
+            if (!mbar_wait(&fin, 0)) atomicExch(err, 2);
+        }
+    } else {
+        const int et = tid - 64;                 // epilogue thread 0..PT_EPI-1
+        const int q = warp & 3;                  // TMEM lane quarter
+        const int h = (warp - 2) >> 2;           // which 16-column chunks
+        const int r = q * 32 + lane;
+        int acc = 0;
+        uint32_t aph = 0;
+        for (int T = blockIdx.x; T < total; T += gridDim.x) {
+            const ScaoPanel pn = P.panels[T];
+            const ScaoLeaf& L = P.leaves[pn.leaf];
+            if (!proj_tma_use(P, L)) continue;
+            // one decision for all four epilogue warps (they meet at named
+            // barriers, so none may leave the loop alone); also frees Ts
+            if (et == 0) ep_go = !abort_flag;
+            named_bar(1, PT_EPI);
+            if (!ep_go) break;
+            const int Kp = (L.kpad + 15) & ~15;
+            const int ld = Kp + 4;
+            const float* Ulp = P.u + L.ul_off + (int64_t)pn.row0 * L.sl;
+            const bool ls_async = ls_sm && (L.sl & 3) == 0;
+            if (ls_async) {
+                // U_l panel rows -> shared, overlapping the wait for T
+                const int q4 = Kp >> 2;
+                for (int c = et; c < 128 * q4; c += PT_EPI) {
+                    const int rr = c / q4, a = (c - rr * q4) * 4;
+                    const bool in = rr < pn.nrows && a < L.kpad;
+                    const float* src = in ? Ulp + (int64_t)rr * L.sl + a : Ulp;
+                    asm volatile("cp.async.ca.shared.global [%0], [%1], 16, %2;"
+                                 :: "r"(smem_u32(Ls + rr * ld + a)), "l"(src), "r"(in ? 16 : 0)
+                                 : "memory");
+                }
+                asm volatile("cp.async.commit_group;" ::: "memory");
+            }
+            const bool ok = __all_sync(0xffffffffu, mbar_wait(&accf[acc], aph));
+            if (!ok) { abort_flag = 1; atomicExch(err, 2); }
+            if (ok) {
+                tc_fence_after();
+                for (int c0 = 16 * h; c0 < Kp; c0 += 32) {
+                    float v[16];
+                    tc_ld16(tmem + acc * 128 + ((uint32_t)(q * 32) << 16) + c0, v);
+#pragma unroll
+                    for (int c = 0; c < 16; ++c) Ts[r * ld + c0 + c] = v[c];
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&acce[acc]);
+            acc ^= 1;
+            if (acc == 0) aph ^= 1;
+            if (ls_async) asm volatile("cp.async.wait_all;" ::: "memory");
+            named_bar(1, PT_EPI);                 // Ts (and Ls) complete
+            // P_part = U_l[rows]^T T, 4 x 4 blocks per thread
+            const int kp = L.kpad, nb = (kp + 3) >> 2;
+            float* out = P.p_part + (int64_t)T * P.p_stride;
+#ifdef SCAO_EXP_NOPB
+            if (nb > 0) continue;
+#endif
+            for (int blk = et; blk < nb * nb; blk += PT_EPI) {
+                const int a0 = (blk / nb) * 4, b0 = (blk % nb) * 4;
+                float accv[4][4] = {};
+#pragma unroll 4
+                for (int rr = 0; rr < pn.nrows; ++rr) {
+                    float av[4];
+                    if (ls_async) {
+                        const float4 la = *(const float4*)&Ls[rr * ld + a0];
+                        av[0] = la.x; av[1] = la.y; av[2] = la.z; av[3] = la.w;
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 4; ++i)
+                            av[i] = a0 + i < kp ? __ldg(Ulp + (int64_t)rr * L.sl + a0 + i) : 0.f;
+                    }
+                    const float4 tb = *(const float4*)&Ts[rr * ld + b0];
+                    const float bv[4] = {tb.x, tb.y, tb.z, tb.w};
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) accv[i][j] = fmaf(av[i], bv[j], accv[i][j]);
+                }
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        if (a0 + i < kp && b0 + j < kp) out[(a0 + i) * kp + b0 + j] = accv[i][j];
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tc_dealloc(tmem, 256);
+}
+
 // bf16 gradients: T = G_panel * U_r with the gradient streamed into shared
 // memory by cp.async (16-byte chunks land directly in the canonical layout),
 // a 4-stage pipeline, U_r^T blocks by TMA bulk copy.
@@ -830,6 +1047,7 @@ proj_bf16_kernel(ScaoPlanDev P, int* err) {
     if (S.phase != 2) return;
     const ScaoParam& pr = P.params[L.param];
     if (!proj_fast(L, S, pr)) return;        // handled by proj_tc_kernel
+    if (proj_tma_use(P, L)) return;          // handled by proj_tma_kernel
     const int Kp = (L.kpad + 15) & ~15;
     constexpr int KB = 64;
     extern __shared__ __align__(1024) unsigned char smx[];
@@ -1160,6 +1378,18 @@ extern "C" int scao_plan_step(const ScaoPlanDev* P, void* stream) {
             cudaFuncSetAttribute(apply_kron_tc_kernel<false>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
             pattr = true;
         }
+        if (P->tmaps_ok) {
+            static bool tattr = false;
+            if (!tattr) {
+                cudaFuncSetAttribute(proj_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)proj_tma_smem(128));
+                tattr = true;
+            }
+            const int g = P->n_panels < scao_sm_count() ? P->n_panels : scao_sm_count();
+            ProfScope _ps(SLOT_PROJ, st);
+            proj_tma_kernel<<<g, PT_THREADS, proj_tma_smem(P->kpad_max), st>>>(*P, P->err);
+        }
+        SCAO_CHECK_LAUNCH();
         { ProfScope _ps(SLOT_PROJ, st);
           proj_bf16_kernel<<<P->n_panels, 128, proj_bf16_smem(P->kpad_max), st>>>(*P, P->err);
           if (P->kron_dtypes & ~(1 << SCAO_BF16))

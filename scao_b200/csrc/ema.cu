@@ -11,14 +11,12 @@
 // Only the lower triangle of tiles is computed; the epilogue mirrors it.
 // This file holds the portable SIMT-FMA tile kernel; see gram_tc.cu for the
 // tcgen05 tensor-core path used for 16-bit gradients.
-#include <cuda.h>
 #include <stdlib.h>
-#include <string.h>
-#include <vector>
 
 #include "common.cuh"
 #include "prof.cuh"
 #include "tc.cuh"
+#include "tmap.cuh"
 
 namespace {
 
@@ -83,10 +81,18 @@ __device__ __forceinline__ bool gram_tc_ok(const Prob& p, const ScaoLeaf& L) {
 }
 
 // TMA path (gram_tma_kernel): whole 64-deep K blocks, 16-byte aligned rows
-__device__ __forceinline__ bool gram_tma_ok(const ScaoLeaf& L, int side, int dt) {
+__host__ __device__ inline bool gram_tma_ok(const ScaoLeaf& L, int side, int dt) {
     const int K = side ? L.a : L.b;
     return dt == SCAO_BF16 && (K % 64) == 0 && (L.a % 64) == 0 && (L.b % 64) == 0 &&
            (L.ld % 8) == 0 && (L.col0 % 8) == 0;
+}
+
+// the TMA kernel takes a factor problem when the block fits it and the
+// parameter's gradient has a tensor map this call
+__host__ __device__ inline bool gram_tma_use(const ScaoParam* params, const ScaoParamStep* step,
+                                             const ScaoLeaf& L, int side) {
+    return gram_tma_ok(L, side, params[L.param].dtype) &&
+           scao_tmap_ok(params[L.param], step[L.param]);
 }
 
 __global__ void __launch_bounds__(256, 2)
@@ -95,7 +101,7 @@ gram_ema_tc_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, float* xbuf, 
     const Prob p = get_prob(P, ids, blockIdx.y, xbuf, xstride, amnew);
     const ScaoLeaf& L = P.leaves[ids[blockIdx.y >> 1]];
     if (!gram_tc_ok(p, L)) return;
-    if (tma_on && gram_tma_ok(L, p.side, p.dt)) return;     // gram_tma_kernel
+    if (tma_on && gram_tma_use(P.params, P.step, L, p.side)) return;     // gram_tma_kernel
     const int nt = (p.n + GT - 1) / GT;
     const int t = blockIdx.x;
     if (t >= nt * (nt + 1) / 2) return;
@@ -294,22 +300,8 @@ constexpr int GEPI = 256;                // epilogue threads (8 warps)
 constexpr int GTHREADS = 64 + GEPI;
 constexpr int GTRI = GT * GT;           // floats per staged 128 x 128 sub-tile
 
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* map, int x, int y,
-                                            uint64_t* mbar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
-        "[%0], [%1, {%2, %3}], [%4];"
-        :: "r"(dst), "l"(map), "r"(x), "r"(y), "r"(smem_u32(mbar)) : "memory");
-}
 
-__device__ __forceinline__ void mbar_arrive(uint64_t* mbar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(smem_u32(mbar)) : "memory");
-}
 
-// 128-byte-swizzle shared-memory descriptor (layout type 2 in bits 61-63)
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-    return smem_desc(saddr, lbo, sbo) | ((uint64_t)2 << 61);
-}
 
 // work tiles of one factor problem: row block ti (128 rows), column block
 // tc (GN columns) for every tc * GN <= 128 ti + 127 (lower triangle)
@@ -335,7 +327,7 @@ __device__ __forceinline__ bool gram_tile(const ScaoPlanDev& P, const int32_t* i
     w.side = w.j & 1;
     const ScaoLeaf& L = P.leaves[w.leaf];
     w.param = L.param;
-    if (!gram_tma_ok(L, w.side, P.params[L.param].dtype)) return false;
+    if (!gram_tma_use(P.params, P.step, L, w.side)) return false;
     w.n = w.side ? L.b : L.a;
     w.K = w.side ? L.a : L.b;
     const int nt = (w.n + 127) / 128;
@@ -467,9 +459,14 @@ gram_tma_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, int nprob, int t
         uint32_t aph = 0;
         GTile w;
         for (int T = blockIdx.x; T < total; T += gridDim.x) {
-            if (abort_flag) break;
+            if (__any_sync(0xffffffffu, abort_flag)) break;
             if (!gram_tile(P, ids, tpp, T, w)) continue;
-            if (!mbar_wait(&accf[acc], aph)) { abort_flag = 1; atomicExch(err, 2); break; }
+            // warp-uniform: the TMEM loads below are warp-collective
+            if (!__all_sync(0xffffffffu, mbar_wait(&accf[acc], aph))) {
+                abort_flag = 1;
+                atomicExch(err, 2);
+                break;
+            }
             tc_fence_after();
             const int n = w.n;
             const int i0 = w.ti * 128, j0 = w.tc * GN + h * (GN / 2);
@@ -561,7 +558,7 @@ requant_tile_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, const float*
     const int j = blockIdx.y;
     const int leaf = ids[j >> 1], side = j & 1;
     const ScaoLeaf& L = P.leaves[leaf];
-    if (!gram_tma_ok(L, side, P.params[L.param].dtype)) return;
+    if (!gram_tma_use(P.params, P.step, L, side)) return;
     const int n = side ? L.b : L.a;
     const int nt = (n + GT - 1) / GT;
     const int t = blockIdx.x;
@@ -722,7 +719,7 @@ __global__ void requant_batch_kernel(ScaoPlanDev P, const int32_t* __restrict__ 
     const int j = blockIdx.y;
     const int leaf = ids[j >> 1], side = j & 1;
     const ScaoLeaf& L = P.leaves[leaf];
-    if (tma_on && gram_tma_ok(L, side, P.params[L.param].dtype)) return;   // requant_tile_kernel
+    if (tma_on && gram_tma_use(P.params, P.step, L, side)) return;   // requant_tile_kernel
     const int n = side ? L.b : L.a;
     const int64_t nn = (int64_t)n * n;
     const float am = amnew[j];
@@ -777,67 +774,6 @@ int64_t xstride_floats(int64_t mx) {
     return ((a > b ? a : b) + 63) / 64 * 64;
 }
 
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    static bool tried = false;
-    if (!tried) {
-        tried = true;
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-                cudaSuccess && q == cudaDriverEntryPointSuccess)
-            fn = (EncodeTiledFn)p;
-    }
-    return fn;
-}
-
-// Two maps per 2-D bf16 gradient (row-major rows x cols): [0] boxes of
-// 128 rows x 64 columns (K-major operands of L), [1] boxes of 64 x 64
-// (MN-major operands of R); 128-byte swizzle, zero fill out of bounds.
-bool build_tensor_maps(const ScaoPlanDev* P, const ScaoParam* ph, const ScaoParamStep* sh,
-                       cudaStream_t st) {
-    EncodeTiledFn enc = encode_fn();
-    if (!enc || !P->tmaps) return false;
-    std::vector<CUtensorMap> maps((size_t)P->n_params * 2);
-    memset(maps.data(), 0, maps.size() * sizeof(CUtensorMap));
-    for (int i = 0; i < P->n_params; ++i) {
-        if (ph[i].mode != 1 || ph[i].dtype != SCAO_BF16 || sh[i].phase == 0 || !sh[i].g_ptr)
-            continue;
-        if ((ph[i].cols % 8) != 0 || (sh[i].g_ptr & 15) != 0) continue;
-        const cuuint64_t dims[2] = {(cuuint64_t)ph[i].cols, (cuuint64_t)ph[i].rows};
-        const cuuint64_t strides[1] = {(cuuint64_t)ph[i].cols * 2};
-        const cuuint32_t es[2] = {1, 1};
-        const cuuint32_t box0[2] = {64, 128}, box1[2] = {64, 64};
-        if (enc(&maps[2 * i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void*)sh[i].g_ptr, dims,
-                strides, box0, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-            return false;
-        if (enc(&maps[2 * i + 1], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void*)sh[i].g_ptr, dims,
-                strides, box1, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-            return false;
-    }
-    // pageable source: the copy is staged before cudaMemcpyAsync returns
-    return cudaMemcpyAsync(P->tmaps, maps.data(), maps.size() * sizeof(CUtensorMap),
-                           cudaMemcpyHostToDevice, st) == cudaSuccess;
-}
-
-int sm_count() {
-    static int n = 0;
-    if (!n) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        if (n <= 0) n = 148;
-    }
-    return n;
-}
-
 }  // namespace
 
 extern "C" int64_t scao_ema_scratch_bytes(int n_ids, int max_a, int max_b) {
@@ -849,6 +785,7 @@ extern "C" int scao_plan_curvature(const ScaoPlanDev* P, const int32_t* leaf_ids
                                    int n_ids, int max_a, int max_b, double rho,
                                    void* scratch, int64_t scratch_bytes,
                                    const ScaoParam* params_host, const ScaoParamStep* step_host,
+                                   const ScaoLeaf* leaves_host, const int32_t* leaf_ids_host,
                                    void* stream) {
     if (!P || n_ids < 0 || !scratch) return SCAO_ERR_ARG;
     if (n_ids == 0) return SCAO_OK;
@@ -868,7 +805,18 @@ extern "C" int scao_plan_curvature(const ScaoPlanDev* P, const int32_t* leaf_ids
     // tests compare both paths)
     const char* no_tma = getenv("SCAO_NO_TMA");
     const int tma_on = (params_host && step_host && !(no_tma && no_tma[0] == '1') &&
-                        build_tensor_maps(P, params_host, step_host, st)) ? 1 : 0;
+                        scao_build_tensor_maps(P, params_host, step_host, st)) ? 1 : 0;
+    // with the host leaf table, the fallback kernels launch only when some
+    // listed problem needs them
+    bool fallback = true;
+    if (tma_on && leaves_host && leaf_ids_host) {
+        fallback = false;
+        for (int k = 0; k < n_ids && !fallback; ++k) {
+            const ScaoLeaf& L = leaves_host[leaf_ids_host[k]];
+            if (!gram_tma_use(params_host, step_host, L, 0) || !gram_tma_use(params_host, step_host, L, 1))
+                fallback = true;
+        }
+    }
     for (int64_t j0 = 0; j0 < 2 * (int64_t)n_ids; j0 += cap) {
         const int np = (int)((2 * (int64_t)n_ids - j0) < cap ? (2 * (int64_t)n_ids - j0) : cap);
         float* xbuf = (float*)scratch;
@@ -885,13 +833,13 @@ extern "C" int scao_plan_curvature(const ScaoPlanDev* P, const int32_t* leaf_ids
                 tattr = true;
             }
             const int64_t work = (int64_t)np * tpp;
-            const int g = (int)(work < sm_count() ? work : sm_count());
+            const int g = (int)(work < scao_sm_count() ? work : scao_sm_count());
             ProfScope _ps(SLOT_GRAM_TC, st);
             gram_tma_kernel<<<g, GTHREADS, gram_tma_smem(), st>>>(*P, ids, np, tpp, xbuf, xstride,
                                                                   amnew, rho_f, alpha_f, P->err);
         }
         SCAO_CHECK_LAUNCH();
-        {
+        if (fallback) {
             static bool attr = false;
             if (!attr) {
                 cudaFuncSetAttribute(gram_ema_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -906,12 +854,17 @@ extern "C" int scao_plan_curvature(const ScaoPlanDev* P, const int32_t* leaf_ids
                 *P, ids, xbuf, xstride, amnew, rho_f, alpha_f, P->err, tma_on);
         }
         SCAO_CHECK_LAUNCH();
-        { ProfScope _ps(SLOT_GRAM_EMA, st); gram_ema_simt_kernel<<<grid, NT, 0, st>>>(*P, ids, xbuf, xstride, amnew,
-                                                   rho_f, alpha_f); }
+        if (fallback) {
+            ProfScope _ps(SLOT_GRAM_EMA, st);
+            gram_ema_simt_kernel<<<grid, NT, 0, st>>>(*P, ids, xbuf, xstride, amnew, rho_f, alpha_f);
+        }
         SCAO_CHECK_LAUNCH();
         if (P->int8_ema) {
             dim3 g2((int)((mx * mx + 255) / 256 < 64 ? (mx * mx + 255) / 256 : 64), np);
-            { ProfScope _ps(SLOT_REQUANT, st); requant_batch_kernel<<<g2, 256, 0, st>>>(*P, ids, xbuf, xstride, amnew, tma_on); }
+            if (fallback) {
+                ProfScope _ps(SLOT_REQUANT, st);
+                requant_batch_kernel<<<g2, 256, 0, st>>>(*P, ids, xbuf, xstride, amnew, tma_on);
+            }
             SCAO_CHECK_LAUNCH();
             if (tma_on) {
                 ProfScope _ps(SLOT_REQUANT, st);

@@ -136,3 +136,28 @@ TC_DEV void bulk_g2s(void* dst_smem, const void* src_gmem, uint32_t bytes, uint6
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
         :: "r"(smem_u32(dst_smem)), "l"(src_gmem), "r"(bytes), "r"(smem_u32(mbar)) : "memory");
 }
+
+// TMA tensor copy of one 2-D box (coordinates x = innermost) into shared
+// memory, completion counted on an mbarrier.  No multicast.
+TC_DEV void tma_load_2d(uint32_t dst, const void* map, int x, int y, uint64_t* mbar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3}], [%4];"
+        :: "r"(dst), "l"(map), "r"(x), "r"(y), "r"(smem_u32(mbar)) : "memory");
+}
+
+TC_DEV void mbar_arrive(uint64_t* mbar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(smem_u32(mbar)) : "memory");
+}
+
+// 128-byte-swizzle shared-memory descriptor (layout type 2 in bits 61-63):
+// K-major tiles of 128-byte rows in 8-row / 1024-byte atoms as written by a
+// TMA copy with CU_TENSOR_MAP_SWIZZLE_128B into a 1024-byte aligned buffer.
+TC_DEV uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    return smem_desc(saddr, lbo, sbo) | ((uint64_t)2 << 61);
+}
+
+// named barrier over a subset of the CTA's warps
+TC_DEV void named_bar(int id, int nthreads) {
+    asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(nthreads) : "memory");
+}

@@ -12,6 +12,7 @@ tensors and the library must be built.
 from __future__ import annotations
 
 import math
+import os
 from typing import Callable, Iterable
 
 import numpy as np
@@ -258,13 +259,15 @@ class SCAO(Optimizer):
         import ctypes
         pd = ctypes.byref(dptr)
         for rho, leaves in curv_leaves.items():
-            ids = torch.tensor(leaves, dtype=torch.int32, device=dev)
+            ids_h = np.ascontiguousarray(leaves, dtype=np.int32)
+            ids = torch.from_numpy(ids_h).to(dev)
             ma, mb, _ = plan.max_dims(leaves)
             need = L.scao_ema_scratch_bytes(len(leaves), ma, mb)
             scratch = self._get_ema_scratch(need)
             _lib.check(L.scao_plan_curvature(pd, ids.data_ptr(), len(leaves), ma, mb, rho,
                                              scratch.data_ptr(), scratch.numel(),
-                                             plan.ptab.ctypes.data, plan.step_host.data_ptr(), sp),
+                                             plan.ptab.ctypes.data, plan.step_host.data_ptr(),
+                                             plan.ltab.ctypes.data, ids_h.ctypes.data, sp),
                        "scao_plan_curvature")
             keep.append(ids)
         for rho, pids in curv_diag.items():
@@ -285,6 +288,17 @@ class SCAO(Optimizer):
             self._last_eig_status = status
             keep.append(ids)
         plan.set_phases(np.array(tab["phase"], dtype=np.int32))
+        if plan.has_bf16_kron and os.environ.get("SCAO_NO_TMA") != "1":
+            # tensor maps of the gradients (rebuilt only when a pointer or
+            # phase changed)
+            key = (tab["g_ptr"].tobytes(), tab["phase"].tobytes())
+            if key != plan.tmap_key:
+                rc = L.scao_plan_tensor_maps(pd, plan.ptab.ctypes.data, plan.step_host.data_ptr(), sp)
+                plan.dev.tmaps_ok = 1 if rc == 0 else 0
+                plan.tmap_key = key if rc == 0 else None
+        else:
+            plan.dev.tmaps_ok = 0
+            plan.tmap_key = None
         f = plan.dev.filt
         f.noise_on = 1 if self._noise_std > 1e-9 else 0     # optimizer.py:544
         f.noise_std = float(np.float32(self._noise_std))

@@ -247,6 +247,9 @@ class Plan:
         self.global_norm_ema = torch.ones(1, dtype=torch.float64, device=dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
         self.tmaps = torch.zeros(self.n_params * 256, dtype=torch.uint8, device=dev)
+        self.tmap_key = None
+        self.has_bf16_kron = any(int(r["mode"]) == 1 and int(r["dtype"]) == DTYPE_CODE[torch.bfloat16]
+                                 for r in self.ptab)
         self.counters = z(16, torch.int32)
         nc = max(len(self.ctab), 1)
         self.t_diag_list = z(nc, torch.int32)

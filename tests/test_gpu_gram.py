@@ -1,5 +1,6 @@
-"""The TMA-fed persistent tensor-core gram kernel against the cp.async
-tensor-core kernel (SCAO_NO_TMA=1) on leaf blocks both can run: identical
+"""The TMA-fed persistent tensor-core kernels (gram of the curvature EMA,
+projection of the step) against the cp.async tensor-core kernels
+(SCAO_NO_TMA=1) on leaf blocks both can run.  Gram: identical
 factor codes (int8) / values (fp32), identical absmax, for L = G G^T
 (K-major operands) and R = G^T G (MN-major operands), diagonal and
 off-diagonal tiles, partial tiles (64-multiples) and blocks inside larger
@@ -59,3 +60,38 @@ def test_tma_gram_matches_cp_async_gram(int8):
         assert torch.equal(fa, fb)
     else:
         assert torch.equal(fa, fb) or (fa - fb).abs().max().item() <= 1e-6 * fb.abs().max().item()
+
+
+def _run_steps(no_tma, steps=6):
+    if no_tma:
+        os.environ["SCAO_NO_TMA"] = "1"
+    else:
+        os.environ.pop("SCAO_NO_TMA", None)
+    try:
+        gen = torch.Generator().manual_seed(3)
+        params = [torch.nn.Parameter((torch.randn(s, generator=gen) * 0.02).to(DEV, torch.bfloat16))
+                  for s in SHAPES]
+        opt = SCAO(params, lr=1e-3, precond_freq=2, warmup_steps=2, min_precond_updates=1,
+                   blend_steps=3, use_int8_ema=True, max_precond_dim=1024, sparsity=0.0,
+                   noise_std_init=0.0, k_max=32, async_precond=False, lookahead_k=0)
+        for _ in range(steps):
+            for p in params:
+                p.grad = (torch.randn(p.shape, generator=gen) * 3.0).to(DEV, torch.bfloat16)
+            opt.step()
+        torch.cuda.synchronize()
+        opt._plan.check_error()
+        return [p.detach().clone().cpu() for p in params], \
+            [opt.state[p]["exp_avg"].clone().cpu() for p in params]
+    finally:
+        os.environ.pop("SCAO_NO_TMA", None)
+
+
+def test_tma_projection_matches_cp_async_projection():
+    """Phase-2 steps: identical parameters and moments with the persistent
+    TMA projection and with the cp.async projection."""
+    pa, ma = _run_steps(no_tma=False)
+    pb, mb = _run_steps(no_tma=True)
+    for x, y in zip(pa, pb):
+        assert torch.equal(x, y)
+    for x, y in zip(ma, mb):
+        assert torch.equal(x, y)
