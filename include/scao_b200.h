@@ -153,6 +153,8 @@ typedef struct {
     float noise_std;       /* float32(noise_std)                              */
     uint64_t noise_seed;   /* Philox-4x32-10 key                              */
     uint64_t noise_step;   /* counter word: global step                       */
+    int32_t gsnr_on;       /* R4: update * (|m| / (sqrt(v) + eps) >= thr)     */
+    float gsnr_thr;        /* float32(gsnr_threshold)                         */
 } ScaoFilterDev;
 
 /* Device-side plan: pointers to the tables and arenas above.              */
@@ -204,7 +206,8 @@ typedef struct {
                                     written by scao_plan_tensor_maps and
                                     scao_plan_curvature)                    */
     int32_t tmaps_ok;            /* 1: tmaps describe this step's gradients */
-    int32_t pad3_;
+    int32_t gnorm_host;          /* 1: the host maintains *global_norm_ema
+                                    this step (the kernels only read it)    */
     ScaoFilterDev filt;          /* gradient filter and noise (mode 0: off) */
 } ScaoPlanDev;
 
@@ -301,6 +304,12 @@ SCAO_API int scao_plan_curvature_diag(const ScaoPlanDev* plan_host,
  * plan_host->tmaps_ok is 1, which the caller sets after SCAO_OK.           */
 SCAO_API int scao_plan_tensor_maps(const ScaoPlanDev* plan_host, const ScaoParam* params_host,
                           const ScaoParamStep* step_host, void* stream);
+
+/* Per-parameter fp32 norm of this step's raw gradient, ||g|| (0 for params
+ * without a gradient) into out (device, n_params floats).  Feeds the host
+ * logic of the R1 / R3 / R5 extensions (optimizer.py:161-214, 383-401,
+ * 439-446).                                                                 */
+SCAO_API int scao_plan_grad_norms(const ScaoPlanDev* plan_host, float* out, void* stream);
 
 /* Eigen update of the listed leaves (preconditioner.py:363-451):
  * debias, Tikhonov eps = max(1e-8, 1e-4 tr/m), top-kmax eigenpairs by

@@ -289,6 +289,28 @@ class OraclePreconditioner:
         P = (self.U_l.T @ g) @ self.U_r
         return norm_f32(s_l[:, None] * P * s_r[None, :])
 
+    def set_k(self, new_k):
+        """R5 rank assignment, preconditioner.py:249-291: clamp to
+        [k_min, k_max]; a decrease truncates the eigenfactors, an increase is
+        clamped to their current width (so it waits for the next eigen
+        update); block-diagonal: every block, then the integer mean."""
+        new_k = int(min(self.k_max, max(self.k_min, new_k)))
+        if self.use_block_diagonal:
+            for b in self.blocks:
+                b.set_k(new_k)
+            self.k = sum(b.k for b in self.blocks) // max(len(self.blocks), 1)
+            return
+        if self.use_kronecker:
+            if new_k < self.k:
+                self.U_l = np.ascontiguousarray(self.U_l[:, :new_k])
+                self.S_l = np.ascontiguousarray(self.S_l[:new_k])
+                self.U_r = np.ascontiguousarray(self.U_r[:, :new_k])
+                self.S_r = np.ascontiguousarray(self.S_r[:new_k])
+            elif new_k > self.k:
+                cols = self.U_l.shape[1]
+                new_k = min(new_k, cols) if new_k > cols else new_k
+        self.k = new_k
+
     def leaves(self):
         """Leaf preconditioners in block order (self for non-split)."""
         if self.use_block_diagonal:
@@ -381,6 +403,63 @@ class OracleSparseFilter:
         return grad * (self.mag >= thr).astype(F32)
 
 
+# ---------------------------------------------------------------------------
+# R1 adaptive warmup (optimizer.py:104-150), R3 lazy trigger (:182-214),
+# R4 gSNR clip (:161-175)
+# ---------------------------------------------------------------------------
+
+class OracleWarmupScheduler:
+    """``_AdaptiveWarmupScheduler`` (optimizer.py:104-150)."""
+
+    def __init__(self, warmup_steps=100, stability_threshold=0.05, patience=5, min_warmup=20):
+        self.warmup_steps, self.thr, self.patience = warmup_steps, stability_threshold, patience
+        self.min_warmup = min_warmup
+        self.prev = float("inf")
+        self.stable = 0
+        self.early = None
+
+    def update(self, step, avg):
+        if step < self.min_warmup:
+            return True
+        if self.prev > 0:
+            rel = abs(avg - self.prev) / (self.prev + 1e-8)
+            self.stable = self.stable + 1 if rel < self.thr else 0
+        self.prev = avg
+        if self.stable >= self.patience:
+            self.early = self.early or step
+            return False
+        return step < self.warmup_steps
+
+
+class OracleLazyTrigger:
+    """``_LazyPrecondTrigger`` (optimizer.py:182-214)."""
+
+    def __init__(self, delta_threshold=0.1, max_skip=50):
+        self.thr, self.max_skip = delta_threshold, max_skip
+        self.prev = 0.0
+        self.since = 0
+
+    def should_update(self, g):
+        self.since += 1
+        if self.since >= self.max_skip:
+            self.since = 0
+            self.prev = g
+            return True
+        if self.prev > 0:
+            if abs(g - self.prev) / (self.prev + 1e-8) > self.thr:
+                self.since = 0
+                self.prev = g
+                return True
+        self.prev = g
+        return False
+
+
+def gsnr_clip(update, m, v, eps, thr):
+    """optimizer.py:161-175: update * (|m| / (sqrt(v) + eps) >= thr)."""
+    snr = np.abs(m) / (np.sqrt(v) + F32(eps))
+    return update * (snr >= F32(thr)).astype(F32)
+
+
 _DEFAULTS = dict(lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01,
                  precond_freq=20, epsilon_sparse=0.05, k_min=8, k_max=128,
                  rho=0.999, tau=1.0, warmup_steps=100, blend_steps=50,
@@ -390,8 +469,8 @@ _DEFAULTS = dict(lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01,
 
 class OracleSCAO:
     """optimizer.py:221-645 restricted to the deterministic path (no gradient
-    noise, no R1/R3-R5 extensions; the sparse filter and its R2 dynamic form
-    are included), numpy float32.
+    noise; the sparse filter with its R2 dynamic form and the R1, R3, R4, R5
+    extensions are included), numpy float32.
 
     ``params`` is a list of float32 arrays holding parameter-dtype values;
     ``groups`` is a list of dicts {"params": [indices], **overrides}.
@@ -405,6 +484,20 @@ class OracleSCAO:
         self.sparsity = float(kw.pop("sparsity", 0.0))
         self.dynamic_sparsity = bool(kw.pop("dynamic_sparsity", False))
         self.filters = {}
+        # R1 / R3 / R4 / R5 (optimizer.py:325-345)
+        self.adaptive_warmup = bool(kw.pop("adaptive_warmup", False))
+        ws = kw.get("warmup_steps", _DEFAULTS["warmup_steps"])
+        self.warmup_sched = OracleWarmupScheduler(
+            ws, kw.pop("warmup_stability_threshold", 0.05), kw.pop("warmup_patience", 5),
+            max(20, ws // 5))
+        self.in_warmup_global = True
+        self.lazy = bool(kw.pop("lazy_precond", False))
+        self.lazy_thr = float(kw.pop("lazy_delta_threshold", 0.1))
+        self.lazy_skip = int(kw.pop("lazy_max_skip", 50))
+        self.triggers = {}
+        self.gsnr = bool(kw.pop("use_gsnr_clip", False))
+        self.gsnr_thr = float(kw.pop("gsnr_threshold", 0.5))
+        self.adaptive_rank = bool(kw.pop("adaptive_rank", False))
         # gradient noise (optimizer.py:544-545) draws from torch's generator and
         # is not restated: the oracle is the noise-free path
         for k in ("noise_std_init", "async_precond", "noise_anneal"):
@@ -446,9 +539,12 @@ class OracleSCAO:
         """optimizer.py:452-503."""
         self.global_step += 1
         norms = [float(norm_f32(g)) for g in grads if g is not None]
+        avg = 0.0
         if norms:
             avg = sum(norms) / len(norms)
             self.global_norm_ema = 0.95 * self.global_norm_ema + 0.05 * avg
+        if self.adaptive_warmup:                       # optimizer.py:470-479
+            self.in_warmup_global = self.warmup_sched.update(self.global_step, avg)
         if self.dynamic_sparsity:
             for f in self.filters.values():
                 f.set_global_norm_ref(self.global_norm_ema)
@@ -499,6 +595,7 @@ class OracleSCAO:
             step = st["step"]
             raw = np.asarray(gr, dtype=F32)       # p.grad (param dtype values)
             grad = raw
+            grad_norm = float(norm_f32(raw))     # optimizer.py:532
             if self.sparsity > 0.0:              # optimizer.py:536-542
                 if i not in self.filters:
                     self.filters[i] = OracleSparseFilter(self.sparsity, self.dynamic_sparsity)
@@ -508,7 +605,14 @@ class OracleSCAO:
                 p = round_to(p * F32(1.0 - lr * wd), dt)
             m, v, d, prev = st["m"], st["v"], st["d"], st["prev"]
             pc = st["precond"]
-            in_warmup = (step <= group["warmup_steps"]) or \
+            if self.adaptive_rank:                      # R5, optimizer.py:383-401
+                ratio = grad_norm / (self.global_norm_ema + 1e-8)
+                if ratio > 2.0:
+                    pc.set_k(min(group["k_max"], int(pc.k * 1.25)))
+                elif ratio < 0.5:
+                    pc.set_k(max(group["k_min"], int(pc.k * 0.8)))
+            in_warmup = (self.in_warmup_global if self.adaptive_warmup
+                         else step <= group["warmup_steps"]) or \
                 (pc.precond_step < group["min_precond_updates"])
             if in_warmup:
                 m = fma(grad, F32(1.0 - beta1), m * F32(beta1))
@@ -527,7 +631,13 @@ class OracleSCAO:
                 st["scao_step"] = 0
             st["scao_step"] += 1
             sstep = st["scao_step"]
-            if step % pf == 0:
+            if self.lazy:                               # R3, optimizer.py:594-599
+                if i not in self.triggers:
+                    self.triggers[i] = OracleLazyTrigger(self.lazy_thr, self.lazy_skip)
+                upd_now = self.triggers[i].should_update(grad_norm)
+            else:
+                upd_now = step % pf == 0
+            if upd_now:
                 pc.update_curvature(raw)
             gp = pc.precondition(raw, dt)
             if tau is not None:
@@ -548,6 +658,8 @@ class OracleSCAO:
             bc3 = 1.0 - beta3 ** step
             upd = (m / F32(bc1) + F32(1.0 - beta3) * (d / F32(bc3))) / \
                 (np.sqrt(v / F32(bc2)) + F32(eps))
+            if self.gsnr:                               # R4, optimizer.py:637-638
+                upd = gsnr_clip(upd, m, v, eps, self.gsnr_thr)
             trust = self._lars(p, upd, lars, wd) if lars > 0 else 1.0
             p = add_alpha(p, round_to(upd, dt), -(lr * trust), dt)
             st.update(m=m, v=v, d=d, prev=prev)

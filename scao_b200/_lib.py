@@ -57,6 +57,7 @@ class FilterDev(C.Structure):
         ("norm_coeff", C.c_double), ("ema", C.c_float), ("ema_c", C.c_float),
         ("noise_on", C.c_int32), ("noise_std", C.c_float),
         ("noise_seed", C.c_uint64), ("noise_step", C.c_uint64),
+        ("gsnr_on", C.c_int32), ("gsnr_thr", C.c_float),
     ]
 
 
@@ -84,7 +85,7 @@ class PlanDev(C.Structure):
         ("diag_list", _P), ("flat_list", _P), ("p_list", _P),
         ("n_diag", C.c_int32), ("n_flat", C.c_int32), ("n_p", C.c_int32), ("pad2_", C.c_int32),
         ("err", _P),
-        ("tmaps", _P), ("tmaps_ok", C.c_int32), ("pad3_", C.c_int32),
+        ("tmaps", _P), ("tmaps_ok", C.c_int32), ("gnorm_host", C.c_int32),
         ("filt", FilterDev),
     ]
 
@@ -95,7 +96,7 @@ def check_layout():
     assert LEAF_DT.itemsize == 160, LEAF_DT.itemsize
     assert CHUNK_DT.itemsize == 24, CHUNK_DT.itemsize
     assert FILTER_PARAM_DT.itemsize == 80, FILTER_PARAM_DT.itemsize
-    assert C.sizeof(FilterDev) == 112, C.sizeof(FilterDev)
+    assert C.sizeof(FilterDev) == 120, C.sizeof(FilterDev)
 
 
 check_layout()
@@ -121,6 +122,7 @@ SIGNATURES = {
                                       C.c_double, _P, C.c_int64, _P, _P, _P, _P, _P]),
     "scao_ema_scratch_bytes": (C.c_int64, [C.c_int, C.c_int, C.c_int]),
     "scao_plan_tensor_maps": (C.c_int, [C.POINTER(PlanDev), _P, _P, _P]),
+    "scao_plan_grad_norms": (C.c_int, [C.POINTER(PlanDev), _P, _P]),
     "scao_plan_curvature_diag": (C.c_int, [C.POINTER(PlanDev), _P, C.c_int, C.c_double, _P]),
     "scao_plan_eigen": (C.c_int, [C.POINTER(PlanDev), _P, C.c_int, _P, _P, C.c_int,
                                   C.c_float, _P, C.c_int, C.c_int, _P]),

@@ -345,7 +345,8 @@ apply_flat_kernel(ScaoPlanDev P) {
             const float den = fadd(powf(fdiv(de[e], S.diag_bias), 0.25f), 1e-8f);
             const float gp = round_dt(fdiv(gv, den), dt);
             float m = M[e], v = V[e], d = Dd[e], pv = Pv[e];
-            const float u = adan_elem(S, dt, fl ? gfilt(gv, e) : gv, gp, m, v, d, pv, clip, clipmul);
+            float u = adan_elem(S, dt, fl ? gfilt(gv, e) : gv, gp, m, v, d, pv, clip, clipmul);
+            if (FN && FD.gsnr_on) u = gsnr_mask(u, m, v, S.eps, FD.gsnr_thr);
             usq = fmaf(u, u, usq);
             gsq = fmaf(gv, gv, gsq);
             M[e] = m; V[e] = v; Dd[e] = d; Pv[e] = pv;
@@ -771,7 +772,8 @@ apply_kron_tc_kernel(ScaoPlanDev P, int* err) {
                 mv[c] += gp; vv[c] += gp * gp; dv[c] -= gp; qv[c] = gv[c];
                 const float u = mv[c];
 #else
-                const float u = adan_elem(S, dt, gf[c], gp, mv[c], vv[c], dv[c], qv[c], clip, clipmul);
+                float u = adan_elem(S, dt, gf[c], gp, mv[c], vv[c], dv[c], qv[c], clip, clipmul);
+                if (FN && FD.gsnr_on) u = gsnr_mask(u, mv[c], vv[c], S.eps, FD.gsnr_thr);
 #endif
                 usq = fmaf(u, u, usq);
                 gsq = fmaf(gv[c], gv[c], gsq);
@@ -798,7 +800,8 @@ apply_kron_tc_kernel(ScaoPlanDev P, int* err) {
                                    FD.noise_on ? f4_get(noise_normal4(FD.noise_seed, L.param,
                                                                       FD.noise_step, oc >> 2), (int)(oc & 3))
                                                : 0.f);
-                const float u = adan_elem(S, dt, gf, gp, mv, vv, dv, qv, clip, clipmul);
+                float u = adan_elem(S, dt, gf, gp, mv, vv, dv, qv, clip, clipmul);
+                if (FN && FD.gsnr_on) u = gsnr_mask(u, mv, vv, S.eps, FD.gsnr_thr);
                 usq = fmaf(u, u, usq);
                 gsq = fmaf(gv, gv, gsq);
                 const float pd = round_dt(fmul(load_dt(pp, oc, dt), wdm), dt);
@@ -1359,7 +1362,7 @@ extern "C" int scao_plan_step(const ScaoPlanDev* P, void* stream) {
         const int rc = scao_filter_run(P, st);
         if (rc != SCAO_OK) return rc;
     }
-    const bool fn = P->filt.mode != 0 || P->filt.noise_on != 0;
+    const bool fn = P->filt.mode != 0 || P->filt.noise_on != 0 || P->filt.gsnr_on != 0;
     if (P->n_panels > 0) {
         static bool pattr = false;
         if (!pattr) {
@@ -1442,7 +1445,7 @@ extern "C" int scao_plan_step(const ScaoPlanDev* P, void* stream) {
     }
     { ProfScope _ps(SLOT_PARAM_POST, st); param_post_kernel<<<P->n_params, NT, 0, st>>>(*P); }
     SCAO_CHECK_LAUNCH();
-    if (P->filt.mode == 0) {
+    if (P->filt.mode == 0 && !P->gnorm_host) {
         { ProfScope _ps(SLOT_GLOBAL_NORM, st); global_norm_kernel<<<1, 256, 0, st>>>(*P); }
         SCAO_CHECK_LAUNCH();
     }
@@ -1450,6 +1453,67 @@ extern "C" int scao_plan_step(const ScaoPlanDev* P, void* stream) {
         if (P->n_p > 0) { ProfScope _ps(SLOT_APPLY_P, st); apply_p_kernel<<<P->n_p, NT, 0, st>>>(*P); }
         SCAO_CHECK_LAUNCH();
     }
+    return SCAO_OK;
+}
+
+namespace {
+
+// sum of raw grad^2 per flat chunk (slot 3 of chunk_part)
+__global__ void __launch_bounds__(NT)
+grad_sq_kernel(ScaoPlanDev P) {
+    const ScaoChunk ch = P.chunks[blockIdx.x];
+    const ScaoParamStep& S = P.step[ch.param];
+    if (S.phase == 0) return;
+    const ScaoParam& pr = P.params[ch.param];
+    __shared__ float red[32];
+    const void* g = (const void*)S.g_ptr;
+    const int dt = pr.dtype;
+    float s = 0.f;
+    const bool vec = ((S.g_ptr & 15) == 0) && ((ch.begin & 3) == 0);
+    int64_t vend = ch.begin;
+    if (vec) {
+        const int64_t n4 = (ch.end - ch.begin) >> 2;
+        vend = ch.begin + n4 * 4;
+        for (int64_t q = threadIdx.x; q < n4; q += NT) {
+            const float4 v = load4_dt(g, ch.begin + q * 4, dt);
+            s = fmaf(v.x, v.x, s); s = fmaf(v.y, v.y, s);
+            s = fmaf(v.z, v.z, s); s = fmaf(v.w, v.w, s);
+        }
+    }
+    for (int64_t e = vend + threadIdx.x; e < ch.end; e += NT) {
+        const float v = load_dt(g, e, dt);
+        s = fmaf(v, v, s);
+    }
+    s = block_sum(s, red);
+    if (threadIdx.x == 0) P.chunk_part[blockIdx.x * 4 + 3] = s;
+}
+
+__global__ void __launch_bounds__(NT)
+grad_norm_param_kernel(ScaoPlanDev P, float* out) {
+    const int pi = blockIdx.x;
+    const ScaoParam& pr = P.params[pi];
+    __shared__ float red[32];
+    if (P.step[pi].phase == 0) {
+        if (threadIdx.x == 0) out[pi] = 0.f;
+        return;
+    }
+    float s = 0.f;
+    for (int c = pr.chunk_begin + threadIdx.x; c < pr.chunk_end; c += NT) s += P.chunk_part[c * 4 + 3];
+    s = block_sum(s, red);
+    if (threadIdx.x == 0) out[pi] = sqrtf(s);
+}
+
+}  // namespace
+
+extern "C" int scao_plan_grad_norms(const ScaoPlanDev* P, float* out, void* stream) {
+    if (!P || !out) return SCAO_ERR_ARG;
+    cudaStream_t st = (cudaStream_t)stream;
+    if (P->n_chunks > 0) {
+        { ProfScope _ps(SLOT_GLOBAL_NORM, st); grad_sq_kernel<<<P->n_chunks, NT, 0, st>>>(*P); }
+        SCAO_CHECK_LAUNCH();
+    }
+    { ProfScope _ps(SLOT_GLOBAL_NORM, st); grad_norm_param_kernel<<<P->n_params, NT, 0, st>>>(*P, out); }
+    SCAO_CHECK_LAUNCH();
     return SCAO_OK;
 }
 

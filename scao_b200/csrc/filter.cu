@@ -134,7 +134,8 @@ filt_global_kernel(ScaoPlanDev P) {
     }
     if (threadIdx.x == 0) {
         double e = *P.global_norm_ema;
-        if (c > 0) e = __dadd_rn(__dmul_rn(0.95, e), __dmul_rn(0.05, s / (double)c));
+        // the host keeps the EMA itself when it needs the norms (R1/R3/R5)
+        if (c > 0 && !P.gnorm_host) e = __dadd_rn(__dmul_rn(0.95, e), __dmul_rn(0.05, s / (double)c));
         *P.global_norm_ema = e;
         gema = e;
     }

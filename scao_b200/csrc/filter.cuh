@@ -54,6 +54,13 @@ SCAO_DEV float filt_grad(const ScaoFilterDev& F, float g, float mag, float thr, 
     return g;
 }
 
+// R4 gSNR clip (optimizer.py:161-175, applied at :637-638): the update is
+// multiplied by (|m| / (sqrt(v) + eps) >= thr) with the updated moments.
+SCAO_DEV float gsnr_mask(float u, float m, float v, float eps, float thr) {
+    const float snr = __fdiv_rn(fabsf(m), __fadd_rn(sqrtf(v), eps));
+    return __fmul_rn(u, snr >= thr ? 1.f : 0.f);
+}
+
 // Host entry of the filter passes (filter.cu): magnitude EMA, radix
 // selection of the quantile, threshold per parameter.
 int scao_filter_run(const ScaoPlanDev* P, cudaStream_t st);

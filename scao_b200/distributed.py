@@ -95,7 +95,8 @@ class ShardedSCAO:
     communication stream, bucket b's step runs as soon as its gradients have
     arrived, and its all-gather is queued right after its step."""
 
-    def __init__(self, params, workload, make_inner, group=None, costs=None, buckets=4):
+    def __init__(self, params, workload, make_inner, group=None, costs=None, buckets=4,
+                 comm_priority=True):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -126,7 +127,12 @@ class ShardedSCAO:
         self.grad_sets = []
         self.cur = None
         self.nccl = dist.get_backend(group) == "nccl"
-        self.comm = torch.cuda.Stream(self.device) if self.nccl else None
+        # a high-priority communication stream: the collectives' blocks are
+        # scheduled ahead of queued compute blocks, so the pipeline keeps moving
+        self.comm = (torch.cuda.Stream(self.device, priority=-1 if comm_priority else 0)
+                     if self.nccl else None)
+        self.skip_comm = False       # measurement only: compute without collectives
+        self.skip_compute = False    # measurement only: collectives without compute
 
     def owned_specs(self):
         return [self.specs[i] for i in self.my]
@@ -197,19 +203,21 @@ class ShardedSCAO:
         with torch.cuda.stream(C):
             for b in range(nb):
                 full_g, _, mine_g = self._views(self.cur, b)
-                dist.reduce_scatter_tensor(mine_g, full_g, op=dist.ReduceOp.AVG,
-                                           group=self.group)
+                if not self.skip_comm:
+                    dist.reduce_scatter_tensor(mine_g, full_g, op=dist.ReduceOp.AVG,
+                                               group=self.group)
                 ev_rs[b].record(C)
         for b in range(nb):
             D.wait_event(ev_rs[b])
-            if self.inner[b] is not None:
+            if self.inner[b] is not None and not self.skip_compute:
                 self.inner[b].step()
             ev = torch.cuda.Event()
             ev.record(D)
             full_p, mine_p, _ = self._views(self.flat_p, b)
             with torch.cuda.stream(C):
                 C.wait_event(ev)
-                dist.all_gather_into_tensor(full_p, mine_p, group=self.group)
+                if not self.skip_comm:
+                    dist.all_gather_into_tensor(full_p, mine_p, group=self.group)
         D.wait_stream(C)
 
     @property

@@ -25,6 +25,68 @@ from .preconditioner import PrecondView
 
 
 
+class _AdaptiveWarmupScheduler:
+    """R1 (optimizer.py:104-150): leave the Adam warmup early once the mean
+    gradient norm has changed by less than ``stability_threshold`` (relative)
+    for ``patience`` consecutive steps.  Host logic on the per-step norms."""
+
+    def __init__(self, warmup_steps=100, stability_threshold=0.05, patience=5, min_warmup=20):
+        self.warmup_steps = warmup_steps
+        self.stability_threshold = stability_threshold
+        self.patience = patience
+        self.min_warmup = min_warmup
+        self._prev_norm = float("inf")
+        self._stable_count = 0
+        self._early_exit_step = None
+
+    def update(self, step: int, avg_grad_norm: float) -> bool:
+        if step < self.min_warmup:
+            return True
+        if self._prev_norm > 0:
+            rel = abs(avg_grad_norm - self._prev_norm) / (self._prev_norm + 1e-8)
+            self._stable_count = self._stable_count + 1 if rel < self.stability_threshold else 0
+        self._prev_norm = avg_grad_norm
+        if self._stable_count >= self.patience:
+            self._early_exit_step = self._early_exit_step or step
+            return False
+        return step < self.warmup_steps
+
+    @property
+    def exited_early(self) -> bool:
+        return self._early_exit_step is not None
+
+    @property
+    def actual_warmup_steps(self) -> int:
+        return self._early_exit_step or self.warmup_steps
+
+
+class _LazyPrecondTrigger:
+    """R3 (optimizer.py:182-214): refresh the curvature when the gradient norm
+    moved by more than ``delta_threshold`` (relative) or after ``max_skip``
+    steps."""
+
+    def __init__(self, delta_threshold=0.1, max_skip=50):
+        self.delta_threshold = delta_threshold
+        self.max_skip = max_skip
+        self._prev_grad_norm = 0.0
+        self._steps_since_update = 0
+
+    def should_update(self, grad_norm: float) -> bool:
+        self._steps_since_update += 1
+        if self._steps_since_update >= self.max_skip:
+            self._steps_since_update = 0
+            self._prev_grad_norm = grad_norm
+            return True
+        if self._prev_grad_norm > 0:
+            rel = abs(grad_norm - self._prev_grad_norm) / (self._prev_grad_norm + 1e-8)
+            if rel > self.delta_threshold:
+                self._steps_since_update = 0
+                self._prev_grad_norm = grad_norm
+                return True
+        self._prev_grad_norm = grad_norm
+        return False
+
+
 class SCAO(Optimizer):
     """B200-native SCAO.  Same signature and defaults as the reference
     (optimizer.py:258-296)."""
@@ -97,9 +159,22 @@ class SCAO(Optimizer):
         self._lookahead_init = False
         self._sparsity = sparsity
         self._dynamic_sparsity = bool(dynamic_sparsity)
-        self._opts = dict(adaptive_warmup=adaptive_warmup, lazy_precond=lazy_precond,
-                          use_gsnr_clip=use_gsnr_clip, adaptive_rank=adaptive_rank)
-        self._warmup_cfg = (warmup_steps, warmup_stability_threshold, warmup_patience)
+        # R1 / R3 / R4 / R5 (optimizer.py:332-345)
+        self._adaptive_warmup = bool(adaptive_warmup)
+        self._warmup_scheduler = _AdaptiveWarmupScheduler(
+            warmup_steps=warmup_steps, stability_threshold=warmup_stability_threshold,
+            patience=warmup_patience, min_warmup=max(20, warmup_steps // 5))
+        self._lazy_precond = bool(lazy_precond)
+        self._lazy_triggers: dict = {}
+        self._lazy_delta_threshold = lazy_delta_threshold
+        self._lazy_max_skip = lazy_max_skip
+        self._use_gsnr_clip = bool(use_gsnr_clip)
+        self._gsnr_threshold = gsnr_threshold
+        self._adaptive_rank = bool(adaptive_rank)
+        # R1 / R3 / R5 decide on the host from per-parameter gradient norms;
+        # the host then keeps the global grad-norm EMA as well
+        self._host_norms = self._adaptive_warmup or self._lazy_precond or self._adaptive_rank
+        self._gema = 1.0
         self._in_warmup_global = True
         self._eig_max_iters = int(eig_max_iters)
         self._eig_tol = float(eig_tol)
@@ -135,6 +210,15 @@ class SCAO(Optimizer):
             self._plan = Plan(ps, gs, dev, int8.pop())
             if self._sparsity > 0.0:
                 self._plan.setup_filter(2 if self._dynamic_sparsity else 1, self._sparsity)
+        f = self._plan.dev.filt
+        f.gsnr_on = 1 if self._use_gsnr_clip else 0          # R4
+        f.gsnr_thr = float(np.float32(self._gsnr_threshold))
+        self._plan.dev.gnorm_host = 1 if self._host_norms else 0
+        self._plan.gnorm_dev = torch.zeros(len(ps), dtype=torch.float32, device=dev)
+        self._plan.gnorm_pin = torch.zeros(len(ps), dtype=torch.float32,
+                                           pin_memory=torch.cuda.is_available())
+        self._plan.k_pin = torch.zeros(max(self._plan.n_leaves, 1), dtype=torch.int32,
+                                       pin_memory=torch.cuda.is_available())
         # noise stream key: the device generator's seed (consumes no draws)
         gen = torch.cuda.default_generators[dev.index if dev.index is not None
                                             else torch.cuda.current_device()]
@@ -150,10 +234,6 @@ class SCAO(Optimizer):
             st["prev_grad"] = self._plan.state_view(self._plan.prev_grad, i)
             st["preconditioner"] = PrecondView(self._plan, i, g)
 
-    def _check_supported(self):
-        for k, v in self._opts.items():
-            if v:
-                raise NotImplementedError(f"scao_b200: {k}=True is not implemented yet")
 
     # ------------------------------------------------------------------
     # step
@@ -164,7 +244,6 @@ class SCAO(Optimizer):
         if closure is not None:
             with torch.enable_grad():
                 loss = closure()
-        self._check_supported()
         if self._plan is None:
             self._build_plan()
             if self._plan is None:
@@ -180,14 +259,14 @@ class SCAO(Optimizer):
         curv_diag: dict = {}
         eig_leaves, eig_bias = [], []
         keep = []
-        warm_max = max((g.get("warmup_steps", 100) for g in self.param_groups), default=100)
-        self._in_warmup_global = self._global_step <= warm_max
-        for i, (p, g) in enumerate(zip(ps, gs)):
+        grads = []
+        for i, p in enumerate(ps):
             row = tab[i]
             row["p_ptr"] = p.data_ptr()
             grad = p.grad
             if grad is None:
                 row["phase"] = 0
+                grads.append(None)
                 continue
             if grad.is_sparse:
                 raise RuntimeError("SCAO does not support sparse gradients.")
@@ -196,6 +275,28 @@ class SCAO(Optimizer):
                 keep.append(grad)
             if not p.is_contiguous():
                 raise RuntimeError("scao_b200 needs contiguous parameters")
+            row["g_ptr"] = grad.data_ptr()
+            row["phase"] = 1
+            grads.append(grad)
+        norms = kvec = None
+        if self._host_norms:
+            norms, kvec = self._grad_norms_and_ranks(plan)
+            live = [float(norms[i]) for i in range(len(ps)) if grads[i] is not None]
+            avg = sum(live) / len(live) if live else 0.0
+            if live:
+                self._gema = 0.95 * self._gema + 0.05 * avg           # optimizer.py:445
+            plan.global_norm_ema.fill_(self._gema)
+        warm_max = max((g.get("warmup_steps", 100) for g in self.param_groups), default=100)
+        if self._adaptive_warmup:                                       # R1, :470-474
+            self._in_warmup_global = self._warmup_scheduler.update(self._global_step, avg)
+        else:
+            self._in_warmup_global = self._global_step <= warm_max
+        k_changed = False
+        for i, (p, g) in enumerate(zip(ps, gs)):
+            row = tab[i]
+            grad = grads[i]
+            if grad is None:
+                continue
             st = self.state[p]
             st["step"] += 1
             step = st["step"]
@@ -204,8 +305,28 @@ class SCAO(Optimizer):
             wd = float(g["weight_decay"])
             b1, b2 = g["betas"]
             b3 = g["beta3"]
-            in_warmup = (step <= g["warmup_steps"]) or (pc.precond_step < g["min_precond_updates"])
-            if step % g["precond_freq"] == 0:
+            if self._adaptive_rank:                                     # R5, :383-401
+                ratio = float(norms[i]) / (self._gema + 1e-8)
+                cur = pc.k_host(kvec)
+                new_k = None
+                if ratio > 2.0:
+                    new_k = min(g["k_max"], int(cur * 1.25))
+                elif ratio < 0.5:
+                    new_k = max(g["k_min"], int(cur * 0.8))
+                if new_k is not None and new_k != cur:
+                    k_changed |= pc.set_k_host(new_k, kvec)
+            in_warmup = (self._in_warmup_global if self._adaptive_warmup
+                         else step <= g["warmup_steps"]) or \
+                (pc.precond_step < g["min_precond_updates"])
+            if self._lazy_precond and not in_warmup:                    # R3, :594-599
+                tr = self._lazy_triggers.get(i)
+                if tr is None:
+                    tr = self._lazy_triggers[i] = _LazyPrecondTrigger(
+                        self._lazy_delta_threshold, self._lazy_max_skip)
+                do_curv = tr.should_update(float(norms[i]))
+            else:
+                do_curv = step % g["precond_freq"] == 0
+            if do_curv:
                 pc.precond_step += 1
                 rho = float(g["rho"])
                 leaves = plan.param_leaves[i]
@@ -216,7 +337,6 @@ class SCAO(Optimizer):
                     eig_bias.extend([bf] * len(leaves))
                 else:
                     curv_diag.setdefault(rho, []).append(i)
-            row["g_ptr"] = grad.data_ptr()
             row["lr"] = lr
             row["wd"] = wd
             row["wd_mult"] = np.float32(1.0 - lr * wd) if wd != 0.0 else np.float32(1.0)
@@ -252,6 +372,8 @@ class SCAO(Optimizer):
         dev = plan.device
         stream = torch.cuda.current_stream(dev)
         sp = C_stream(stream)
+        if k_changed:
+            plan.k.copy_(torch.from_numpy(kvec).to(dev))
         plan.t_step.copy_(plan.step_host, non_blocking=True)
         plan.step_event = torch.cuda.Event()
         plan.step_event.record(stream)
@@ -318,6 +440,22 @@ class SCAO(Optimizer):
                 cb(metrics)
         return loss
 
+    def _grad_norms_and_ranks(self, plan):
+        """Per-parameter ||g|| of this step (device kernel over the step
+        table's gradient pointers) and the current leaf ranks, read back
+        together (one synchronisation)."""
+        import ctypes
+        L = _lib.lib()
+        stream = torch.cuda.current_stream(plan.device)
+        plan.t_step.copy_(plan.step_host, non_blocking=True)
+        _lib.check(L.scao_plan_grad_norms(ctypes.byref(plan.dev), plan.gnorm_dev.data_ptr(),
+                                          C_stream(stream)), "scao_plan_grad_norms")
+        plan.gnorm_pin.copy_(plan.gnorm_dev, non_blocking=True)
+        if plan.n_leaves:
+            plan.k_pin.copy_(plan.k, non_blocking=True)
+        stream.synchronize()
+        return plan.gnorm_pin.numpy().copy(), plan.k_pin.numpy()[:plan.n_leaves].copy()
+
     def _get_ema_scratch(self, need):
         cap = 2 << 30
         need = min(int(need), cap)
@@ -343,7 +481,9 @@ class SCAO(Optimizer):
     @property
     def _global_norm_ema(self) -> float:
         if self._plan is None:
-            return 1.0
+            return self._gema
+        if self._host_norms:
+            return self._gema
         return float(self._plan.global_norm_ema.item())
 
     def collect_metrics(self) -> dict:
@@ -372,8 +512,8 @@ class SCAO(Optimizer):
             return {}
         return {"num_precond_layers": len(ks), "rank_min": min(ks), "rank_max": max(ks),
                 "rank_mean": sum(ks) / len(ks), "global_norm_ema": self._global_norm_ema,
-                "warmup_exited_early": False,
-                "actual_warmup_steps": self._warmup_cfg[0]}
+                "warmup_exited_early": self._warmup_scheduler.exited_early,
+                "actual_warmup_steps": self._warmup_scheduler.actual_warmup_steps}
 
     def synchronize_precond(self) -> None:
         """Single-stream implementation: nothing is pending on a side stream."""
@@ -410,9 +550,9 @@ class SCAO(Optimizer):
                 "global_step": self._global_step,
                 "noise_std": self._noise_std,
                 "global_norm_ema": self._global_norm_ema,
-                "warmup_prev_norm": float("inf"),
-                "warmup_stable_count": 0,
-                "warmup_early_exit_step": None,
+                "warmup_prev_norm": self._warmup_scheduler._prev_norm,
+                "warmup_stable_count": self._warmup_scheduler._stable_count,
+                "warmup_early_exit_step": self._warmup_scheduler._early_exit_step,
             },
         }
 
@@ -445,7 +585,12 @@ class SCAO(Optimizer):
             self._global_step = int(runtime.get("global_step", self._global_step))
             self._noise_std = float(runtime.get("noise_std", self._noise_std))
             if "global_norm_ema" in runtime:
-                self._plan.global_norm_ema.fill_(float(runtime["global_norm_ema"]))
+                self._gema = float(runtime["global_norm_ema"])
+                self._plan.global_norm_ema.fill_(self._gema)
+            ws = self._warmup_scheduler
+            ws._prev_norm = float(runtime.get("warmup_prev_norm", ws._prev_norm))
+            ws._stable_count = int(runtime.get("warmup_stable_count", ws._stable_count))
+            ws._early_exit_step = runtime.get("warmup_early_exit_step", ws._early_exit_step)
         self._lookahead_init = False
 
 

@@ -11,7 +11,7 @@ from __future__ import annotations
 import numpy as np
 import torch
 
-from .plan import to_2d_shape
+from .plan import k_bounds, to_2d_shape
 
 
 def _scale_from_absmax(am):
@@ -134,6 +134,67 @@ class PrecondView:
         self.use_block_diagonal = int(plan.ptab[pi]["mode"]) == 1 and not self.use_kronecker
         self._leaves = [LeafView(plan, li, self) for li in leaves]
         self._blocks = self._leaves if self.use_block_diagonal else []
+        # rank bounds of every node of the block tree (preconditioner.py:122-124)
+        self._ktree = self._bounds_tree(self.m, self.n, group["max_precond_dim"],
+                                        group["k_min"], group["k_max"], iter(leaves)) \
+            if leaves else None
+        self._k_mean = False     # an R5 assignment made every level a block mean
+        self._k_plain = None     # R5-assigned k of a leaf-free (diagonal) parameter
+
+    @staticmethod
+    def _bounds_tree(m, n, mpd, kmin, kmax, leaves):
+        lo, hi = k_bounds(m, n, kmin, kmax)
+        if max(m, n) <= mpd:
+            return (lo, hi, next(leaves))
+        large, small = (m, n) if m >= n else (n, m)
+        sizes = [mpd] * (large // mpd) + ([large % mpd] if large % mpd else [])
+        kids = [PrecondView._bounds_tree(*((bs, small) if m >= n else (small, bs)), mpd, kmin,
+                                         kmax, leaves) for bs in sizes]
+        return (lo, hi, kids)
+
+    def _walk_k(self, node, kvec):
+        lo, hi, c = node
+        if not isinstance(c, list):
+            return int(kvec[c])
+        sub = [self._walk_k(x, kvec) for x in c]
+        if self.precond_step == 0 and not self._k_mean:   # initialised as the first block's k (:194)
+            return sub[0]
+        return sum(sub) // max(len(sub), 1)              # mean of the blocks (:329)
+
+    def k_host(self, kvec):
+        """``k`` from a host copy of the per-leaf ranks."""
+        if self._ktree is None:
+            return 1 if self._k_plain is None else self._k_plain
+        return self._walk_k(self._ktree, kvec)
+
+    def set_k_host(self, new_k, kvec):
+        """R5 rank assignment (preconditioner.py:249-291) on a host copy of
+        the per-leaf ranks: clamp to each node's [k_min, k_max]; a leaf only
+        ever shrinks (growth waits for the next eigen update, because the
+        eigenfactors hold exactly k columns); block-diagonal nodes propagate
+        and become the mean of their blocks.  Returns True if kvec changed."""
+        if self._ktree is None:
+            lo, hi = k_bounds(self.m, self.n, 1, 1) if self.m > 1 else (1, 1)
+            self._k_plain = int(min(hi, max(lo, new_k)))
+            return False
+        changed = False
+
+        def setk(node, k):
+            nonlocal changed
+            lo, hi, c = node
+            k = int(min(hi, max(lo, k)))
+            if isinstance(c, list):
+                for x in c:
+                    setk(x, k)
+                return
+            if k < int(kvec[c]):
+                kvec[c] = k
+                changed = True
+
+        setk(self._ktree, new_k)
+        if isinstance(self._ktree[2], list):
+            self._k_mean = True
+        return changed
 
     @property
     def diag_bias(self):
@@ -142,19 +203,15 @@ class PrecondView:
     @property
     def k(self):
         if not self._leaves:
-            return 1
-        ks = iter(self.plan.k[self.plan.param_leaves[self.pi]].tolist())
+            return 1 if self._k_plain is None else self._k_plain
+        return self._walk_k(self._ktree, self.plan.k.cpu().numpy())
 
-        def walk(t):
-            # block-diagonal k = integer mean of the sub-blocks' k
-            # (preconditioner.py:329), applied at every nesting level
-            if t == 1:
-                return next(ks)
-            sub = [walk(c) for c in t]
-            if self.precond_step == 0:      # initialised as the first block's k (:194)
-                return sub[0]
-            return sum(sub) // max(len(sub), 1)
-        return walk(self.plan.param_trees[self.pi])
+    @k.setter
+    def k(self, new_k):
+        """preconditioner.py:249-291 (external rank assignment, R5)."""
+        kvec = self.plan.k.cpu().numpy().copy()
+        if self.set_k_host(int(new_k), kvec):
+            self.plan.k.copy_(torch.from_numpy(kvec).to(self.plan.device))
 
     @property
     def diag_ema(self):
@@ -164,7 +221,7 @@ class PrecondView:
         if t == 1:
             return next(leaves).state_dict()
         blocks = [self._tree_state(c, leaves) for c in t]
-        k = blocks[0]["k"] if self.precond_step == 0 else \
+        k = blocks[0]["k"] if self.precond_step == 0 and not self._k_mean else \
             sum(b["k"] for b in blocks) // max(len(blocks), 1)
         return {"precond_step": self.precond_step, "k": k, "use_kronecker": False,
                 "use_block_diagonal": True, "blocks": blocks}

@@ -99,6 +99,8 @@ class LowRankGradients:
             x = (U * self.s[:rr].unsqueeze(0)) @ V.T
             x += torch.randn(x.shape, generator=g, device=self.device,
                              dtype=torch.float64) * self.noise
+            if self.w.grad_scales is not None:
+                x *= self.w.grad_scales[i]
             grads.append(x.to(self.dtype))
             m, n = spec.shape
             zu = torch.randn(U.shape, generator=g, device=self.device,

@@ -32,6 +32,7 @@ class Workload:
     param_dtype: str = "float32"
     steps: int = 100
     grad_scale: float = 1e-2
+    grad_scales: tuple = None     # optional per-parameter multipliers
     notes: str = ""
 
     @property
@@ -94,10 +95,11 @@ def tiny(dtype="float32", max_precond_dim=4096, steps=40, grad_scale=1e-2,
               blend_steps=10, min_precond_updates=1, k_min=4, k_max=8,
               use_int8_ema=int8, max_precond_dim=max_precond_dim, **_PARITY)
     kw.update(extra or {})
+    scales = kw.pop("_grad_scales", None)
     return Workload(
         "tiny", ps, kw,
         grad_rank=4, grad_decay=0.7, param_dtype=dtype, steps=steps,
-        grad_scale=grad_scale)
+        grad_scale=grad_scale, grad_scales=scales)
 
 
 def c1() -> Workload:

@@ -15,13 +15,21 @@ CASES = {
     "bf16_spec": ("bfloat16", 48, 30, 1.0, True),
     "f32_sparse": ("float32", 4096, 30, 1.0, True),
     "bf16_dyn": ("bfloat16", 48, 30, 1.0, True),
+    "f32_r135": ("float32", 48, 30, 1.0, False),
+    "bf16_gsnr": ("bfloat16", 4096, 30, 1.0, True),
 }
 
-# optimizer keyword overrides of a case (the gradient filter of
-# optimizer.py:40-97, static and R2-dynamic)
+# optimizer keyword overrides of a case: the gradient filter of
+# optimizer.py:40-97 (static and R2-dynamic), R1 adaptive warmup, R3 lazy
+# curvature trigger, R5 adaptive rank, R4 gSNR clip
 EXTRA = {
     "f32_sparse": dict(sparsity=0.7),
     "bf16_dyn": dict(sparsity=0.6, dynamic_sparsity=True),
+    "f32_r135": dict(adaptive_warmup=True, warmup_patience=2, warmup_stability_threshold=0.5,
+                     lazy_precond=True, lazy_delta_threshold=0.02, lazy_max_skip=4,
+                     adaptive_rank=True, k_min=2, k_max=4,
+                     _grad_scales=(1.0, 1.0, 0.05, 1.0, 1.0, 1.0)),
+    "bf16_gsnr": dict(use_gsnr_clip=True, gsnr_threshold=0.3),
 }
 
 

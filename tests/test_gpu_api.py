@@ -151,3 +151,40 @@ def test_quadratic_converges():
         loss().backward()
         opt.step()
     assert loss().item() < l0 - 1.0
+
+
+def test_rank_setter_matches_oracle():
+    """``preconditioner.k = v`` (preconditioner.py:249-291) on a nested
+    block-diagonal parameter: clamping, truncation only, block mean."""
+    from oracle import scao_oracle as O
+    shape = (1100, 2500)
+    p = torch.nn.Parameter(torch.zeros(shape, device=DEV))
+    opt = SCAO([p], lr=1e-3, max_precond_dim=512, k_min=4, k_max=32, **KW)
+    p.grad = torch.randn(shape, device=DEV) * 1e-2
+    opt.step()
+    pc = opt.state[p]["preconditioner"]
+    ref = O.OraclePreconditioner(shape, k_min=4, k_max=32, max_precond_dim=512)
+    assert pc.k == ref.k
+    for v in (3, 40, 7, 2, 100):
+        pc.k = v
+        ref.set_k(v)
+        assert pc.k == ref.k, v
+        got = [lf["k"] for lf in pc.state_dict()["blocks"]]
+        assert got == [b.k for b in ref.blocks], v
+
+
+def test_large_model_presets_run():
+    """The 40B / 125B presets (lazy trigger, gSNR clip, adaptive rank) step."""
+    from scao_b200 import presets
+    gen = torch.Generator().manual_seed(1)
+    for make in (presets.scao_40b, presets.scao_125b):
+        params = [torch.nn.Parameter((torch.randn(s, generator=gen) * 0.02).to(DEV))
+                  for s in [(96, 64), (64,), (128, 96)]]
+        opt = make(params, warmup_steps=3, min_precond_updates=1)
+        for _ in range(8):
+            for q in params:
+                q.grad = (torch.randn(q.shape, generator=gen) * 1e-2).to(DEV)
+            opt.step()
+        torch.cuda.synchronize()
+        opt._plan.check_error()
+        assert all(torch.isfinite(q).all() for q in params)
