@@ -200,6 +200,8 @@ def main():
                          "configuration runs the deterministic path, 0)")
     ap.add_argument("--dynamic-sparsity", action="store_true")
     ap.add_argument("--noise", type=float, default=0.0, help="noise_std_init")
+    ap.add_argument("--buckets", type=int, default=4,
+                    help="N>1: reduce-scatter / step / all-gather pipeline buckets")
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3)
 
@@ -253,7 +255,8 @@ def main():
     torch.cuda.synchronize()
     if world > 1:
         from scao_b200.distributed import ShardedSCAO
-        opt = ShardedSCAO(params, workload, lambda ps: build_opt_list(workload, ps, SCAO))
+        opt = ShardedSCAO(params, workload, lambda ps: build_opt_list(workload, ps, SCAO),
+                          buckets=a.buckets)
     else:
         opt = build_opt(workload, params, SCAO)
 
@@ -354,6 +357,65 @@ def main():
                "note": "grads copied H2D from pinned host memory every step, "
                        "global-norm EMA read back"}
 
+    if world > 1 and a.e2e_steps > 0:
+        # each rank's full gradient list from pinned host memory into the
+        # flat owner layout, then the sharded step; one scalar read back
+        import torch.distributed as dist
+        flat_idx = opt.stage_grads(grad_sets[0])
+        host = opt.grad_sets[flat_idx].cpu().pin_memory()
+        h2d = host.numel() * host.element_size()
+        res = torch.empty(1, dtype=torch.float64).pin_memory()
+        first = next(x for x in opt.inner if x is not None)
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for k in range(a.e2e_steps):
+            opt.cur = opt.grad_sets[flat_idx]
+            opt.cur.copy_(host, non_blocking=True)
+            opt.step()
+            res.copy_(first._plan.global_norm_ema, non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / a.e2e_steps], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e = {"value": round(t.item(), 3), "unit": UNIT,
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 8,
+               "note": "per rank: full gradient list copied H2D from pinned host memory into the "
+                       "owner layout every step, then reduce-scatter / step / all-gather; "
+                       "max over ranks"}
+
+    split = None
+    if world > 1:
+        # communication and computation of the regular step measured apart
+        # (same pipeline with the other half switched off); max over ranks
+        import torch.distributed as dist
+
+        def timed(n):
+            opt.load_grads(grad_sets[0])
+            torch.cuda.synchronize()
+            dist.barrier()
+            t0 = torch.cuda.Event(enable_timing=True)
+            t1 = torch.cuda.Event(enable_timing=True)
+            t0.record(stream)
+            for _ in range(n):
+                opt.step()
+            t1.record(stream)
+            torch.cuda.synchronize()
+            t = torch.tensor([t0.elapsed_time(t1) / n], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return round(t.item(), 3)
+        opt.skip_compute = True
+        comm_ms = timed(3)
+        opt.skip_compute = False
+        opt.skip_comm = True
+        compute_ms = timed(3)
+        opt.skip_comm = False
+        split = {"comm_only_ms": comm_ms, "compute_only_ms": compute_ms,
+                 "note": "3 steps each after the timed region; compute-only steps include "
+                         "curvature steps when the cadence lands on them"}
+
     if rank != 0:
         return
     line = {
@@ -371,6 +433,7 @@ def main():
                      "peak_source": pname},
         "kernels": kern,
         "gpu_launches": int(launches),
+        **({"comm_compute_split": split} if split else {}),
         "clocks": clk,
     }
     if e2e:
