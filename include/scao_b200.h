@@ -199,10 +199,15 @@ typedef struct {
     /* chunk id lists: diagonal-mode params (static); params whose flat pass
      * runs this step (Phase 1, or Phase 2 diagonal); Phase-2 params        */
     const int32_t *diag_list, *flat_list, *p_list;
-    int32_t n_diag, n_flat, n_p, pad2_;
+    int32_t n_diag, n_flat, n_p;
+    int32_t proj_fallback;       /* 1: some Phase-2 bf16 panel needs the
+                                    cp.async projection kernel this step   */
+    int32_t apply_fallback;      /* 1: some Phase-2 tile needs the register-
+                                    streaming apply kernel this step        */
+    int32_t pad4_;
     int32_t* err;                /* device error flag: set to 1 when a bounded
                                     wait on the tensor core timed out       */
-    uint8_t* tmaps;              /* n_params x 2 TMA tensor maps (128 B each,
+    uint8_t* tmaps;              /* n_params x 9 TMA tensor maps (128 B each,
                                     written by scao_plan_tensor_maps and
                                     scao_plan_curvature)                    */
     int32_t tmaps_ok;            /* 1: tmaps describe this step's gradients */

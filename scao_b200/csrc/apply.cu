@@ -647,6 +647,15 @@ __device__ __forceinline__ void apply_prefetch_row(const ScaoPlanDev& P, const S
 #ifndef SCAO_APPLY_MINB
 #define SCAO_APPLY_MINB 3
 #endif
+// tiles the persistent TMA apply kernel takes (bf16, whole 128 x 128 tiles,
+// 16-byte aligned rows, tensor maps valid this step)
+__device__ __forceinline__ bool apply_tma_use(const ScaoPlanDev& P, const ScaoLeaf& L) {
+    const ScaoParam& pr = P.params[L.param];
+    const ScaoParamStep& S = P.step[L.param];
+    return P.tmaps_ok && S.phase == 2 && pr.dtype == SCAO_BF16 && (L.a % 128) == 0 &&
+           (L.b % 128) == 0 && (L.ld % 8) == 0 && (L.col0 % 8) == 0 && scao_tmap_state_ok(pr, S);
+}
+
 // FN: the gradient filter or noise is on this step (a separate
 // instantiation keeps the plain epilogue's register budget).
 template <bool FN>
@@ -656,6 +665,7 @@ apply_kron_tc_kernel(ScaoPlanDev P, int* err) {
     const ScaoLeaf& L = P.leaves[tl.leaf];
     const ScaoParamStep& S = P.step[L.param];
     if (S.phase != 2) return;
+    if (!FN && apply_tma_use(P, L)) return;     // apply_tma_kernel
     const ScaoParam& pr = P.params[L.param];
     const int dt = pr.dtype;
     const int Kp = (L.kpad + 15) & ~15;
@@ -893,7 +903,7 @@ proj_tma_kernel(ScaoPlanDev P, int* err) {
                 if (!proj_tma_use(P, L)) continue;
                 const int Kp = (L.kpad + 15) & ~15;
                 const uint32_t bb = (uint32_t)Kp * 64 * 2;
-                const void* map = P.tmaps + (size_t)L.param * 2 * 128;
+                const void* map = scao_tmap(P.tmaps, L.param, TM_G128);
                 for (int kb = 0; kb < L.b / 64; ++kb) {
                     if (!mbar_wait(&empty[stage], ph ^ 1)) { abort_flag = 1; atomicExch(err, 2); break; }
                     mbar_expect_tx(&full[stage], 128 * 64 * 2 + 2 * bb);
@@ -1031,6 +1041,249 @@ proj_tma_kernel(ScaoPlanDev P, int* err) {
                         if (a0 + i < kp && b0 + j < kp) out[(a0 + i) * kp + b0 + j] = accv[i][j];
             }
         }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tc_dealloc(tmem, 256);
+}
+
+// ---------------------------------------------------------------------------
+// Persistent apply for bf16 parameters (Phase 2, filter and noise off): the
+// Kronecker correction of a 128 x 128 tile on the tensor core, and the
+// Adan / blend / weight-decay epilogue streaming the tile's gradient,
+// parameter and four fp32 moments through shared memory by TMA tensor
+// copies in 16-row chunks; the moments and the rounded update go back by
+// TMA tensor stores from the same buffers.
+//   warp 0      state producer: 6 tensor loads per chunk into a stage ring
+//   warp 1      TMEM owner + operand loads (bulk) + MMA issuer, two
+//               accumulators (corr^T: lane j, column i)
+//   warps 2-9   epilogue: thread = tile column j (its TMEM lane), half the
+//               rows of each chunk; an elected thread issues the stores
+// ---------------------------------------------------------------------------
+#ifndef SCAO_APPLY_EPI
+#define SCAO_APPLY_EPI 512
+#endif
+constexpr int AT_EPI = SCAO_APPLY_EPI;          // epilogue threads (256 or 512)
+constexpr int AT_THREADS = 64 + AT_EPI;
+#ifndef SCAO_APPLY_ST
+#define SCAO_APPLY_ST 3
+#endif
+constexpr int AT_MAXST = 4;
+constexpr int AT_R = TMA_STATE_ROWS;                   // rows per chunk (16)
+constexpr int AT_RPT = AT_R * 128 / AT_EPI;           // rows per thread per chunk
+constexpr uint32_t AT_G = 0, AT_P = AT_R * 128 * 2, AT_M = 2 * AT_R * 128 * 2;
+constexpr uint32_t AT_V = AT_M + AT_R * 128 * 4, AT_D = AT_V + AT_R * 128 * 4;
+constexpr uint32_t AT_PV = AT_D + AT_R * 128 * 4;
+constexpr uint32_t AT_STAGE = AT_PV + AT_R * 128 * 4;  // 40 KB
+
+
+__host__ __device__ inline int apply_tma_stages(int kpm) { return kpm > 64 ? 2 : SCAO_APPLY_ST; }
+__host__ __device__ inline uint32_t apply_tma_ops_bytes(int kpm) { return 4u * 128 * kpm * 2; }
+size_t apply_tma_smem(int kpad_max) {
+    const int Kp = (kpad_max + 15) & ~15;
+    return (size_t)apply_tma_ops_bytes(Kp) + (size_t)apply_tma_stages(Kp) * AT_STAGE + 1024;
+}
+
+__global__ void __launch_bounds__(AT_THREADS, 1)
+apply_tma_kernel(ScaoPlanDev P, int* err) {
+    extern __shared__ unsigned char asm_raw[];
+    unsigned char* sm = (unsigned char*)(((uintptr_t)asm_raw + 1023) & ~(uintptr_t)1023);
+    const int Kpm = (P.kpad_max + 15) & ~15;
+    const int nst = apply_tma_stages(Kpm);
+    unsigned char* ops = sm;                                  // [A hi|lo][B hi|lo]
+    unsigned char* stg = sm + apply_tma_ops_bytes(Kpm);
+    __shared__ uint64_t full[AT_MAXST], empty[AT_MAXST], accf[2], acce[2], opfull, opfree, fin;
+    __shared__ uint32_t tslot;
+    __shared__ volatile int abort_flag, ep_go;
+    __shared__ float red[AT_EPI / 32][3];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {
+        for (int i = 0; i < AT_MAXST; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
+        for (int i = 0; i < 2; ++i) { mbar_init(&accf[i], 1); mbar_init(&acce[i], AT_EPI); }
+        mbar_init(&opfull, 1);
+        mbar_init(&opfree, 1);
+        mbar_init(&fin, 1);
+        abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) tc_alloc(&tslot, 256);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tslot;
+    const int total = P.n_tiles;
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- state producer ----------------
+            int stage = 0;
+            uint32_t ph = 0, issued = 0, last_ph = 0;
+            constexpr int NCH = 128 / AT_R;
+            for (int T = blockIdx.x; T < total && !abort_flag; T += gridDim.x) {
+                const ScaoTile tl = P.tiles[T];
+                const ScaoLeaf& L = P.leaves[tl.leaf];
+                if (!apply_tma_use(P, L)) continue;
+                const int x = L.col0 + tl.col0;
+                for (int c = 0; c < NCH; ++c) {
+                    if (!mbar_wait(&empty[stage], ph ^ 1)) { abort_flag = 1; atomicExch(err, 2); break; }
+                    const int y = L.row0 + tl.row0 + c * AT_R;
+                    mbar_expect_tx(&full[stage], AT_STAGE);
+                    const uint32_t s = smem_u32(stg + (size_t)stage * AT_STAGE);
+                    tma_load_2d(s + AT_G, scao_tmap(P.tmaps, L.param, TM_GS), x, y, &full[stage]);
+                    tma_load_2d(s + AT_P, scao_tmap(P.tmaps, L.param, TM_PS), x, y, &full[stage]);
+                    tma_load_2d(s + AT_M, scao_tmap(P.tmaps, L.param, TM_M), x, y, &full[stage]);
+                    tma_load_2d(s + AT_V, scao_tmap(P.tmaps, L.param, TM_V), x, y, &full[stage]);
+                    tma_load_2d(s + AT_D, scao_tmap(P.tmaps, L.param, TM_D), x, y, &full[stage]);
+                    tma_load_2d(s + AT_PV, scao_tmap(P.tmaps, L.param, TM_PV), x, y, &full[stage]);
+                    issued |= 1u << stage;
+                    last_ph = (last_ph & ~(1u << stage)) | (ph << stage);
+                    if (++stage == nst) { stage = 0; ph ^= 1; }
+                }
+            }
+            for (int s2 = 0; s2 < nst; ++s2)
+                if ((issued >> s2) & 1u)
+                    if (!mbar_wait(&full[s2], (last_ph >> s2) & 1u)) atomicExch(err, 2);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- operands + MMA ----------------
+            int acc = 0;
+            uint32_t aph = 0, opph = 0, ofph = 0;
+            bool any = false;
+            const uint32_t tbm = 128u * Kpm * 2;
+            for (int T = blockIdx.x; T < total && !abort_flag; T += gridDim.x) {
+                const ScaoTile tl = P.tiles[T];
+                const ScaoLeaf& L = P.leaves[tl.leaf];
+                if (!apply_tma_use(P, L)) continue;
+                const int Kp = (L.kpad + 15) & ~15;
+                const uint32_t tb = 128u * Kp * 2;
+                if (any) {               // the previous tile's MMAs have read the operands
+                    if (!mbar_wait(&opfree, opph)) { abort_flag = 1; atomicExch(err, 2); break; }
+                    opph ^= 1;
+                }
+                any = true;
+                unsigned char* A = ops;                  // U_r rows j0.. [hi][lo]
+                unsigned char* B = ops + 2 * tbm;        // W rows i0..   [hi][lo]
+                mbar_expect_tx(&opfull, 4 * tb);
+                bulk_g2s(A, P.ua + L.ua_off + (int64_t)(tl.col0 / 128) * 2 * tb, 2 * tb, &opfull);
+                bulk_g2s(B, P.wa + L.wa_off + (int64_t)(tl.row0 / 128) * 2 * tb, 2 * tb, &opfull);
+                if (!mbar_wait(&opfull, ofph)) { abort_flag = 1; atomicExch(err, 2); break; }
+                ofph ^= 1;
+                if (!mbar_wait(&acce[acc], aph ^ 1)) { abort_flag = 1; atomicExch(err, 2); break; }
+                tc_fence_after();
+                const uint32_t d = tmem + acc * 128;
+                const uint32_t idesc = idesc_bf16(128, 128);
+                const uint32_t sbo = 16 * Kp;
+                const uint32_t a0 = smem_u32(A), b0 = smem_u32(B);
+                for (int s = 0; s < Kp / 16; ++s) {
+                    const uint64_t ah = smem_desc(a0 + s * 256, 128, sbo);
+                    const uint64_t al = smem_desc(a0 + tb + s * 256, 128, sbo);
+                    const uint64_t bh = smem_desc(b0 + s * 256, 128, sbo);
+                    const uint64_t bl = smem_desc(b0 + tb + s * 256, 128, sbo);
+                    tc_mma_bf16(d, ah, bh, idesc, s > 0 ? 1u : 0u);
+                    tc_mma_bf16(d, ah, bl, idesc, 1u);
+                    tc_mma_bf16(d, al, bh, idesc, 1u);
+                }
+                tc_commit(&accf[acc]);
+                tc_commit(&opfree);
+                acc ^= 1;
+                if (acc == 0) aph ^= 1;
+            }
+            tc_commit(&fin);
+            if (!mbar_wait(&fin, 0)) atomicExch(err, 2);
+        }
+    } else {
+        // ---------------- epilogue ----------------
+        const int et = tid - 64;
+        const int ew = warp - 2;                  // epilogue warp
+        const int q = warp & 3;                   // TMEM lane quarter -> columns 32q..
+        const int h = ew >> 2;                    // row group of each chunk
+        const int j = q * 32 + lane;              // tile column of this thread
+        int acc = 0, stage = 0;
+        uint32_t aph = 0, ph = 0;
+        for (int T = blockIdx.x; T < total; T += gridDim.x) {
+            const ScaoTile tl = P.tiles[T];
+            const ScaoLeaf& L = P.leaves[tl.leaf];
+            if (!apply_tma_use(P, L)) continue;
+            if (et == 0) ep_go = !abort_flag;
+            named_bar(1, AT_EPI);
+            if (!ep_go) break;
+            const ScaoParamStep& S = P.step[L.param];
+            const float* ps = P.param_scalars + L.param * 8;
+            const bool clip = ps[PS_CLIP] != 0.f;
+            const float clipmul = ps[PS_CLIPMUL];
+            const float wdm = S.wd_mult;
+            const int x = L.col0 + tl.col0;
+            bool ok = __all_sync(0xffffffffu, mbar_wait(&accf[acc], aph));
+            if (ok) tc_fence_after();
+            float usq = 0.f, gsq = 0.f, psq = 0.f;
+            for (int c = 0; c < 128 / AT_R; ++c) {
+                const bool okc = ok && __all_sync(0xffffffffu, mbar_wait(&full[stage], ph));
+                if (!okc) { abort_flag = 1; atomicExch(err, 2); }
+                unsigned char* st = stg + (size_t)stage * AT_STAGE;
+                if (okc) {
+                    float corr[AT_RPT];
+                    if (AT_RPT == 8) tc_ld8(tmem + acc * 128 + ((uint32_t)(q * 32) << 16) + c * AT_R + h * 8, corr);
+                    else tc_ld4(tmem + acc * 128 + ((uint32_t)(q * 32) << 16) + c * AT_R + h * 4, corr);
+                    uint16_t* gs = (uint16_t*)(st + AT_G);
+                    const uint16_t* pps = (const uint16_t*)(st + AT_P);
+                    float* ms = (float*)(st + AT_M);
+                    float* vs = (float*)(st + AT_V);
+                    float* ds = (float*)(st + AT_D);
+                    float* qs = (float*)(st + AT_PV);
+#pragma unroll
+                    for (int rr = 0; rr < AT_RPT; ++rr) {
+                        const int o = (h * AT_RPT + rr) * 128 + j;
+                        const float gv = bf16_bits_to_f(gs[o]);
+                        const float pv = bf16_bits_to_f(pps[o]);
+                        float mv = ms[o], vv = vs[o], dv = ds[o], qv = qs[o];
+                        const float gp = round_dt(fadd(gv, corr[rr]), SCAO_BF16);
+                        const float u = adan_elem(S, SCAO_BF16, gv, gp, mv, vv, dv, qv, clip, clipmul);
+                        usq = fmaf(u, u, usq);
+                        gsq = fmaf(gv, gv, gsq);
+                        const float pd = round_dt(fmul(pv, wdm), SCAO_BF16);
+                        psq = fmaf(pd, pd, psq);
+                        ms[o] = mv; vs[o] = vv; ds[o] = dv; qs[o] = qv;
+                        gs[o] = f_to_bf16_bits(u);
+                    }
+                }
+                fence_async_smem();
+                named_bar(1, AT_EPI);
+                if (et == 0) {
+                    if (okc) {
+                        const int y = L.row0 + tl.row0 + c * AT_R;
+                        const uint32_t s = smem_u32(st);
+                        tma_store_2d(scao_tmap(P.tmaps, L.param, TM_US), x, y, s + AT_G);
+                        tma_store_2d(scao_tmap(P.tmaps, L.param, TM_M), x, y, s + AT_M);
+                        tma_store_2d(scao_tmap(P.tmaps, L.param, TM_V), x, y, s + AT_V);
+                        tma_store_2d(scao_tmap(P.tmaps, L.param, TM_D), x, y, s + AT_D);
+                        tma_store_2d(scao_tmap(P.tmaps, L.param, TM_PV), x, y, s + AT_PV);
+                        bulk_commit();
+                        bulk_wait_read0();
+                    }
+                    mbar_arrive(&empty[stage]);
+                }
+                if (++stage == nst) { stage = 0; ph ^= 1; }
+            }
+            tc_fence_before();
+            mbar_arrive(&acce[acc]);
+            acc ^= 1;
+            if (acc == 0) aph ^= 1;
+            // per-tile sums (usq, gsq, psq) -> tile_part
+            usq = warp_sum(usq);
+            gsq = warp_sum(gsq);
+            psq = warp_sum(psq);
+            if (lane == 0) { red[ew][0] = usq; red[ew][1] = gsq; red[ew][2] = psq; }
+            named_bar(1, AT_EPI);
+            if (et == 0) {
+                float a = 0.f, b = 0.f, cc = 0.f;
+                for (int w = 0; w < AT_EPI / 32; ++w) { a += red[w][0]; b += red[w][1]; cc += red[w][2]; }
+                P.tile_part[T * 4 + 0] = a;
+                P.tile_part[T * 4 + 1] = b;
+                P.tile_part[T * 4 + 2] = cc;
+            }
+        }
+        if (et == 0) bulk_wait0();
     }
     tc_fence_before();
     __syncthreads();
@@ -1394,7 +1647,8 @@ extern "C" int scao_plan_step(const ScaoPlanDev* P, void* stream) {
         }
         SCAO_CHECK_LAUNCH();
         { ProfScope _ps(SLOT_PROJ, st);
-          proj_bf16_kernel<<<P->n_panels, 128, proj_bf16_smem(P->kpad_max), st>>>(*P, P->err);
+          if (!P->tmaps_ok || P->proj_fallback)
+              proj_bf16_kernel<<<P->n_panels, 128, proj_bf16_smem(P->kpad_max), st>>>(*P, P->err);
           if (P->kron_dtypes & ~(1 << SCAO_BF16))
               proj_tc_kernel<<<P->n_panels, 128, proj_tc_smem(P->kpad_max), st>>>(*P, P->err); }
         SCAO_CHECK_LAUNCH();
@@ -1431,8 +1685,22 @@ extern "C" int scao_plan_step(const ScaoPlanDev* P, void* stream) {
     SCAO_CHECK_LAUNCH();
     if (P->n_tiles > 0) {
         { ProfScope _ps(SLOT_APPLY_KRON, st);
-          if (fn) apply_kron_tc_kernel<true><<<P->n_tiles, SCAO_APPLY_NT, apply_tc_smem(P->kpad_max), st>>>(*P, P->err);
-          else apply_kron_tc_kernel<false><<<P->n_tiles, SCAO_APPLY_NT, apply_tc_smem(P->kpad_max), st>>>(*P, P->err); }
+          if (fn) {
+              apply_kron_tc_kernel<true><<<P->n_tiles, SCAO_APPLY_NT, apply_tc_smem(P->kpad_max), st>>>(*P, P->err);
+          } else {
+              if (P->tmaps_ok) {
+                  static bool aattr = false;
+                  if (!aattr) {
+                      cudaFuncSetAttribute(apply_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)apply_tma_smem(128));
+                      aattr = true;
+                  }
+                  const int g = P->n_tiles < scao_sm_count() ? P->n_tiles : scao_sm_count();
+                  apply_tma_kernel<<<g, AT_THREADS, apply_tma_smem(P->kpad_max), st>>>(*P, P->err);
+              }
+              if (!P->tmaps_ok || P->apply_fallback)
+                  apply_kron_tc_kernel<false><<<P->n_tiles, SCAO_APPLY_NT, apply_tc_smem(P->kpad_max), st>>>(*P, P->err);
+          } }
         SCAO_CHECK_LAUNCH();
     }
     if (P->n_chunks > 0) {

@@ -376,7 +376,7 @@ gram_tma_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, int nprob, int t
             GTile w;
             for (int T = blockIdx.x; T < total && !abort_flag; T += gridDim.x) {
                 if (!gram_tile(P, ids, tpp, T, w)) continue;
-                const void* map = maps + ((size_t)w.param * 2 + w.side) * 128;
+                const void* map = scao_tmap(maps, w.param, w.side ? TM_G64 : TM_G128);
                 const int i0 = w.ti * 128, j0 = w.tc * GN;
                 const int x0 = (int)w.col0, y0 = (int)w.row0;
                 for (int kb = 0; kb < w.K / 64; ++kb) {

@@ -37,22 +37,37 @@ bool scao_build_tensor_maps(const ScaoPlanDev* P, const ScaoParam* ph, const Sca
     static_assert(sizeof(CUtensorMap) == 128, "tensor map size");
     EncodeTiledFn enc = encode_fn();
     if (!enc || !P->tmaps) return false;
-    std::vector<CUtensorMap> maps((size_t)P->n_params * 2);
+    std::vector<CUtensorMap> maps((size_t)P->n_params * TMA_PER_PARAM);
     memset(maps.data(), 0, maps.size() * sizeof(CUtensorMap));
+    auto encode = [&](CUtensorMap* m, CUtensorMapDataType t, int es, const void* base, int64_t rows,
+                      int64_t cols, cuuint32_t bx, cuuint32_t by, CUtensorMapSwizzle sw) {
+        const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+        const cuuint64_t strides[1] = {(cuuint64_t)cols * es};
+        const cuuint32_t box[2] = {bx, by};
+        const cuuint32_t estr[2] = {1, 1};
+        return enc(m, t, 2, (void*)base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+               CUDA_SUCCESS;
+    };
+    const auto BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, F4 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    const auto SW = CU_TENSOR_MAP_SWIZZLE_128B, NS = CU_TENSOR_MAP_SWIZZLE_NONE;
+    const cuuint32_t SR = TMA_STATE_ROWS;
     for (int i = 0; i < P->n_params; ++i) {
         if (!scao_tmap_ok(ph[i], sh[i])) continue;
-        const cuuint64_t dims[2] = {(cuuint64_t)ph[i].cols, (cuuint64_t)ph[i].rows};
-        const cuuint64_t strides[1] = {(cuuint64_t)ph[i].cols * 2};
-        const cuuint32_t es[2] = {1, 1};
-        const cuuint32_t box0[2] = {64, 128}, box1[2] = {64, 64};
-        if (enc(&maps[2 * i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void*)sh[i].g_ptr, dims,
-                strides, box0, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-            return false;
-        if (enc(&maps[2 * i + 1], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void*)sh[i].g_ptr, dims,
-                strides, box1, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-            return false;
+        CUtensorMap* m = &maps[(size_t)i * TMA_PER_PARAM];
+        const int64_t r = ph[i].rows, c = ph[i].cols;
+        const void* g = (const void*)sh[i].g_ptr;
+        if (!encode(m + TM_G128, BF, 2, g, r, c, 64, 128, SW)) return false;
+        if (!encode(m + TM_G64, BF, 2, g, r, c, 64, 64, SW)) return false;
+        if (!encode(m + TM_GS, BF, 2, g, r, c, 128, SR, NS)) return false;
+        if (!scao_tmap_state_ok(ph[i], sh[i])) continue;
+        const int64_t o = ph[i].offset;
+        if (!encode(m + TM_PS, BF, 2, (const void*)sh[i].p_ptr, r, c, 128, SR, NS)) return false;
+        if (!encode(m + TM_US, BF, 2, P->upd + o, r, c, 128, SR, NS)) return false;
+        if (!encode(m + TM_M, F4, 4, P->exp_avg + o, r, c, 128, SR, NS)) return false;
+        if (!encode(m + TM_V, F4, 4, P->exp_avg_sq + o, r, c, 128, SR, NS)) return false;
+        if (!encode(m + TM_D, F4, 4, P->exp_avg_diff + o, r, c, 128, SR, NS)) return false;
+        if (!encode(m + TM_PV, F4, 4, P->prev_grad + o, r, c, 128, SR, NS)) return false;
     }
     // pageable source: the copy is staged before cudaMemcpyAsync returns
     return cudaMemcpyAsync(P->tmaps, maps.data(), maps.size() * sizeof(CUtensorMap),

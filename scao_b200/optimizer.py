@@ -373,7 +373,7 @@ class SCAO(Optimizer):
         stream = torch.cuda.current_stream(dev)
         sp = C_stream(stream)
         if k_changed:
-            plan.k.copy_(torch.from_numpy(kvec).to(dev))
+            plan.upload_k(kvec)
         plan.t_step.copy_(plan.step_host, non_blocking=True)
         plan.step_event = torch.cuda.Event()
         plan.step_event.record(stream)
@@ -382,7 +382,7 @@ class SCAO(Optimizer):
         pd = ctypes.byref(dptr)
         for rho, leaves in curv_leaves.items():
             ids_h = np.ascontiguousarray(leaves, dtype=np.int32)
-            ids = torch.from_numpy(ids_h).to(dev)
+            ids = plan.dev_ids(ids_h)
             ma, mb, _ = plan.max_dims(leaves)
             need = L.scao_ema_scratch_bytes(len(leaves), ma, mb)
             scratch = self._get_ema_scratch(need)
@@ -393,14 +393,14 @@ class SCAO(Optimizer):
                        "scao_plan_curvature")
             keep.append(ids)
         for rho, pids in curv_diag.items():
-            ids = torch.tensor(pids, dtype=torch.int32, device=dev)
+            ids = plan.dev_ids(np.ascontiguousarray(pids, dtype=np.int32))
             _lib.check(L.scao_plan_curvature_diag(pd, ids.data_ptr(), len(pids), rho, sp),
                        "scao_plan_curvature_diag")
             keep.append(ids)
         if eig_leaves:
-            ids = torch.tensor(eig_leaves, dtype=torch.int32, device=dev)
-            bias = plan.t_bias
-            bias[ids.long()] = torch.tensor(eig_bias, dtype=torch.float32, device=dev)
+            eig_h = np.ascontiguousarray(eig_leaves, dtype=np.int32)
+            ids = plan.dev_ids(eig_h)
+            bias = plan.upload_bias(eig_h, eig_bias)
             ma, mb, smax = plan.max_dims(eig_leaves)
             status = plan.eig_status[: 2 * len(eig_leaves)]
             _lib.check(L.scao_plan_eigen(pd, ids.data_ptr(), len(eig_leaves), bias.data_ptr(),
@@ -413,7 +413,7 @@ class SCAO(Optimizer):
         if plan.has_bf16_kron and os.environ.get("SCAO_NO_TMA") != "1":
             # tensor maps of the gradients (rebuilt only when a pointer or
             # phase changed)
-            key = (tab["g_ptr"].tobytes(), tab["phase"].tobytes())
+            key = (tab["g_ptr"].tobytes(), tab["p_ptr"].tobytes(), tab["phase"].tobytes())
             if key != plan.tmap_key:
                 rc = L.scao_plan_tensor_maps(pd, plan.ptab.ctypes.data, plan.step_host.data_ptr(), sp)
                 plan.dev.tmaps_ok = 1 if rc == 0 else 0
@@ -421,6 +421,13 @@ class SCAO(Optimizer):
         else:
             plan.dev.tmaps_ok = 0
             plan.tmap_key = None
+        if plan.n_leaves:
+            # the cp.async projection runs only for Phase-2 leaves the TMA one cannot take
+            ph = tab["phase"][plan.leaf_param]
+            al = (tab["g_ptr"][plan.leaf_param] % 16) == 0
+            plan.dev.proj_fallback = int(bool(np.any((ph == 2) & ~(plan.leaf_tma_shape & al))))
+            alp = al & ((tab["p_ptr"][plan.leaf_param] % 16) == 0)
+            plan.dev.apply_fallback = int(bool(np.any((ph == 2) & ~(plan.leaf_tma_apply & alp))))
         f = plan.dev.filt
         f.noise_on = 1 if self._noise_std > 1e-9 else 0     # optimizer.py:544
         f.noise_std = float(np.float32(self._noise_std))

@@ -186,7 +186,7 @@ class Plan:
             for c0 in range(0, numel, CHUNK):
                 chunks.append((i, 0, c0, min(numel, c0 + CHUNK)))
             r["chunk_end"] = len(chunks)
-            off += _round_up(numel, 4)
+            off += _round_up(numel, 8)     # 16-byte aligned in the bf16 arenas too
         self.numel_total = off
         self.ptab = ptab
         self.ltab = np.array(leaves, LEAF_DT) if leaves else np.zeros(0, LEAF_DT)
@@ -246,8 +246,21 @@ class Plan:
         self.param_scalars = z(self.n_params * 8)
         self.global_norm_ema = torch.ones(1, dtype=torch.float64, device=dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
-        self.tmaps = torch.zeros(self.n_params * 256, dtype=torch.uint8, device=dev)
+        self.tmaps = torch.zeros(self.n_params * 9 * 128, dtype=torch.uint8, device=dev)
         self.tmap_key = None
+        # leaves whose panels the TMA projection can take (static part of its
+        # test: bf16, 16-byte aligned rows and block origin, 64-multiple width)
+        self.leaf_tma_shape = np.array(
+            [int(self.ptab[int(L["param"])]["dtype"]) == DTYPE_CODE[torch.bfloat16] and
+             int(L["ld"]) % 8 == 0 and int(L["col0"]) % 8 == 0 and int(L["b"]) % 64 == 0
+             for L in self.ltab], dtype=bool) if self.n_leaves else np.zeros(0, bool)
+        self.leaf_param = self.ltab["param"].astype(np.int64) if self.n_leaves else np.zeros(0, np.int64)
+        # ... and whose tiles the TMA apply can take (whole 128 x 128 tiles)
+        self.leaf_tma_apply = np.array(
+            [int(self.ptab[int(L["param"])]["dtype"]) == DTYPE_CODE[torch.bfloat16] and
+             int(L["ld"]) % 8 == 0 and int(L["col0"]) % 8 == 0 and int(L["a"]) % 128 == 0 and
+             int(L["b"]) % 128 == 0 and int(self.ptab[int(L["param"])]["offset"]) % 8 == 0
+             for L in self.ltab], dtype=bool) if self.n_leaves else np.zeros(0, bool)
         self.has_bf16_kron = any(int(r["mode"]) == 1 and int(r["dtype"]) == DTYPE_CODE[torch.bfloat16]
                                  for r in self.ptab)
         self.counters = z(16, torch.int32)
@@ -270,6 +283,8 @@ class Plan:
         self.t_eps_sparse = torch.tensor(self.eps_sparse or [0.0], dtype=torch.float32,
                                          device=dev)
         self.t_bias = torch.zeros(max(self.n_leaves, 1), dtype=torch.float32, device=dev)
+        self.t_bias_host = np.zeros(self.n_leaves, np.float32)
+        self._ids_cache = {}
         self._init_factors()
         self.dev = PlanDev_from(self)
         if self.n_leaves and self.device.type == "cuda":
@@ -369,6 +384,49 @@ class Plan:
         if not self.dev.filt.mode:
             return None
         return self.t_fp.cpu().numpy().view(_lib.FILTER_PARAM_DT)
+
+    # host -> device uploads without a stream synchronisation -------------
+    def dev_ids(self, ids_h):
+        """Device copy of an int32 id list, cached by content (the lists a
+        step uses repeat with the curvature cadence)."""
+        key = ids_h.tobytes()
+        t = self._ids_cache.get(key)
+        if t is None:
+            t = torch.from_numpy(ids_h.copy()).to(self.device)
+            self._ids_cache[key] = t
+        return t
+
+    def _pinned(self, name, n, dtype):
+        buf = getattr(self, name, None)
+        ev = getattr(self, name + "_ev", None)
+        if ev is not None:
+            ev.synchronize()            # the previous upload has left the buffer
+        if buf is None or buf.numel() < n:
+            buf = torch.zeros(max(n, 1), dtype=dtype, pin_memory=torch.cuda.is_available())
+            setattr(self, name, buf)
+        return buf
+
+    def _mark(self, name):
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self.device))
+        setattr(self, name + "_ev", ev)
+
+    def upload_bias(self, leaf_ids, values):
+        """t_bias[leaf_ids] = values, from pinned memory, stream-ordered."""
+        buf = self._pinned("_bias_pin", self.n_leaves, torch.float32)
+        arr = buf.numpy()
+        arr[:self.n_leaves] = self.t_bias_host
+        arr[leaf_ids] = np.asarray(values, np.float32)
+        self.t_bias_host[:] = arr[:self.n_leaves]
+        self.t_bias[:self.n_leaves].copy_(buf[:self.n_leaves], non_blocking=True)
+        self._mark("_bias_pin")
+        return self.t_bias
+
+    def upload_k(self, kvec):
+        buf = self._pinned("_k_pin_up", self.n_leaves, torch.int32)
+        buf.numpy()[:self.n_leaves] = kvec
+        self.k.copy_(buf[:self.n_leaves], non_blocking=True)
+        self._mark("_k_pin_up")
 
     def check_error(self):
         """Raise if a kernel recorded a timed-out wait (synchronises)."""
