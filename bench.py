@@ -202,6 +202,8 @@ def main():
     ap.add_argument("--noise", type=float, default=0.0, help="noise_std_init")
     ap.add_argument("--buckets", type=int, default=4,
                     help="N>1: reduce-scatter / step / all-gather pipeline buckets")
+    ap.add_argument("--sm-reserve", type=int, default=32,
+                    help="N>1: SMs the persistent kernels leave to the collectives")
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3)
 
@@ -256,7 +258,7 @@ def main():
     if world > 1:
         from scao_b200.distributed import ShardedSCAO
         opt = ShardedSCAO(params, workload, lambda ps: build_opt_list(workload, ps, SCAO),
-                          buckets=a.buckets)
+                          buckets=a.buckets, sm_reserve=a.sm_reserve)
     else:
         opt = build_opt(workload, params, SCAO)
 

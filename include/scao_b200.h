@@ -204,7 +204,8 @@ typedef struct {
                                     cp.async projection kernel this step   */
     int32_t apply_fallback;      /* 1: some Phase-2 tile needs the register-
                                     streaming apply kernel this step        */
-    int32_t pad4_;
+    int32_t sm_reserve;          /* SMs the persistent kernels leave free
+                                    (for concurrent collectives)            */
     int32_t* err;                /* device error flag: set to 1 when a bounded
                                     wait on the tensor core timed out       */
     uint8_t* tmaps;              /* n_params x 9 TMA tensor maps (128 B each,

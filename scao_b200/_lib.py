@@ -84,7 +84,7 @@ class PlanDev(C.Structure):
         ("global_norm_ema", _P), ("slow", _P), ("slow32", _P), ("ua", _P), ("ut", _P), ("wa", _P), ("counters", _P),
         ("diag_list", _P), ("flat_list", _P), ("p_list", _P),
         ("n_diag", C.c_int32), ("n_flat", C.c_int32), ("n_p", C.c_int32), ("proj_fallback", C.c_int32),
-        ("apply_fallback", C.c_int32), ("pad4_", C.c_int32),
+        ("apply_fallback", C.c_int32), ("sm_reserve", C.c_int32),
         ("err", _P),
         ("tmaps", _P), ("tmaps_ok", C.c_int32), ("gnorm_host", C.c_int32),
         ("filt", FilterDev),

@@ -1641,7 +1641,7 @@ extern "C" int scao_plan_step(const ScaoPlanDev* P, void* stream) {
                                      (int)proj_tma_smem(128));
                 tattr = true;
             }
-            const int g = P->n_panels < scao_sm_count() ? P->n_panels : scao_sm_count();
+            const int g = scao_persistent_grid(P, P->n_panels);
             ProfScope _ps(SLOT_PROJ, st);
             proj_tma_kernel<<<g, PT_THREADS, proj_tma_smem(P->kpad_max), st>>>(*P, P->err);
         }
@@ -1695,7 +1695,7 @@ extern "C" int scao_plan_step(const ScaoPlanDev* P, void* stream) {
                                            (int)apply_tma_smem(128));
                       aattr = true;
                   }
-                  const int g = P->n_tiles < scao_sm_count() ? P->n_tiles : scao_sm_count();
+                  const int g = scao_persistent_grid(P, P->n_tiles);
                   apply_tma_kernel<<<g, AT_THREADS, apply_tma_smem(P->kpad_max), st>>>(*P, P->err);
               }
               if (!P->tmaps_ok || P->apply_fallback)

@@ -833,7 +833,7 @@ extern "C" int scao_plan_curvature(const ScaoPlanDev* P, const int32_t* leaf_ids
                 tattr = true;
             }
             const int64_t work = (int64_t)np * tpp;
-            const int g = (int)(work < scao_sm_count() ? work : scao_sm_count());
+            const int g = scao_persistent_grid(P, work);
             ProfScope _ps(SLOT_GRAM_TC, st);
             gram_tma_kernel<<<g, GTHREADS, gram_tma_smem(), st>>>(*P, ids, np, tpp, xbuf, xstride,
                                                                   amnew, rho_f, alpha_f, P->err);

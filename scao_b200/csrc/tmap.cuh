@@ -38,3 +38,10 @@ __host__ __device__ inline const void* scao_tmap(const uint8_t* base, int param,
 }
 
 int scao_sm_count();
+
+// persistent-kernel grid: SMs minus the plan's reservation, at most `work`
+inline int scao_persistent_grid(const ScaoPlanDev* P, long long work) {
+    int n = scao_sm_count() - (P->sm_reserve > 0 ? P->sm_reserve : 0);
+    if (n < 1) n = 1;
+    return (int)(work < n ? work : n);
+}

@@ -96,7 +96,7 @@ class ShardedSCAO:
     arrived, and its all-gather is queued right after its step."""
 
     def __init__(self, params, workload, make_inner, group=None, costs=None, buckets=4,
-                 comm_priority=True):
+                 comm_priority=True, sm_reserve=32):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -123,6 +123,10 @@ class ShardedSCAO:
             mine = [i for i in self.my if lay.bucket[i] == b]
             self.inner.append(make_inner([(self.params[i], self.specs[i]) for i in mine])
                               if mine else None)
+        # the step's persistent kernels leave SMs to the concurrent NCCL kernels
+        for opt in self.inner:
+            if opt is not None and hasattr(opt, "_sm_reserve"):
+                opt._sm_reserve = sm_reserve if dist.get_backend(group) == "nccl" else 0
         self.global_step = 0
         self.grad_sets = []
         self.cur = None

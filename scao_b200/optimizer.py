@@ -175,6 +175,7 @@ class SCAO(Optimizer):
         # the host then keeps the global grad-norm EMA as well
         self._host_norms = self._adaptive_warmup or self._lazy_precond or self._adaptive_rank
         self._gema = 1.0
+        self._sm_reserve = 0     # SMs the persistent kernels leave to concurrent collectives
         self._in_warmup_global = True
         self._eig_max_iters = int(eig_max_iters)
         self._eig_tol = float(eig_tol)
@@ -214,6 +215,7 @@ class SCAO(Optimizer):
         f.gsnr_on = 1 if self._use_gsnr_clip else 0          # R4
         f.gsnr_thr = float(np.float32(self._gsnr_threshold))
         self._plan.dev.gnorm_host = 1 if self._host_norms else 0
+        self._plan.dev.sm_reserve = int(self._sm_reserve)
         self._plan.gnorm_dev = torch.zeros(len(ps), dtype=torch.float32, device=dev)
         self._plan.gnorm_pin = torch.zeros(len(ps), dtype=torch.float32,
                                            pin_memory=torch.cuda.is_available())
