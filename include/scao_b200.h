@@ -78,7 +78,8 @@ typedef struct {
     float tau;
     float lars;
     float diag_bias;       /* float(max(1 - rho**precond_step, 1e-8))       */
-    float rbc1, rbc2, rbc3;/* reciprocals of bc1..bc3 (division by constant) */
+    float rbc1, rbc2, rbc3;/* reciprocals of bc1..bc3 (division by constant);
+                              Phase 1: rbc2 = 1 / sqrt_bc2               */
 } ScaoParamStep;
 
 /* One per Kronecker leaf block (static).  Each leaf owns two symmetric
@@ -206,6 +207,12 @@ typedef struct {
                                     streaming apply kernel this step        */
     int32_t sm_reserve;          /* SMs the persistent kernels leave free
                                     (for concurrent collectives)            */
+    int32_t la_fused;            /* 1: this step's lookahead of Phase-2 params
+                                    runs inside the parameter write (then
+                                    scao_plan_lookahead skips them)         */
+    int32_t la_init;             /* 1: first lookahead (slow <- p)          */
+    float la_alpha;              /* lookahead_alpha                         */
+    int32_t pad5_;
     int32_t* err;                /* device error flag: set to 1 when a bounded
                                     wait on the tensor core timed out       */
     uint8_t* tmaps;              /* n_params x 9 TMA tensor maps (128 B each,

@@ -85,6 +85,8 @@ class PlanDev(C.Structure):
         ("diag_list", _P), ("flat_list", _P), ("p_list", _P),
         ("n_diag", C.c_int32), ("n_flat", C.c_int32), ("n_p", C.c_int32), ("proj_fallback", C.c_int32),
         ("apply_fallback", C.c_int32), ("sm_reserve", C.c_int32),
+        ("la_fused", C.c_int32), ("la_init", C.c_int32), ("la_alpha", C.c_float),
+        ("pad5_", C.c_int32),
         ("err", _P),
         ("tmaps", _P), ("tmaps_ok", C.c_int32), ("gnorm_host", C.c_int32),
         ("filt", FilterDev),

@@ -286,7 +286,8 @@ apply_flat_kernel(ScaoPlanDev P) {
             const float pd = round_dt(fmul(p_, S.wd_mult), dt);
             m_ = fmaf(g_, S.c1, fmul(m_, S.beta1));
             v_ = fmaf(fmul(S.c2, g_), g_, fmul(v_, S.beta2));
-            const float den = fadd(fdiv(sqrtf(v_), S.sqrt_bc2), S.eps);
+            // Phase-1 rows carry 1 / sqrt_bc2 in rbc2
+            const float den = fadd(div_c(sqrtf(v_), S.sqrt_bc2, S.rbc2), S.eps);
             const float u = round_dt(fdiv(m_, den), dt);
             gsq = fmaf(graw, graw, gsq);
             return round_dt(fmaf(a1, u, pd), dt);
@@ -328,7 +329,7 @@ apply_flat_kernel(ScaoPlanDev P) {
             const float pd = round_dt(fmul(load_dt(pp, e, dt), S.wd_mult), dt);
             float m = fmaf(gv, S.c1, fmul(M[e], S.beta1));
             float v = fmaf(fmul(S.c2, gv), gv, fmul(V[e], S.beta2));
-            const float den = fadd(fdiv(sqrtf(v), S.sqrt_bc2), S.eps);
+            const float den = fadd(div_c(sqrtf(v), S.sqrt_bc2, S.rbc2), S.eps);
             const float u = round_dt(fdiv(m, den), dt);
             store_dt(pp, e, dt, round_dt(fmaf(a1, u, pd), dt));
             M[e] = m; V[e] = v; Pv[e] = gv;
@@ -437,6 +438,9 @@ __global__ void global_norm_kernel(ScaoPlanDev P) {
 }
 
 // Phase-2 parameter write: p = round(round(p*(1-lr wd)) + alpha*u)
+// LA: lookahead step fused (a separate instantiation keeps the plain
+// kernel's register count and occupancy)
+template <bool LA>
 __global__ void __launch_bounds__(NT)
 apply_p_kernel(ScaoPlanDev P) {
     const int cid = P.p_list[blockIdx.x];
@@ -449,6 +453,43 @@ apply_p_kernel(ScaoPlanDev P) {
     const float alpha = P.param_scalars[ch.param * 8 + PS_ALPHA];
     const float wdm = S.wd_mult;
     const bool vec = ((S.p_ptr & 15) == 0) && ((pr.offset & 3) == 0) && ((ch.begin & 3) == 0);
+    if (LA) {
+        // lookahead step (optimizer.py:356-365) fused into the write:
+        //   slow <- slow + a (p_new - slow) (param dtype roundings); p <- slow
+        void* sl = dt == SCAO_F32 ? (void*)(P.slow32 + pr.offset) : (void*)(P.slow + pr.offset);
+        const float la_a = P.la_alpha;
+        const int init = P.la_init;
+        auto step1 = [&](int64_t e, float pv, float u, float s) {
+            const float pn = round_dt(fmaf(alpha, u, round_dt(fmul(pv, wdm), dt)), dt);
+            const float s0 = init ? pn : s;
+            const float diff = round_dt(fsub(pn, s0), dt);
+            return round_dt(fadd(s0, round_dt(fmul(la_a, diff), dt)), dt);
+        };
+        int64_t vend = ch.begin;
+        if (vec) {
+            const int64_t n4 = (ch.end - ch.begin) >> 2;
+            vend = ch.begin + n4 * 4;
+            for (int64_t q = threadIdx.x; q < n4; q += NT) {
+                const int64_t e = ch.begin + q * 4;
+                const float4 p4 = load4_dt(pp, e, dt);
+                const float4 u4 = dt == SCAO_F32 ? *(const float4*)(P.upd32 + pr.offset + e)
+                                                 : load4_dt(P.upd + pr.offset, e, dt);
+                const float4 s4 = init ? p4 : load4_dt(sl, e, dt);
+                const float4 o = make_float4(step1(e, p4.x, u4.x, s4.x), step1(e, p4.y, u4.y, s4.y),
+                                             step1(e, p4.z, u4.z, s4.z), step1(e, p4.w, u4.w, s4.w));
+                store4_dt(sl, e, dt, o);
+                store4_dt(pp, e, dt, o);
+            }
+        }
+        for (int64_t e = vend + threadIdx.x; e < ch.end; e += NT) {
+            const float u = dt == SCAO_F32 ? P.upd32[pr.offset + e] : load_dt(P.upd + pr.offset, e, dt);
+            const float pv = load_dt(pp, e, dt);
+            const float o = step1(e, pv, u, init ? 0.f : load_dt(sl, e, dt));
+            store_dt(sl, e, dt, o);
+            store_dt(pp, e, dt, o);
+        }
+        return;
+    }
     if (vec) {
         const int64_t n4 = (ch.end - ch.begin) >> 2;
         for (int64_t q = threadIdx.x; q < n4; q += NT) {
@@ -482,6 +523,7 @@ lookahead_kernel(ScaoPlanDev P, float alpha, int init) {
     const ScaoChunk ch = P.chunks[blockIdx.x];
     const ScaoParam& pr = P.params[ch.param];
     const ScaoParamStep& S = P.step[ch.param];
+    if (P.la_fused && S.phase == 2) return;     // done inside apply_p_kernel
     const int dt = pr.dtype;
     void* pp = (void*)S.p_ptr;
     void* sl = dt == SCAO_F32 ? (void*)(P.slow32 + pr.offset) : (void*)(P.slow + pr.offset);
@@ -553,29 +595,62 @@ __device__ __forceinline__ void stage_ls(float* Ls, const float* Ul, int row0, i
 }
 
 // P_part = Ls^T Ts (kp x kp) from two row-major [rows][ld] fp32 tiles in
-// shared memory; each thread accumulates 4 x 4 blocks (16 FMA per two
-// 128-bit shared loads).
-__device__ __forceinline__ void proj_pblock(const float* Ls, const float* Ts, int ld, int kp,
-                                            int nrows, float* out, bool ok) {
-    const int nb = (kp + 3) >> 2;
-    for (int blk = threadIdx.x; blk < nb * nb; blk += blockDim.x) {
-        const int a0 = (blk / nb) * 4, b0 = (blk % nb) * 4;
-        float acc[4][4] = {};
-        for (int r = 0; r < nrows; ++r) {
-            const float4 la = *(const float4*)&Ls[r * ld + a0];
-            const float4 tb = *(const float4*)&Ts[r * ld + b0];
-            const float av[4] = {la.x, la.y, la.z, la.w}, bv[4] = {tb.x, tb.y, tb.z, tb.w};
+// shared memory.  Work item = an 8 x 4 output block and one half of the
+// rows; the two halves of a block sit in lanes l and l ^ 16 of one warp and
+// are added by a shuffle (fixed order: first half + second half).  Per row a
+// thread does 32 FMA for three 128-bit shared loads.  t / nthreads: this
+// thread among the participating ones (a multiple of 32).
+template <class LsRow>
+__device__ __forceinline__ void proj_pblock_g(LsRow ls_row, const float* Ts, int ld, int kp,
+                                              int nrows, float* out, bool ok, int t, int nthreads) {
+    const int nbb = (kp >> 3) * (kp >> 2);           // 8 x 4 blocks (kp is a multiple of 8)
+    const int lane = t & 31, w = t >> 5;
+    const int ks = lane >> 4;
+    const int h = (nrows + 1) >> 1;
+    const int r0 = ks ? h : 0, r1 = ks ? nrows : h;
+    const int per_it = nthreads >> 1;
+    for (int base = 0; base < nbb; base += per_it) {
+        const int blk = base + w * 16 + (lane & 15);
+        const bool live = blk < nbb;
+        const int a0 = live ? (blk / (kp >> 2)) * 8 : 0, b0 = live ? (blk % (kp >> 2)) * 4 : 0;
+        float acc[8][4] = {};
+        if (live) {
+            for (int r = r0; r < r1; ++r) {
+                float av[8];
+                ls_row(r, a0, av);
+                const float4 tb = *(const float4*)&Ts[r * ld + b0];
+                const float bv[4] = {tb.x, tb.y, tb.z, tb.w};
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
+                for (int i2 = 0; i2 < 8; ++i2)
 #pragma unroll
-                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+                    for (int j2 = 0; j2 < 4; ++j2) acc[i2][j2] = fmaf(av[i2], bv[j2], acc[i2][j2]);
+            }
         }
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
+        for (int i2 = 0; i2 < 8; ++i2)
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-                if (a0 + i < kp && b0 + j < kp) out[(a0 + i) * kp + b0 + j] = ok ? acc[i][j] : 0.f;
+            for (int j2 = 0; j2 < 4; ++j2) {
+                const float o = __shfl_xor_sync(0xffffffffu, acc[i2][j2], 16);
+                acc[i2][j2] = ks ? acc[i2][j2] : __fadd_rn(acc[i2][j2], o);
+            }
+        if (live && ks == 0)
+#pragma unroll
+            for (int i2 = 0; i2 < 8; ++i2)
+#pragma unroll
+                for (int j2 = 0; j2 < 4; ++j2)
+                    out[(a0 + i2) * kp + b0 + j2] = ok ? acc[i2][j2] : 0.f;
     }
+}
+
+// U_l rows staged in shared memory (row stride ld)
+__device__ __forceinline__ void proj_pblock(const float* Ls, const float* Ts, int ld, int kp,
+                                            int nrows, float* out, bool ok, int t, int nthreads) {
+    proj_pblock_g([&](int r, int a0, float* av) {
+        const float4 l0 = *(const float4*)&Ls[r * ld + a0];
+        const float4 l1 = *(const float4*)&Ls[r * ld + a0 + 4];
+        av[0] = l0.x; av[1] = l0.y; av[2] = l0.z; av[3] = l0.w;
+        av[4] = l1.x; av[5] = l1.y; av[6] = l1.z; av[7] = l1.w;
+    }, Ts, ld, kp, nrows, out, ok, t, nthreads);
 }
 
 // U_r rows -> ua tiles; U_r^T 64-row blocks -> ut tiles
@@ -887,7 +962,10 @@ proj_tma_kernel(ScaoPlanDev P, int* err) {
         abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 1) tc_alloc(&tslot, 256);
+    // two accumulators of 2 Kp columns: T_hi = G U_r,hi and T_lo = G U_r,lo
+    // side by side (one MMA of N = 2 Kp reads the gradient block once)
+    const uint32_t tcols = Kpm > 64 ? 512u : 256u;
+    if (warp == 1) tc_alloc(&tslot, tcols);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -928,23 +1006,21 @@ proj_tma_kernel(ScaoPlanDev P, int* err) {
                 const ScaoLeaf& L = P.leaves[pn.leaf];
                 if (!proj_tma_use(P, L)) continue;
                 const int Kp = (L.kpad + 15) & ~15;
-                const uint32_t bb = (uint32_t)Kp * 64 * 2;
                 if (!mbar_wait(&acce[acc], aph ^ 1)) { abort_flag = 1; atomicExch(err, 2); break; }
                 tc_fence_after();
-                const uint32_t d = tmem + acc * 128;
-                const uint32_t idesc = idesc_bf16(128, Kp);
+                const uint32_t d = tmem + acc * 2 * Kpm;
+                const uint32_t idesc = idesc_bf16(128, 2 * Kp);
                 bool ok = true;
                 for (int kb = 0; kb < L.b / 64; ++kb) {
                     if (!mbar_wait(&full[stage], ph)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t a = smem_u32(psm + (size_t)stage * SB);
-                    const uint32_t bh = a + 128 * 64 * 2, bl = bh + bb;
+                    const uint32_t bh = a + 128 * 64 * 2;     // [hi: Kp rows][lo: Kp rows]
 #pragma unroll
                     for (int s = 0; s < 4; ++s) {
                         const uint64_t ad = smem_desc_sw128(a + s * 32, 16, 1024);
                         tc_mma_bf16(d, ad, smem_desc(bh + s * 256, 128, 16 * 64), idesc,
                                     (kb > 0 || s > 0) ? 1u : 0u);
-                        tc_mma_bf16(d, ad, smem_desc(bl + s * 256, 128, 16 * 64), idesc, 1u);
                     }
                     tc_commit(&empty[stage]);
                     if (++stage == nst) { stage = 0; ph ^= 1; }
@@ -994,11 +1070,13 @@ proj_tma_kernel(ScaoPlanDev P, int* err) {
             if (!ok) { abort_flag = 1; atomicExch(err, 2); }
             if (ok) {
                 tc_fence_after();
+                const uint32_t tb = tmem + acc * 2 * Kpm + ((uint32_t)(q * 32) << 16);
                 for (int c0 = 16 * h; c0 < Kp; c0 += 32) {
-                    float v[16];
-                    tc_ld16(tmem + acc * 128 + ((uint32_t)(q * 32) << 16) + c0, v);
+                    float vh[16], vl[16];
+                    tc_ld16(tb + c0, vh);
+                    tc_ld16(tb + Kp + c0, vl);
 #pragma unroll
-                    for (int c = 0; c < 16; ++c) Ts[r * ld + c0 + c] = v[c];
+                    for (int c = 0; c < 16; ++c) Ts[r * ld + c0 + c] = __fadd_rn(vh[c], vl[c]);
                 }
             }
             tc_fence_before();
@@ -1007,45 +1085,28 @@ proj_tma_kernel(ScaoPlanDev P, int* err) {
             if (acc == 0) aph ^= 1;
             if (ls_async) asm volatile("cp.async.wait_all;" ::: "memory");
             named_bar(1, PT_EPI);                 // Ts (and Ls) complete
-            // P_part = U_l[rows]^T T, 4 x 4 blocks per thread
-            const int kp = L.kpad, nb = (kp + 3) >> 2;
+            // P_part = U_l[rows]^T T
+            const int kp = L.kpad;
             float* out = P.p_part + (int64_t)T * P.p_stride;
 #ifdef SCAO_EXP_NOPB
-            if (nb > 0) continue;
+            if (kp > 0) continue;
 #endif
-            for (int blk = et; blk < nb * nb; blk += PT_EPI) {
-                const int a0 = (blk / nb) * 4, b0 = (blk % nb) * 4;
-                float accv[4][4] = {};
-#pragma unroll 4
-                for (int rr = 0; rr < pn.nrows; ++rr) {
-                    float av[4];
-                    if (ls_async) {
-                        const float4 la = *(const float4*)&Ls[rr * ld + a0];
-                        av[0] = la.x; av[1] = la.y; av[2] = la.z; av[3] = la.w;
-                    } else {
+            if (ls_async) {
+                proj_pblock(Ls, Ts, ld, kp, pn.nrows, out, ok, et, PT_EPI);
+            } else {
+                const int sl = L.sl;
+                proj_pblock_g([&](int r, int a0, float* av) {
 #pragma unroll
-                        for (int i = 0; i < 4; ++i)
-                            av[i] = a0 + i < kp ? __ldg(Ulp + (int64_t)rr * L.sl + a0 + i) : 0.f;
-                    }
-                    const float4 tb = *(const float4*)&Ts[rr * ld + b0];
-                    const float bv[4] = {tb.x, tb.y, tb.z, tb.w};
-#pragma unroll
-                    for (int i = 0; i < 4; ++i)
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) accv[i][j] = fmaf(av[i], bv[j], accv[i][j]);
-                }
-#pragma unroll
-                for (int i = 0; i < 4; ++i)
-#pragma unroll
-                    for (int j = 0; j < 4; ++j)
-                        if (a0 + i < kp && b0 + j < kp) out[(a0 + i) * kp + b0 + j] = accv[i][j];
+                    for (int i2 = 0; i2 < 8; ++i2)
+                        av[i2] = a0 + i2 < kp ? __ldg(Ulp + (int64_t)r * sl + a0 + i2) : 0.f;
+                }, Ts, ld, kp, pn.nrows, out, ok, et, PT_EPI);
             }
         }
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 1) tc_dealloc(tmem, 256);
+    if (warp == 1) tc_dealloc(tmem, tcols);
 }
 
 // ---------------------------------------------------------------------------
@@ -1314,8 +1375,8 @@ proj_bf16_kernel(ScaoPlanDev P, int* err) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint16_t* g = (const uint16_t*)S.g_ptr;
     const float* Ul = P.u + L.ul_off;
-    uint32_t ncols = 32;
-    while ((int)ncols < Kp) ncols <<= 1;
+    uint32_t ncols = 32;                        // [T_hi | T_lo]: 2 Kp columns
+    while ((int)ncols < 2 * Kp) ncols <<= 1;
     if (warp == 0) tc_alloc(&tslot, ncols);
     if (tid == 0) {
         for (int i = 0; i < PJ_STAGES; ++i) { mbar_init(&mbar_b[i], 1); mbar_init(&mbar_m[i], 1); }
@@ -1325,7 +1386,7 @@ proj_bf16_kernel(ScaoPlanDev P, int* err) {
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tslot;
-    const uint32_t idesc = idesc_bf16(TC_T, Kp);
+    const uint32_t idesc = idesc_bf16(TC_T, 2 * Kp);
     const int64_t base = (int64_t)(L.row0 + pn.row0) * L.ld + L.col0;
     const int nkb = (L.b + KB - 1) / KB;
     bool ok = true;
@@ -1375,11 +1436,11 @@ proj_bf16_kernel(ScaoPlanDev P, int* err) {
         tc_fence_after();
         if (tid == 0) {
             ok = mbar_wait(&mbar_b[buf], (kb / PJ_STAGES) & 1) && ok;
-            const uint32_t sa = smem_u32(smx + buf * sbytes), sbh = sa + abytes, sbl = sbh + bbytes;
+            const uint32_t sa = smem_u32(smx + buf * sbytes), sbh = sa + abytes;
             for (int s = 0; s < KB / 16; ++s) {
                 const uint64_t a0 = smem_desc(sa + s * 256, 128, 16 * KB);
+                // B = [U_r,hi ; U_r,lo] (2 Kp rows): one MMA gives T_hi and T_lo
                 tc_mma_bf16(tmem, a0, smem_desc(sbh + s * 256, 128, 16 * KB), idesc, (kb > 0 || s > 0));
-                tc_mma_bf16(tmem, a0, smem_desc(sbl + s * 256, 128, 16 * KB), idesc, 1);
             }
             tc_commit(&mbar_m[buf]);
         }
@@ -1394,8 +1455,10 @@ proj_bf16_kernel(ScaoPlanDev P, int* err) {
         const int r = warp * 32 + lane;
         for (int c0 = 0; c0 < Kp; c0 += 16) {
             float v[16];
+            float vl[16];
             tc_ld16(tmem + ((uint32_t)(warp * 32) << 16) + c0, v);
-            for (int c = 0; c < 16; ++c) Ts[r * (Kp + 4) + c0 + c] = ok ? v[c] : 0.f;
+            tc_ld16(tmem + ((uint32_t)(warp * 32) << 16) + Kp + c0, vl);
+            for (int c = 0; c < 16; ++c) Ts[r * (Kp + 4) + c0 + c] = ok ? __fadd_rn(v[c], vl[c]) : 0.f;
         }
     }
     stage_ls(Ls, Ul, pn.row0, pn.nrows, L.sl, L.kpad, Kp);
@@ -1404,7 +1467,7 @@ proj_bf16_kernel(ScaoPlanDev P, int* err) {
     if (warp == 0) tc_dealloc(tmem, ncols);
     float* out = P.p_part + (int64_t)blockIdx.x * P.p_stride;
     const int kp = L.kpad;
-    proj_pblock(Ls, Ts, Kp + 4, kp, pn.nrows, out, true);
+    proj_pblock(Ls, Ts, Kp + 4, kp, pn.nrows, out, true, threadIdx.x, blockDim.x);
 }
 
 size_t proj_bf16_smem(int kpad) {
@@ -1588,7 +1651,7 @@ proj_tc_kernel(ScaoPlanDev P, int* err) {
     if (warp == 0) tc_dealloc(tmem, ncols);
     float* out = P.p_part + (int64_t)blockIdx.x * P.p_stride;
     const int kp = L.kpad;
-    proj_pblock(Ls, Ts, Kp + 4, kp, pn.nrows, out, ok);
+    proj_pblock(Ls, Ts, Kp + 4, kp, pn.nrows, out, ok, threadIdx.x, blockDim.x);
     (void)psq;
 }
 
@@ -1718,7 +1781,11 @@ extern "C" int scao_plan_step(const ScaoPlanDev* P, void* stream) {
         SCAO_CHECK_LAUNCH();
     }
     if (P->n_chunks > 0) {
-        if (P->n_p > 0) { ProfScope _ps(SLOT_APPLY_P, st); apply_p_kernel<<<P->n_p, NT, 0, st>>>(*P); }
+        if (P->n_p > 0) {
+            ProfScope _ps(SLOT_APPLY_P, st);
+            if (P->la_fused) apply_p_kernel<true><<<P->n_p, NT, 0, st>>>(*P);
+            else apply_p_kernel<false><<<P->n_p, NT, 0, st>>>(*P);
+        }
         SCAO_CHECK_LAUNCH();
     }
     return SCAO_OK;

@@ -353,6 +353,7 @@ class SCAO(Optimizer):
                 row["phase"] = 1
                 row["alpha1"] = -(lr / bc1)
                 row["sqrt_bc2"] = math.sqrt(bc2)
+                row["rbc2"] = 1.0 / float(row["sqrt_bc2"])      # x / c as x * r + correction
                 continue
             row["phase"] = 2
             if not st.get("scao_phase_started", False):
@@ -430,18 +431,26 @@ class SCAO(Optimizer):
             plan.dev.proj_fallback = int(bool(np.any((ph == 2) & ~(plan.leaf_tma_shape & al))))
             alp = al & ((tab["p_ptr"][plan.leaf_param] % 16) == 0)
             plan.dev.apply_fallback = int(bool(np.any((ph == 2) & ~(plan.leaf_tma_apply & alp))))
+        # lookahead (optimizer.py:356-365, after the parameter update): fused into
+        # the Phase-2 parameter write; the lookahead kernel does the rest
+        la_now = self._lookahead_k > 0 and self._global_step % self._lookahead_k == 0
+        if la_now:
+            plan.ensure_slow()
+        plan.dev.la_fused = 1 if la_now else 0
+        plan.dev.la_init = 0 if self._lookahead_init else 1
+        plan.dev.la_alpha = float(self._lookahead_alpha)
         f = plan.dev.filt
         f.noise_on = 1 if self._noise_std > 1e-9 else 0     # optimizer.py:544
         f.noise_std = float(np.float32(self._noise_std))
         f.noise_step = self._global_step
         _lib.check(L.scao_plan_step(pd, sp), "scao_plan_step")
         self._noise_std *= self._noise_anneal
-        if self._lookahead_k > 0 and self._global_step % self._lookahead_k == 0:
-            plan.ensure_slow()
+        if la_now:
             _lib.check(L.scao_plan_lookahead(pd, float(self._lookahead_alpha),
                                              0 if self._lookahead_init else 1, sp),
                        "scao_plan_lookahead")
             self._lookahead_init = True
+        plan.dev.la_fused = 0
         self._keep = keep   # keep temporaries alive until the next step
         if self._callbacks:
             metrics = self.collect_metrics()
