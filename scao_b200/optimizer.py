@@ -383,6 +383,14 @@ class SCAO(Optimizer):
         dptr = plan.dev
         import ctypes
         pd = ctypes.byref(dptr)
+        # TMA tensor maps of this step's gradients / parameters: one device
+        # buffer per pointer set (a few kept, so alternating gradient buffers
+        # do not re-encode); selected before any kernel that reads them
+        if plan.has_bf16_kron and os.environ.get("SCAO_NO_TMA") != "1":
+            plan.select_tensor_maps((tab["g_ptr"].tobytes(), tab["p_ptr"].tobytes(),
+                                     tab["phase"].tobytes()), pd, sp)
+        else:
+            plan.dev.tmaps_ok = 0
         for rho, leaves in curv_leaves.items():
             ids_h = np.ascontiguousarray(leaves, dtype=np.int32)
             ids = plan.dev_ids(ids_h)
@@ -413,17 +421,6 @@ class SCAO(Optimizer):
             self._last_eig_status = status
             keep.append(ids)
         plan.set_phases(np.array(tab["phase"], dtype=np.int32))
-        if plan.has_bf16_kron and os.environ.get("SCAO_NO_TMA") != "1":
-            # tensor maps of the gradients (rebuilt only when a pointer or
-            # phase changed)
-            key = (tab["g_ptr"].tobytes(), tab["p_ptr"].tobytes(), tab["phase"].tobytes())
-            if key != plan.tmap_key:
-                rc = L.scao_plan_tensor_maps(pd, plan.ptab.ctypes.data, plan.step_host.data_ptr(), sp)
-                plan.dev.tmaps_ok = 1 if rc == 0 else 0
-                plan.tmap_key = key if rc == 0 else None
-        else:
-            plan.dev.tmaps_ok = 0
-            plan.tmap_key = None
         if plan.n_leaves:
             # the cp.async projection runs only for Phase-2 leaves the TMA one cannot take
             ph = tab["phase"][plan.leaf_param]

@@ -247,7 +247,7 @@ class Plan:
         self.global_norm_ema = torch.ones(1, dtype=torch.float64, device=dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
         self.tmaps = torch.zeros(self.n_params * 9 * 128, dtype=torch.uint8, device=dev)
-        self.tmap_key = None
+        self.tmap_cache = {}          # pointer-set key -> device buffer of maps (LRU order)
         # leaves whose panels the TMA projection can take (static part of its
         # test: bf16, 16-byte aligned rows and block origin, 64-multiple width)
         self.leaf_tma_shape = np.array(
@@ -427,6 +427,30 @@ class Plan:
         buf.numpy()[:self.n_leaves] = kvec
         self.k.copy_(buf[:self.n_leaves], non_blocking=True)
         self._mark("_k_pin_up")
+
+    def select_tensor_maps(self, key, pd, stream, keep=4):
+        """Point the plan at the tensor maps of ``key`` (gradient / parameter
+        pointers and phases), encoding them on a miss.  Buffers are reused in
+        LRU order; a rewrite is stream-ordered after the kernels that read it."""
+        buf = self.tmap_cache.pop(key, None)
+        hit = buf is not None
+        if not hit:
+            if len(self.tmap_cache) >= keep:
+                old = next(iter(self.tmap_cache))
+                buf = self.tmap_cache.pop(old)
+            else:
+                buf = torch.zeros(self.n_params * 9 * 128, dtype=torch.uint8, device=self.device)
+        self.tmap_cache[key] = buf
+        self.tmaps = buf
+        self.dev.tmaps = buf.data_ptr()
+        if hit:
+            self.dev.tmaps_ok = 1
+            return
+        rc = _lib.lib().scao_plan_tensor_maps(pd, self.ptab.ctypes.data, self.step_host.data_ptr(),
+                                              stream)
+        self.dev.tmaps_ok = 1 if rc == 0 else 0
+        if rc != 0:
+            self.tmap_cache.pop(key, None)
 
     def check_error(self):
         """Raise if a kernel recorded a timed-out wait (synchronises)."""
