@@ -372,10 +372,19 @@ def main():
         # host gradients (pinned) -> device every step through opt.step(); the
         # next step's copy runs on a copy stream into the other of two
         # gradient buffers while this step computes (input prefetch)
-        host = [g.cpu().pin_memory() for g in grad_sets[0]]
-        h2d = sum(h.numel() * h.element_size() for h in host)
+        # one flat pinned host buffer and two flat device buffers (each
+        # gradient a 16-byte aligned view), so a step is one large copy
+        offs, tot = [], 0
+        for g in grad_sets[0]:
+            offs.append(tot)
+            tot += (g.numel() + 7) // 8 * 8
+        host_flat = torch.zeros(tot, dtype=grad_sets[0][0].dtype).pin_memory()
+        for g, o in zip(grad_sets[0], offs):
+            host_flat[o:o + g.numel()].copy_(g.reshape(-1))
+        h2d = host_flat.numel() * host_flat.element_size()
         res = torch.empty(1, dtype=torch.float64).pin_memory()
-        bufs = [[torch.empty_like(p) for p in params] for _ in range(2)]
+        flats = [torch.empty(tot, dtype=host_flat.dtype, device=dev) for _ in range(2)]
+        bufs = [[f[o:o + p.numel()].view_as(p) for p, o in zip(params, offs)] for f in flats]
         cstream = torch.cuda.Stream(dev)
         copied = [torch.cuda.Event() for _ in range(2)]
         freed = [torch.cuda.Event() for _ in range(2)]
@@ -389,8 +398,7 @@ def main():
             with torch.cuda.stream(cstream):
                 if k >= 2:
                     cstream.wait_event(freed[k % 2])      # step k-2 is done with it
-                for d_, h in zip(bufs[k % 2], host):
-                    d_.copy_(h, non_blocking=True)
+                flats[k % 2].copy_(host_flat, non_blocking=True)
                 copied[k % 2].record(cstream)
         upload(0)
         for k in range(a.e2e_steps):
