@@ -215,7 +215,7 @@ typedef struct {
     int32_t pad5_;
     int32_t* err;                /* device error flag: set to 1 when a bounded
                                     wait on the tensor core timed out       */
-    uint8_t* tmaps;              /* n_params x 9 TMA tensor maps (128 B each,
+    uint8_t* tmaps;              /* n_params x 10 TMA tensor maps (128 B each,
                                     written by scao_plan_tensor_maps and
                                     scao_plan_curvature)                    */
     int32_t tmaps_ok;            /* 1: tmaps describe this step's gradients */

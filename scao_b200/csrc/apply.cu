@@ -740,7 +740,7 @@ apply_kron_tc_kernel(ScaoPlanDev P, int* err) {
     const ScaoLeaf& L = P.leaves[tl.leaf];
     const ScaoParamStep& S = P.step[L.param];
     if (S.phase != 2) return;
-    if (!FN && apply_tma_use(P, L)) return;     // apply_tma_kernel
+    if (apply_tma_use(P, L)) return;     // apply_tma_kernel
     const ScaoParam& pr = P.params[L.param];
     const int dt = pr.dtype;
     const int Kp = (L.kpad + 15) & ~15;
@@ -1137,21 +1137,29 @@ constexpr uint32_t AT_G = 0, AT_P = AT_R * 128 * 2, AT_M = 2 * AT_R * 128 * 2;
 constexpr uint32_t AT_V = AT_M + AT_R * 128 * 4, AT_D = AT_V + AT_R * 128 * 4;
 constexpr uint32_t AT_PV = AT_D + AT_R * 128 * 4;
 constexpr uint32_t AT_STAGE = AT_PV + AT_R * 128 * 4;  // 40 KB
+constexpr uint32_t AT_MG = AT_STAGE;                   // filter: magnitude EMA chunk
+constexpr uint32_t AT_STAGE_FN = AT_STAGE + AT_R * 128 * 4;   // 48 KB
 
 
 __host__ __device__ inline int apply_tma_stages(int kpm) { return kpm > 64 ? 2 : SCAO_APPLY_ST; }
 __host__ __device__ inline uint32_t apply_tma_ops_bytes(int kpm) { return 4u * 128 * kpm * 2; }
-size_t apply_tma_smem(int kpad_max) {
+__host__ __device__ inline uint32_t apply_tma_stage_bytes(bool fn) { return fn ? AT_STAGE_FN : AT_STAGE; }
+size_t apply_tma_smem(int kpad_max, bool fn) {
     const int Kp = (kpad_max + 15) & ~15;
-    return (size_t)apply_tma_ops_bytes(Kp) + (size_t)apply_tma_stages(Kp) * AT_STAGE + 1024;
+    return (size_t)apply_tma_ops_bytes(Kp) + (size_t)apply_tma_stages(Kp) * apply_tma_stage_bytes(fn) +
+           1024;
 }
 
+// FN: the gradient filter, noise or gSNR clip is on this step
+template <bool FN>
 __global__ void __launch_bounds__(AT_THREADS, 1)
 apply_tma_kernel(ScaoPlanDev P, int* err) {
     extern __shared__ unsigned char asm_raw[];
     unsigned char* sm = (unsigned char*)(((uintptr_t)asm_raw + 1023) & ~(uintptr_t)1023);
     const int Kpm = (P.kpad_max + 15) & ~15;
     const int nst = apply_tma_stages(Kpm);
+    constexpr uint32_t SBY = FN ? AT_STAGE_FN : AT_STAGE;
+    const bool with_mg = FN && P.filt.mode != 0;
     unsigned char* ops = sm;                                  // [A hi|lo][B hi|lo]
     unsigned char* stg = sm + apply_tma_ops_bytes(Kpm);
     __shared__ uint64_t full[AT_MAXST], empty[AT_MAXST], accf[2], acce[2], opfull, opfree, fin;
@@ -1188,8 +1196,10 @@ apply_tma_kernel(ScaoPlanDev P, int* err) {
                 for (int c = 0; c < NCH; ++c) {
                     if (!mbar_wait(&empty[stage], ph ^ 1)) { abort_flag = 1; atomicExch(err, 2); break; }
                     const int y = L.row0 + tl.row0 + c * AT_R;
-                    mbar_expect_tx(&full[stage], AT_STAGE);
-                    const uint32_t s = smem_u32(stg + (size_t)stage * AT_STAGE);
+                    mbar_expect_tx(&full[stage], with_mg ? AT_STAGE_FN : AT_STAGE);
+                    const uint32_t s = smem_u32(stg + (size_t)stage * SBY);
+                    if (with_mg)
+                        tma_load_2d(s + AT_MG, scao_tmap(P.tmaps, L.param, TM_MG), x, y, &full[stage]);
                     tma_load_2d(s + AT_G, scao_tmap(P.tmaps, L.param, TM_GS), x, y, &full[stage]);
                     tma_load_2d(s + AT_P, scao_tmap(P.tmaps, L.param, TM_PS), x, y, &full[stage]);
                     tma_load_2d(s + AT_M, scao_tmap(P.tmaps, L.param, TM_M), x, y, &full[stage]);
@@ -1281,7 +1291,7 @@ apply_tma_kernel(ScaoPlanDev P, int* err) {
             for (int c = 0; c < 128 / AT_R; ++c) {
                 const bool okc = ok && __all_sync(0xffffffffu, mbar_wait(&full[stage], ph));
                 if (!okc) { abort_flag = 1; atomicExch(err, 2); }
-                unsigned char* st = stg + (size_t)stage * AT_STAGE;
+                unsigned char* st = stg + (size_t)stage * SBY;
                 if (okc) {
                     float corr[AT_RPT];
                     if (AT_RPT == 8) tc_ld8(tmem + acc * 128 + ((uint32_t)(q * 32) << 16) + c * AT_R + h * 8, corr);
@@ -1292,6 +1302,42 @@ apply_tma_kernel(ScaoPlanDev P, int* err) {
                     float* vs = (float*)(st + AT_V);
                     float* ds = (float*)(st + AT_D);
                     float* qs = (float*)(st + AT_PV);
+                    float zr[AT_RPT];
+                    if (FN) {
+                        // gradient noise of (row, column j): the Philox block of a
+                        // 4-column group is drawn once per row by one lane of the
+                        // group and handed to the others by shuffles
+                        const int rbase = L.row0 + tl.row0 + c * AT_R + h * AT_RPT;
+                        const int64_t cols = P.params[L.param].cols;
+                        const int g4 = lane >> 2, t4 = lane & 3;
+#pragma unroll
+                        for (int rr = 0; rr < AT_RPT; ++rr) zr[rr] = 0.f;
+                        if (P.filt.noise_on) {
+                            if (AT_RPT == 4) {
+                                const int64_t e = (int64_t)(rbase + t4) * cols + x + q * 32 + g4 * 4;
+                                const float4 z4 = noise_normal4(P.filt.noise_seed, L.param,
+                                                                P.filt.noise_step, e >> 2);
+#pragma unroll
+                                for (int rr = 0; rr < AT_RPT; ++rr) {
+                                    const int src = (lane & ~3) + rr;
+                                    const float a0 = __shfl_sync(0xffffffffu, z4.x, src);
+                                    const float a1 = __shfl_sync(0xffffffffu, z4.y, src);
+                                    const float a2 = __shfl_sync(0xffffffffu, z4.z, src);
+                                    const float a3 = __shfl_sync(0xffffffffu, z4.w, src);
+                                    zr[rr] = t4 == 0 ? a0 : t4 == 1 ? a1 : t4 == 2 ? a2 : a3;
+                                }
+                            } else {
+#pragma unroll
+                                for (int rr = 0; rr < AT_RPT; ++rr) {
+                                    const int64_t e = (int64_t)(rbase + rr) * cols + x + j;
+                                    zr[rr] = f4_get(noise_normal4(P.filt.noise_seed, L.param,
+                                                                  P.filt.noise_step, e >> 2), (int)(e & 3));
+                                }
+                            }
+                        }
+                    }
+                    const float* mgs = (const float*)(st + AT_MG);
+                    const float thr = (FN && P.filt.mode) ? P.filt.fp[L.param].thr : 0.f;
 #pragma unroll
                     for (int rr = 0; rr < AT_RPT; ++rr) {
                         const int o = (h * AT_RPT + rr) * 128 + j;
@@ -1299,7 +1345,10 @@ apply_tma_kernel(ScaoPlanDev P, int* err) {
                         const float pv = bf16_bits_to_f(pps[o]);
                         float mv = ms[o], vv = vs[o], dv = ds[o], qv = qs[o];
                         const float gp = round_dt(fadd(gv, corr[rr]), SCAO_BF16);
-                        const float u = adan_elem(S, SCAO_BF16, gv, gp, mv, vv, dv, qv, clip, clipmul);
+                        float gf = gv;
+                        if (FN) gf = filt_grad(P.filt, gv, with_mg ? mgs[o] : 0.f, thr, zr[rr]);
+                        float u = adan_elem(S, SCAO_BF16, gf, gp, mv, vv, dv, qv, clip, clipmul);
+                        if (FN && P.filt.gsnr_on) u = gsnr_mask(u, mv, vv, S.eps, P.filt.gsnr_thr);
                         usq = fmaf(u, u, usq);
                         gsq = fmaf(gv, gv, gsq);
                         const float pd = round_dt(fmul(pv, wdm), SCAO_BF16);
@@ -1748,21 +1797,22 @@ extern "C" int scao_plan_step(const ScaoPlanDev* P, void* stream) {
     SCAO_CHECK_LAUNCH();
     if (P->n_tiles > 0) {
         { ProfScope _ps(SLOT_APPLY_KRON, st);
-          if (fn) {
-              apply_kron_tc_kernel<true><<<P->n_tiles, SCAO_APPLY_NT, apply_tc_smem(P->kpad_max), st>>>(*P, P->err);
-          } else {
-              if (P->tmaps_ok) {
-                  static bool aattr = false;
-                  if (!aattr) {
-                      cudaFuncSetAttribute(apply_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)apply_tma_smem(128));
-                      aattr = true;
-                  }
-                  const int g = scao_persistent_grid(P, P->n_tiles);
-                  apply_tma_kernel<<<g, AT_THREADS, apply_tma_smem(P->kpad_max), st>>>(*P, P->err);
-              }
-              if (!P->tmaps_ok || P->apply_fallback)
-                  apply_kron_tc_kernel<false><<<P->n_tiles, SCAO_APPLY_NT, apply_tc_smem(P->kpad_max), st>>>(*P, P->err);
+          static bool aattr = false;
+          if (!aattr) {
+              cudaFuncSetAttribute(apply_tma_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)apply_tma_smem(128, false));
+              cudaFuncSetAttribute(apply_tma_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)apply_tma_smem(128, true));
+              aattr = true;
+          }
+          const int g = scao_persistent_grid(P, P->n_tiles);
+          if (P->tmaps_ok) {
+              if (fn) apply_tma_kernel<true><<<g, AT_THREADS, apply_tma_smem(P->kpad_max, true), st>>>(*P, P->err);
+              else apply_tma_kernel<false><<<g, AT_THREADS, apply_tma_smem(P->kpad_max, false), st>>>(*P, P->err);
+          }
+          if (!P->tmaps_ok || P->apply_fallback) {
+              if (fn) apply_kron_tc_kernel<true><<<P->n_tiles, SCAO_APPLY_NT, apply_tc_smem(P->kpad_max), st>>>(*P, P->err);
+              else apply_kron_tc_kernel<false><<<P->n_tiles, SCAO_APPLY_NT, apply_tc_smem(P->kpad_max), st>>>(*P, P->err);
           } }
         SCAO_CHECK_LAUNCH();
     }

@@ -68,6 +68,9 @@ bool scao_build_tensor_maps(const ScaoPlanDev* P, const ScaoParam* ph, const Sca
         if (!encode(m + TM_V, F4, 4, P->exp_avg_sq + o, r, c, 128, SR, NS)) return false;
         if (!encode(m + TM_D, F4, 4, P->exp_avg_diff + o, r, c, 128, SR, NS)) return false;
         if (!encode(m + TM_PV, F4, 4, P->prev_grad + o, r, c, 128, SR, NS)) return false;
+        if (P->filt.mode && P->filt.mag_ema &&
+            !encode(m + TM_MG, F4, 4, P->filt.mag_ema + o, r, c, 128, SR, NS))
+            return false;
     }
     // pageable source: the copy is staged before cudaMemcpyAsync returns
     return cudaMemcpyAsync(P->tmaps, maps.data(), maps.size() * sizeof(CUtensorMap),

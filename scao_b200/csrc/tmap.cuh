@@ -12,12 +12,13 @@
 //   TM_GS, TM_PS, TM_US  gradient, parameter, bf16 update arena;
 //   TM_M, TM_V, TM_D, TM_PV  exp_avg, exp_avg_sq, exp_avg_diff, prev_grad
 //                      arenas: 16-row x 128-column boxes, no swizzle (state
-//                      streaming of the apply kernel).
+//                      streaming of the apply kernel);
+//   TM_MG              the gradient filter's magnitude EMA (when it is on).
 // Zero fill out of bounds.  A parameter that is not bf16, not 16-byte
 // aligned, or has no gradient this step gets zeroed maps (the kernels never
 // read them: their eligibility tests are the same).  Returns false when the
 // driver entry point is missing or an encode fails.
-enum { TM_G128 = 0, TM_G64, TM_GS, TM_PS, TM_US, TM_M, TM_V, TM_D, TM_PV, TMA_PER_PARAM };
+enum { TM_G128 = 0, TM_G64, TM_GS, TM_PS, TM_US, TM_M, TM_V, TM_D, TM_PV, TM_MG, TMA_PER_PARAM };
 constexpr int TMA_STATE_ROWS = 16;
 bool scao_build_tensor_maps(const ScaoPlanDev* P, const ScaoParam* params_host,
                             const ScaoParamStep* step_host, cudaStream_t st);

@@ -246,7 +246,7 @@ class Plan:
         self.param_scalars = z(self.n_params * 8)
         self.global_norm_ema = torch.ones(1, dtype=torch.float64, device=dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
-        self.tmaps = torch.zeros(self.n_params * 9 * 128, dtype=torch.uint8, device=dev)
+        self.tmaps = torch.zeros(self.n_params * 10 * 128, dtype=torch.uint8, device=dev)
         self.tmap_cache = {}          # pointer-set key -> device buffer of maps (LRU order)
         # leaves whose panels the TMA projection can take (static part of its
         # test: bf16, 16-byte aligned rows and block origin, 64-multiple width)
@@ -439,7 +439,7 @@ class Plan:
                 old = next(iter(self.tmap_cache))
                 buf = self.tmap_cache.pop(old)
             else:
-                buf = torch.zeros(self.n_params * 9 * 128, dtype=torch.uint8, device=self.device)
+                buf = torch.zeros(self.n_params * 10 * 128, dtype=torch.uint8, device=self.device)
         self.tmap_cache[key] = buf
         self.tmaps = buf
         self.dev.tmaps = buf.data_ptr()

@@ -62,7 +62,7 @@ def test_tma_gram_matches_cp_async_gram(int8):
         assert torch.equal(fa, fb) or (fa - fb).abs().max().item() <= 1e-6 * fb.abs().max().item()
 
 
-def _run_steps(no_tma, steps=6):
+def _run_steps(no_tma, steps=6, **extra):
     if no_tma:
         os.environ["SCAO_NO_TMA"] = "1"
     else:
@@ -71,9 +71,11 @@ def _run_steps(no_tma, steps=6):
         gen = torch.Generator().manual_seed(3)
         params = [torch.nn.Parameter((torch.randn(s, generator=gen) * 0.02).to(DEV, torch.bfloat16))
                   for s in SHAPES]
-        opt = SCAO(params, lr=1e-3, precond_freq=2, warmup_steps=2, min_precond_updates=1,
-                   blend_steps=3, use_int8_ema=True, max_precond_dim=1024, sparsity=0.0,
-                   noise_std_init=0.0, k_max=32, async_precond=False, lookahead_k=0)
+        kw = dict(lr=1e-3, precond_freq=2, warmup_steps=2, min_precond_updates=1,
+                  blend_steps=3, use_int8_ema=True, max_precond_dim=1024, sparsity=0.0,
+                  noise_std_init=0.0, k_max=32, async_precond=False, lookahead_k=0)
+        kw.update(extra)
+        opt = SCAO(params, **kw)
         for _ in range(steps):
             for p in params:
                 p.grad = (torch.randn(p.shape, generator=gen) * 3.0).to(DEV, torch.bfloat16)
@@ -86,11 +88,17 @@ def _run_steps(no_tma, steps=6):
         os.environ.pop("SCAO_NO_TMA", None)
 
 
-def test_tma_projection_matches_cp_async_projection():
+@pytest.mark.parametrize("extra", [{}, dict(sparsity=0.6, noise_std_init=0.05, use_gsnr_clip=True,
+                                              gsnr_threshold=0.2, lookahead_k=3)])
+def test_tma_projection_matches_cp_async_projection(extra):
     """Phase-2 steps: identical parameters and moments with the persistent
-    TMA projection and with the cp.async projection."""
-    pa, ma = _run_steps(no_tma=False)
-    pb, mb = _run_steps(no_tma=True)
+    TMA projection / apply and with the cp.async projection / register-
+    streaming apply -- also with the gradient filter, noise, gSNR clip and
+    lookahead on (the noise stream depends only on the element)."""
+    torch.cuda.manual_seed(5)
+    pa, ma = _run_steps(no_tma=False, **extra)
+    torch.cuda.manual_seed(5)
+    pb, mb = _run_steps(no_tma=True, **extra)
     for x, y in zip(pa, pb):
         assert torch.equal(x, y)
     for x, y in zip(ma, mb):
