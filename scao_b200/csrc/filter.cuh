@@ -24,8 +24,10 @@ SCAO_DEV uint4 philox4x32_10(uint4 c, uint32_t k0, uint32_t k1) {
 
 // Four standard normals for the elements 4*e4 .. 4*e4+3 of parameter
 // ``param`` at global step ``step``: one Philox block, two Box-Muller pairs
-// (uniforms in (0, 1] from the top 24 bits).  The stream depends only on
-// (seed, param, step, element), never on which kernel or thread asks.
+// (uniforms in (0, 1] from the top 24 bits; the hardware approximations of
+// log and sin/cos -- the noise is a distribution, not a value to match).
+// The stream depends only on (seed, param, step, element), never on which
+// kernel or thread asks.
 SCAO_DEV float4 noise_normal4(uint64_t seed, uint32_t param, uint64_t step, int64_t e4) {
     const uint4 r = philox4x32_10(
         make_uint4((uint32_t)e4, (uint32_t)((uint64_t)e4 >> 32), (uint32_t)step, param),
@@ -33,10 +35,11 @@ SCAO_DEV float4 noise_normal4(uint64_t seed, uint32_t param, uint64_t step, int6
     const float k = 5.9604644775390625e-08f;   // 2^-24
     const float u0 = ((r.x >> 8) + 1) * k, u1 = ((r.y >> 8) + 1) * k;
     const float u2 = ((r.z >> 8) + 1) * k, u3 = ((r.w >> 8) + 1) * k;
-    const float ra = sqrtf(-2.f * logf(u0)), rb = sqrtf(-2.f * logf(u2));
+    const float ra = sqrtf(-2.f * __logf(u0)), rb = sqrtf(-2.f * __logf(u2));
+    const float two_pi = 6.283185307179586f;
     float sa, ca, sb, cb;
-    sincospif(2.f * u1, &sa, &ca);
-    sincospif(2.f * u3, &sb, &cb);
+    __sincosf(two_pi * u1, &sa, &ca);
+    __sincosf(two_pi * u3, &sb, &cb);
     return make_float4(ra * ca, ra * sa, rb * cb, rb * sb);
 }
 
