@@ -630,40 +630,40 @@ extern "C" int scao_plan_eigen(const ScaoPlanDev* P, const int32_t* leaf_ids, in
         GemmSpec g;
         // Y = A U
         g = {BUF_FAC, BUF_U, BUF_Y, DIM_N, DIM_S, DIM_N, 0, 0};
-        { ProfScope _ps(SLOT_EIG_GEMM, 0); eig_gemm_kernel<<<dim3(tiles_nn, np), NT, 0, st>>>(*P, leaf_ids, g); }
+        { ProfScope _ps(SLOT_EIG_GEMM, st); eig_gemm_kernel<<<dim3(tiles_nn, np), NT, 0, st>>>(*P, leaf_ids, g); }
         SCAO_CHECK_LAUNCH();
         // H = U^T Y
         g = {BUF_U, BUF_Y, BUF_H, DIM_S, DIM_S, DIM_N, 1, 0};
-        { ProfScope _ps(SLOT_EIG_GEMM, 0); eig_gemm_kernel<<<dim3(tiles_ss, np), NT, 0, st>>>(*P, leaf_ids, g); }
+        { ProfScope _ps(SLOT_EIG_GEMM, st); eig_gemm_kernel<<<dim3(tiles_ss, np), NT, 0, st>>>(*P, leaf_ids, g); }
         SCAO_CHECK_LAUNCH();
         { ProfScope _ps(SLOT_EIG_JACOBI, st); eig_jacobi_kernel<<<np, NT, jsm, st>>>(*P, leaf_ids, 30); }
         SCAO_CHECK_LAUNCH();
         // X = U V, AX = Y V
         g = {BUF_U, BUF_V, BUF_X, DIM_N, DIM_S, DIM_S, 0, 0};
-        { ProfScope _ps(SLOT_EIG_GEMM, 0); eig_gemm_kernel<<<dim3(tiles_nn, np), NT, 0, st>>>(*P, leaf_ids, g); }
+        { ProfScope _ps(SLOT_EIG_GEMM, st); eig_gemm_kernel<<<dim3(tiles_nn, np), NT, 0, st>>>(*P, leaf_ids, g); }
         SCAO_CHECK_LAUNCH();
         g = {BUF_Y, BUF_V, BUF_AX, DIM_N, DIM_S, DIM_S, 0, 0};
-        { ProfScope _ps(SLOT_EIG_GEMM, 0); eig_gemm_kernel<<<dim3(tiles_nn, np), NT, 0, st>>>(*P, leaf_ids, g); }
+        { ProfScope _ps(SLOT_EIG_GEMM, st); eig_gemm_kernel<<<dim3(tiles_nn, np), NT, 0, st>>>(*P, leaf_ids, g); }
         SCAO_CHECK_LAUNCH();
         { ProfScope _ps(SLOT_EIG_RESIDUAL, st); eig_residual_kernel<<<np, NT, 0, st>>>(*P, leaf_ids, tol, it, last); }
         SCAO_CHECK_LAUNCH();
         if (last) break;
         // CholeskyQR2 of the normalised AX: AX -> Y -> U
         g = {BUF_AX, BUF_AX, BUF_H, DIM_S, DIM_S, DIM_N, 1, 1};
-        { ProfScope _ps(SLOT_EIG_GEMM, 0); eig_gemm_kernel<<<dim3(tiles_ss, np), NT, 0, st>>>(*P, leaf_ids, g); }
+        { ProfScope _ps(SLOT_EIG_GEMM, st); eig_gemm_kernel<<<dim3(tiles_ss, np), NT, 0, st>>>(*P, leaf_ids, g); }
         SCAO_CHECK_LAUNCH();
         { ProfScope _ps(SLOT_EIG_CHOLINV, st); eig_cholinv_kernel<<<np, NT, csm, st>>>(*P, leaf_ids); }
         SCAO_CHECK_LAUNCH();
         g = {BUF_AX, BUF_H, BUF_Y, DIM_N, DIM_S, DIM_S, 0, 1};
-        { ProfScope _ps(SLOT_EIG_GEMM, 0); eig_gemm_kernel<<<dim3(tiles_nn, np), NT, 0, st>>>(*P, leaf_ids, g); }
+        { ProfScope _ps(SLOT_EIG_GEMM, st); eig_gemm_kernel<<<dim3(tiles_nn, np), NT, 0, st>>>(*P, leaf_ids, g); }
         SCAO_CHECK_LAUNCH();
         g = {BUF_Y, BUF_Y, BUF_H, DIM_S, DIM_S, DIM_N, 1, 1};
-        { ProfScope _ps(SLOT_EIG_GEMM, 0); eig_gemm_kernel<<<dim3(tiles_ss, np), NT, 0, st>>>(*P, leaf_ids, g); }
+        { ProfScope _ps(SLOT_EIG_GEMM, st); eig_gemm_kernel<<<dim3(tiles_ss, np), NT, 0, st>>>(*P, leaf_ids, g); }
         SCAO_CHECK_LAUNCH();
         { ProfScope _ps(SLOT_EIG_CHOLINV, st); eig_cholinv_kernel<<<np, NT, csm, st>>>(*P, leaf_ids); }
         SCAO_CHECK_LAUNCH();
         g = {BUF_Y, BUF_H, BUF_U, DIM_N, DIM_S, DIM_S, 0, 1};
-        { ProfScope _ps(SLOT_EIG_GEMM, 0); eig_gemm_kernel<<<dim3(tiles_nn, np), NT, 0, st>>>(*P, leaf_ids, g); }
+        { ProfScope _ps(SLOT_EIG_GEMM, st); eig_gemm_kernel<<<dim3(tiles_nn, np), NT, 0, st>>>(*P, leaf_ids, g); }
         SCAO_CHECK_LAUNCH();
     }
     { ProfScope _ps(SLOT_EIG_RANK, st); eig_rank_kernel<<<(n_ids + 127) / 128, 128, 0, st>>>(*P, leaf_ids, n_ids, eps_sparse, status); }
