@@ -1128,7 +1128,7 @@ proj_tma_kernel(ScaoPlanDev P, int* err) {
 constexpr int AT_EPI = SCAO_APPLY_EPI;          // epilogue threads (256 or 512)
 constexpr int AT_THREADS = 64 + AT_EPI;
 #ifndef SCAO_APPLY_ST
-#define SCAO_APPLY_ST 3
+#define SCAO_APPLY_ST 4
 #endif
 constexpr int AT_MAXST = 4;
 constexpr int AT_R = TMA_STATE_ROWS;                   // rows per chunk (16)
@@ -1141,12 +1141,17 @@ constexpr uint32_t AT_MG = AT_STAGE;                   // filter: magnitude EMA 
 constexpr uint32_t AT_STAGE_FN = AT_STAGE + AT_R * 128 * 4;   // 48 KB
 
 
-__host__ __device__ inline int apply_tma_stages(int kpm) { return kpm > 64 ? 2 : SCAO_APPLY_ST; }
 __host__ __device__ inline uint32_t apply_tma_ops_bytes(int kpm) { return 4u * 128 * kpm * 2; }
 __host__ __device__ inline uint32_t apply_tma_stage_bytes(bool fn) { return fn ? AT_STAGE_FN : AT_STAGE; }
+// as many stages (<= SCAO_APPLY_ST) as fit next to the operand tiles
+__host__ __device__ inline int apply_tma_stages(int kpm, bool fn) {
+    int s = SCAO_APPLY_ST;
+    while (s > 2 && apply_tma_ops_bytes(kpm) + (uint32_t)s * apply_tma_stage_bytes(fn) + 1024 > 232448u) --s;
+    return s;
+}
 size_t apply_tma_smem(int kpad_max, bool fn) {
     const int Kp = (kpad_max + 15) & ~15;
-    return (size_t)apply_tma_ops_bytes(Kp) + (size_t)apply_tma_stages(Kp) * apply_tma_stage_bytes(fn) +
+    return (size_t)apply_tma_ops_bytes(Kp) + (size_t)apply_tma_stages(Kp, fn) * apply_tma_stage_bytes(fn) +
            1024;
 }
 
@@ -1157,7 +1162,7 @@ apply_tma_kernel(ScaoPlanDev P, int* err) {
     extern __shared__ unsigned char asm_raw[];
     unsigned char* sm = (unsigned char*)(((uintptr_t)asm_raw + 1023) & ~(uintptr_t)1023);
     const int Kpm = (P.kpad_max + 15) & ~15;
-    const int nst = apply_tma_stages(Kpm);
+    const int nst = apply_tma_stages(Kpm, FN);
     constexpr uint32_t SBY = FN ? AT_STAGE_FN : AT_STAGE;
     const bool with_mg = FN && P.filt.mode != 0;
     unsigned char* ops = sm;                                  // [A hi|lo][B hi|lo]
@@ -1799,10 +1804,11 @@ extern "C" int scao_plan_step(const ScaoPlanDev* P, void* stream) {
         { ProfScope _ps(SLOT_APPLY_KRON, st);
           static bool aattr = false;
           if (!aattr) {
+              // the opt-in maximum: the launch size depends on kpad_max
               cudaFuncSetAttribute(apply_tma_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)apply_tma_smem(128, false));
+                                   232448);
               cudaFuncSetAttribute(apply_tma_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)apply_tma_smem(128, true));
+                                   232448);
               aattr = true;
           }
           const int g = scao_persistent_grid(P, P->n_tiles);
