@@ -1146,7 +1146,8 @@ __host__ __device__ inline uint32_t apply_tma_stage_bytes(bool fn) { return fn ?
 // as many stages (<= SCAO_APPLY_ST) as fit next to the operand tiles
 __host__ __device__ inline int apply_tma_stages(int kpm, bool fn) {
     int s = SCAO_APPLY_ST;
-    while (s > 2 && apply_tma_ops_bytes(kpm) + (uint32_t)s * apply_tma_stage_bytes(fn) + 1024 > 232448u) --s;
+    // 227 KB opt-in per block, less 1 KB for the kernel's static shared data
+    while (s > 2 && apply_tma_ops_bytes(kpm) + (uint32_t)s * apply_tma_stage_bytes(fn) + 1024 > 231424u) --s;
     return s;
 }
 size_t apply_tma_smem(int kpad_max, bool fn) {
@@ -1804,11 +1805,14 @@ extern "C" int scao_plan_step(const ScaoPlanDev* P, void* stream) {
         { ProfScope _ps(SLOT_APPLY_KRON, st);
           static bool aattr = false;
           if (!aattr) {
-              // the opt-in maximum: the launch size depends on kpad_max
-              cudaFuncSetAttribute(apply_tma_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   232448);
-              cudaFuncSetAttribute(apply_tma_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   232448);
+              // the largest launch size over kpad_max
+              size_t m0 = 0, m1 = 0;
+              for (int k = 16; k <= 128; k += 16) {
+                  m0 = apply_tma_smem(k, false) > m0 ? apply_tma_smem(k, false) : m0;
+                  m1 = apply_tma_smem(k, true) > m1 ? apply_tma_smem(k, true) : m1;
+              }
+              cudaFuncSetAttribute(apply_tma_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m0);
+              cudaFuncSetAttribute(apply_tma_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m1);
               aattr = true;
           }
           const int g = scao_persistent_grid(P, P->n_tiles);
