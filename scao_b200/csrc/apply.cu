@@ -853,13 +853,8 @@ apply_kron_tc_kernel(ScaoPlanDev P, int* err) {
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
                 const float gp = round_dt(fadd(gv[c], crv[c]), dt);
-#ifdef SCAO_EXP_LIGHT
-                mv[c] += gp; vv[c] += gp * gp; dv[c] -= gp; qv[c] = gv[c];
-                const float u = mv[c];
-#else
                 float u = adan_elem(S, dt, gf[c], gp, mv[c], vv[c], dv[c], qv[c], clip, clipmul);
                 if (FN && FD.gsnr_on) u = gsnr_mask(u, mv[c], vv[c], S.eps, FD.gsnr_thr);
-#endif
                 usq = fmaf(u, u, usq);
                 gsq = fmaf(gv[c], gv[c], gsq);
                 const float pd = round_dt(fmul(pv[c], wdm), dt);
@@ -1088,9 +1083,6 @@ proj_tma_kernel(ScaoPlanDev P, int* err) {
             // P_part = U_l[rows]^T T
             const int kp = L.kpad;
             float* out = P.p_part + (int64_t)T * P.p_stride;
-#ifdef SCAO_EXP_NOPB
-            if (kp > 0) continue;
-#endif
             if (ls_async) {
                 proj_pblock(Ls, Ts, ld, kp, pn.nrows, out, ok, et, PT_EPI);
             } else {
