@@ -204,8 +204,13 @@ def main():
                     help="N>1: reduce-scatter / step / all-gather pipeline buckets")
     ap.add_argument("--sm-reserve", type=int, default=32,
                     help="N>1: SMs the persistent kernels leave to the collectives")
+    ap.add_argument("--workload", default="llama-1b", choices=["llama-1b", "gpt2m-train"],
+                    help="gpt2m-train: the GPT-2-medium data-parallel training step "
+                         "(BASELINE config 2) instead of the headline optimizer step")
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3)
+    if a.workload == "gpt2m-train":
+        return gpt2_train_bench(a)
 
     from scao_b200 import workloads
     workload = workloads.c4(n_layers=a.layers)
@@ -527,6 +532,72 @@ def build_opt_list(workload, params_specs, scao_cls):
     if adam:
         groups.append({"params": adam, "warmup_steps": 10 ** 9})
     return scao_cls(groups, **workload.scao_kwargs)
+
+
+def gpt2_train_bench(a):
+    """GPT-2-medium training step (forward + backward under bf16 autocast +
+    SCAO step; per rank 8 x 1024 tokens, fp32 weights and state) on N GPUs,
+    data-parallel through the owner-compute ShardedSCAO; tokens/s over all
+    ranks, CUDA events, max over ranks."""
+    from scao_b200 import gpt, workloads
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        torch.distributed.init_process_group("nccl", device_id=dev)
+    c = gpt.GPT2_MEDIUM
+    model = gpt.GPT(c, seed=0).to(dev)
+    params = list(model.parameters())
+    kw = dict(lr=3e-4, betas=(0.9, 0.999), precond_freq=10, warmup_steps=20, blend_steps=50,
+              min_precond_updates=1, k_max=64, max_precond_dim=1024, use_int8_ema=True,
+              sparsity=0.0, noise_std_init=0.0, async_precond=False)
+    sharded = None
+    opt = None
+    if world > 1:
+        from scao_b200.distributed import ShardedSCAO
+        specs = [workloads.ParamSpec(f"p{i}", tuple(p.shape)) for i, p in enumerate(params)]
+        wl = workloads.Workload("gpt2-medium", specs, kw, 0, 0.0, "float32")
+        sharded = ShardedSCAO(params, wl, lambda ps: SCAO([p for p, _ in ps], **kw),
+                              buckets=a.buckets, sm_reserve=a.sm_reserve)
+    else:
+        opt = SCAO(params, **kw)
+    batch = 8
+    toks = [gpt.token_batch(c, batch, seed=1000 * rank + s, device=dev) for s in range(4)]
+    stream = torch.cuda.current_stream(dev)
+    for k in range(kw["warmup_steps"] + a.warmup):
+        gpt.train_step(model, opt, toks[k % 4], sharded)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    ev[0].record(stream)
+    losses = []
+    for k in range(a.steps):
+        losses.append(gpt.train_step(model, opt, toks[k % 4], sharded))
+    ev[1].record(stream)
+    torch.cuda.synchronize()
+    ms = ev[0].elapsed_time(ev[1]) / a.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = t.item()
+    if rank != 0:
+        return
+    tokens = world * batch * c.seq_len
+    print(json.dumps({
+        "metric": "GPT-2-medium training step (forward+backward+SCAO) tokens/s",
+        "value": round(tokens / (ms * 1e-3), 1), "unit": "tokens/s", "n_gpus": world,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms, 3),
+        "higher_is_better": True, "scaling": "weak", "dtype": "bf16 autocast, fp32 state",
+        "data": "synthetic tokens, uniform over the vocabulary",
+        "config": {"workload": "gpt2-medium-train", "layers": c.n_layer, "d_model": c.d_model,
+                   "heads": c.n_head, "d_ff": c.d_ff, "vocab": c.vocab, "seq_len": c.seq_len,
+                   "batch_per_gpu": batch, "params": sum(p.numel() for p in params),
+                   "parallelism": f"data-parallel x{world}, owner-compute SCAO"},
+        "loss_last": round(float(losses[-1].item()), 4),
+    }), flush=True)
 
 
 if __name__ == "__main__":

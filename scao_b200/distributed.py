@@ -171,13 +171,20 @@ class ShardedSCAO:
 
     def flat_grad_from_params(self):
         """Training-loop entry: gather every parameter's local .grad (as left
-        by backward) into the flat buffer."""
-        flat = torch.zeros(self.layout.total, dtype=self.dtype, device=self.device)
+        by backward) into the flat buffer, then point the owned parameters'
+        .grad back at their shard of the reduced gradient."""
+        if getattr(self, "_train_flat", None) is None:
+            self._train_flat = torch.zeros(self.layout.total, dtype=self.dtype, device=self.device)
+        flat = self._train_flat
         for i, p in enumerate(self.params):
-            if p.grad is None:
-                continue
             o = self.layout.global_offset(i)
-            flat[o:o + p.numel()].copy_(p.grad.reshape(-1))
+            if p.grad is None:
+                flat[o:o + p.numel()].zero_()
+            else:
+                flat[o:o + p.numel()].copy_(p.grad.reshape(-1))
+        for i in self.my:
+            o = self.layout.shard_offset(i)
+            self.params[i].grad = self.my_g[o:o + self.params[i].numel()].view_as(self.params[i])
         self.cur = flat
 
     # step -------------------------------------------------------------------
