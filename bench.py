@@ -539,7 +539,7 @@ def gpt2_train_bench(a):
     SCAO step; per rank 8 x 1024 tokens, fp32 weights and state) on N GPUs,
     data-parallel through the owner-compute ShardedSCAO; tokens/s over all
     ranks, CUDA events, max over ranks."""
-    from scao_b200 import gpt, workloads
+    from scao_b200 import SCAO, gpt, workloads
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
