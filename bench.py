@@ -598,6 +598,8 @@ def gpt2_train_bench(a):
                    "parallelism": f"data-parallel x{world}, owner-compute SCAO"},
         "loss_last": round(float(losses[-1].item()), 4),
     }), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
 
 
 if __name__ == "__main__":
