@@ -254,6 +254,13 @@ class SCAO(Optimizer):
         L = _lib.lib()
         if plan.step_event is not None:
             plan.step_event.synchronize()   # previous table upload has left the pinned buffer
+        # a bounded device wait that ran out in an earlier step (read back
+        # asynchronously; checked once its copy has landed, no synchronisation)
+        if plan.err_event is not None and plan.err_event.query():
+            plan.err_event = None
+            if int(plan.err_pin[0]):
+                raise RuntimeError("scao_b200: a device-side wait timed out in an earlier step "
+                                   "(results of that step are not valid)")
         self._global_step += 1
         ps, gs = self._flat()
         tab = plan.step_np
@@ -441,6 +448,10 @@ class SCAO(Optimizer):
         f.noise_std = float(np.float32(self._noise_std))
         f.noise_step = self._global_step
         _lib.check(L.scao_plan_step(pd, sp), "scao_plan_step")
+        if plan.err_event is None:
+            plan.err_pin.copy_(plan.err, non_blocking=True)
+            plan.err_event = torch.cuda.Event()
+            plan.err_event.record(stream)
         self._noise_std *= self._noise_anneal
         if la_now:
             _lib.check(L.scao_plan_lookahead(pd, float(self._lookahead_alpha),

@@ -18,7 +18,7 @@ from ._lib import CHUNK_DT, LEAF_DT, PANEL_DT, PARAM_DT, STEP_DT, TILE_DT
 
 TILE = 128       # apply tile edge (apply.cu TC_T)
 PANEL = 128      # projection panel rows
-CHUNK = 4096     # flat chunk length
+CHUNK = 16384    # flat chunk length (elements per block of the flat passes)
 SEL = 65536      # elements per chunk of the gradient filter's selection passes
 SMAX = 160       # largest eigen subspace width (eig.cu SMAX)
 
@@ -246,6 +246,8 @@ class Plan:
         self.param_scalars = z(self.n_params * 8)
         self.global_norm_ema = torch.ones(1, dtype=torch.float64, device=dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.err_pin = torch.zeros(1, dtype=torch.int32, pin_memory=torch.cuda.is_available())
+        self.err_event = None
         self.tmaps = torch.zeros(self.n_params * 10 * 128, dtype=torch.uint8, device=dev)
         self.tmap_cache = {}          # pointer-set key -> device buffer of maps (LRU order)
         # leaves whose panels the TMA projection can take (static part of its
