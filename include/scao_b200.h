@@ -375,6 +375,11 @@ SCAO_API int scao_tc_selftest(const uint16_t* A, const uint16_t* B, float* C, in
 /* Check of the division-by-constant rewrite used by the Adan update: counts
  * x[i] / c[i % 1024] where reciprocal-plus-FMA-correction differs from the
  * IEEE quotient (adds into *mismatches).                                   */
+/* Self-check of the bounded device waits (no reference counterpart): one
+ * kernel waits on an mbarrier nothing arrives at, with an iteration limit;
+ * it must give up, write 1 to *err (device int) and return normally.      */
+SCAO_API int scao_wait_timeout_check(int* err, unsigned int limit, void* stream);
+
 SCAO_API int scao_divc_check(const float* x, const float* c, int n, int* mismatches,
                              void* stream);
 

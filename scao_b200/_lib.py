@@ -125,6 +125,7 @@ SIGNATURES = {
                                       C.c_double, _P, C.c_int64, _P, _P, _P, _P, _P]),
     "scao_ema_scratch_bytes": (C.c_int64, [C.c_int, C.c_int, C.c_int]),
     "scao_plan_tensor_maps": (C.c_int, [C.POINTER(PlanDev), _P, _P, _P]),
+    "scao_wait_timeout_check": (C.c_int, [_P, C.c_uint, _P]),
     "scao_plan_grad_norms": (C.c_int, [C.POINTER(PlanDev), _P, _P]),
     "scao_plan_curvature_diag": (C.c_int, [C.POINTER(PlanDev), _P, C.c_int, C.c_double, _P]),
     "scao_plan_eigen": (C.c_int, [C.POINTER(PlanDev), _P, C.c_int, _P, _P, C.c_int,

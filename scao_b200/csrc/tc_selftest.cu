@@ -103,3 +103,30 @@ extern "C" int scao_divc_check(const float* x, const float* c, int n, int* misma
     SCAO_CHECK_LAUNCH();
     return SCAO_OK;
 }
+
+namespace {
+
+// An mbarrier wait that nobody satisfies: the bounded wait must give up,
+// record the error in *err and return (no trap, the context stays usable).
+__global__ void wait_timeout_kernel(int* err, uint32_t limit) {
+    __shared__ uint64_t mbar;
+    if (threadIdx.x == 0) {
+        mbar_init(&mbar, 1);
+        fence_async_smem();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const bool ok = mbar_wait(&mbar, 0, limit);
+        *err = ok ? 0 : 1;
+    }
+}
+
+}  // namespace
+
+extern "C" int scao_wait_timeout_check(int* err, unsigned int limit, void* stream) {
+    if (!err) return SCAO_ERR_ARG;
+    { ProfScope _ps(SLOT_SEAM, (cudaStream_t)stream);
+      wait_timeout_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(err, limit); }
+    SCAO_CHECK_LAUNCH();
+    return SCAO_OK;
+}

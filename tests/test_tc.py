@@ -40,3 +40,33 @@ def test_division_by_constant_is_ieee():
                                  torch.cuda.current_stream().cuda_stream), "divc")
     torch.cuda.synchronize()
     assert m.item() == 0
+
+
+def test_bounded_wait_gives_up_and_context_survives():
+    """A wait nobody satisfies runs out, reports through the status flag, and
+    the context keeps working (a tensor-core self-check right after)."""
+    L = _lib.lib()
+    err = torch.full((1,), -1, dtype=torch.int32, device="cuda")
+    _lib.check(L.scao_wait_timeout_check(err.data_ptr(), 1 << 16,
+                                         torch.cuda.current_stream().cuda_stream), "wait")
+    torch.cuda.synchronize()
+    assert int(err.item()) == 1
+    x = torch.ones(1024, device="cuda")
+    assert float((x * 2).sum().item()) == 2048.0
+
+
+def test_device_error_flag_raises_on_a_later_step():
+    """A timed-out wait inside a step (simulated by setting the plan's error
+    flag) is reported by an exception on a following step."""
+    from scao_b200 import SCAO
+    p = torch.nn.Parameter(torch.zeros(64, 32, device="cuda"))
+    opt = SCAO([p], sparsity=0.0, noise_std_init=0.0)
+    p.grad = torch.ones_like(p)
+    opt.step()
+    torch.cuda.synchronize()
+    opt._plan.err.fill_(1)
+    with pytest.raises(RuntimeError, match="timed out"):
+        for _ in range(4):
+            p.grad = torch.ones_like(p)
+            opt.step()
+            torch.cuda.synchronize()
