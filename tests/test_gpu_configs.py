@@ -39,3 +39,43 @@ def test_config0_full_run_matches_oracle():
         assert _rel(p.detach().cpu().numpy() - a0, orc.params[i] - a0) < 1e-3, i
         assert _rel(st["exp_avg"].cpu().numpy(), orc.state[i]["m"]) < 1e-3, i
         assert _rel(st["exp_avg_sq"].cpu().numpy(), orc.state[i]["v"]) < 1e-3, i
+
+
+def _llama_run(n_layers=2, steps=24):
+    w = workloads.c4(n_layers=n_layers)
+    params = [torch.nn.Parameter(p) for p in synthetic.init_params(w, device="cuda")]
+    specs = list(w.params)
+    groups = [{"params": [p for p, s in zip(params, specs) if not s.adam_only]},
+              {"params": [p for p, s in zip(params, specs) if s.adam_only],
+               "warmup_steps": 10 ** 9}]
+    opt = SCAO(groups, **w.scao_kwargs)
+    gen = synthetic.LowRankGradients(w, device="cuda")
+    for _ in range(steps):
+        for p, g in zip(params, gen.next()):
+            p.grad = g
+        opt.step()
+    torch.cuda.synchronize()
+    opt._plan.check_error()
+    return params, opt
+
+
+def test_llama_shapes_properties():
+    """Llama-1B layer shapes (2 layers + embedding, bf16, int8 EMA) through the
+    warmup into Phase 2 and two curvature refreshes: every step is
+    deterministic (two runs bit-identical), the int8 factors are symmetric,
+    ranks stay inside their bounds, values stay finite."""
+    pa, oa = _llama_run()
+    pb, ob = _llama_run()
+    for x, y in zip(pa, pb):
+        assert torch.equal(x, y)
+        assert torch.isfinite(x.float()).all()
+    plan = oa._plan
+    for li in range(plan.n_leaves):
+        for side in (0, 1):
+            L = plan.ltab[li]
+            n = int(L["a"] if side == 0 else L["b"])
+            o = int(L["lq_off"] if side == 0 else L["rq_off"])
+            q = plan.fac[o:o + n * n].view(n, n)
+            assert torch.equal(q, q.T), (li, side)
+    ks = plan.k.cpu().numpy()
+    assert (ks >= plan.ltab["kmin"]).all() and (ks <= plan.ltab["kmax"]).all()
