@@ -1196,14 +1196,20 @@ apply_tma_kernel(ScaoPlanDev P, int* err) {
                     const int y = L.row0 + tl.row0 + c * AT_R;
                     mbar_expect_tx(&full[stage], with_mg ? AT_STAGE_FN : AT_STAGE);
                     const uint32_t s = smem_u32(stg + (size_t)stage * SBY);
-                    if (with_mg)
-                        tma_load_2d(s + AT_MG, scao_tmap(P.tmaps, L.param, TM_MG), x, y, &full[stage]);
-                    tma_load_2d(s + AT_G, scao_tmap(P.tmaps, L.param, TM_GS), x, y, &full[stage]);
-                    tma_load_2d(s + AT_P, scao_tmap(P.tmaps, L.param, TM_PS), x, y, &full[stage]);
-                    tma_load_2d(s + AT_M, scao_tmap(P.tmaps, L.param, TM_M), x, y, &full[stage]);
-                    tma_load_2d(s + AT_V, scao_tmap(P.tmaps, L.param, TM_V), x, y, &full[stage]);
-                    tma_load_2d(s + AT_D, scao_tmap(P.tmaps, L.param, TM_D), x, y, &full[stage]);
-                    tma_load_2d(s + AT_PV, scao_tmap(P.tmaps, L.param, TM_PV), x, y, &full[stage]);
+#ifdef SCAO_APPLY_EVF
+                    const uint64_t pol = l2_policy_evict_first();
+#define AT_LOAD(off, slot) tma_load_2d_hint(s + off, scao_tmap(P.tmaps, L.param, slot), x, y, &full[stage], pol)
+#else
+#define AT_LOAD(off, slot) tma_load_2d(s + off, scao_tmap(P.tmaps, L.param, slot), x, y, &full[stage])
+#endif
+                    if (with_mg) AT_LOAD(AT_MG, TM_MG);
+                    AT_LOAD(AT_G, TM_GS);
+                    AT_LOAD(AT_P, TM_PS);
+                    AT_LOAD(AT_M, TM_M);
+                    AT_LOAD(AT_V, TM_V);
+                    AT_LOAD(AT_D, TM_D);
+                    AT_LOAD(AT_PV, TM_PV);
+#undef AT_LOAD
                     issued |= 1u << stage;
                     last_ph = (last_ph & ~(1u << stage)) | (ph << stage);
                     if (++stage == nst) { stage = 0; ph ^= 1; }
@@ -1361,11 +1367,18 @@ apply_tma_kernel(ScaoPlanDev P, int* err) {
                     if (okc) {
                         const int y = L.row0 + tl.row0 + c * AT_R;
                         const uint32_t s = smem_u32(st);
-                        tma_store_2d(scao_tmap(P.tmaps, L.param, TM_US), x, y, s + AT_G);
-                        tma_store_2d(scao_tmap(P.tmaps, L.param, TM_M), x, y, s + AT_M);
-                        tma_store_2d(scao_tmap(P.tmaps, L.param, TM_V), x, y, s + AT_V);
-                        tma_store_2d(scao_tmap(P.tmaps, L.param, TM_D), x, y, s + AT_D);
-                        tma_store_2d(scao_tmap(P.tmaps, L.param, TM_PV), x, y, s + AT_PV);
+#ifdef SCAO_APPLY_EVF
+                        const uint64_t pol = l2_policy_evict_first();
+#define AT_STORE(slot, off) tma_store_2d_hint(scao_tmap(P.tmaps, L.param, slot), x, y, s + off, pol)
+#else
+#define AT_STORE(slot, off) tma_store_2d(scao_tmap(P.tmaps, L.param, slot), x, y, s + off)
+#endif
+                        AT_STORE(TM_US, AT_G);
+                        AT_STORE(TM_M, AT_M);
+                        AT_STORE(TM_V, AT_V);
+                        AT_STORE(TM_D, AT_D);
+                        AT_STORE(TM_PV, AT_PV);
+#undef AT_STORE
                         bulk_commit();
                         bulk_wait_read0();
                     }

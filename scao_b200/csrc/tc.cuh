@@ -197,3 +197,22 @@ TC_DEV void tc_ld4(uint32_t taddr, float* v) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) v[i] = __uint_as_float(r[i]);
 }
+
+// L2 eviction-priority policies for TMA copies of streamed data
+TC_DEV uint64_t l2_policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+TC_DEV void tma_load_2d_hint(uint32_t dst, const void* map, int x, int y, uint64_t* mbar,
+                             uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint "
+        "[%0], [%1, {%2, %3}], [%4], %5;"
+        :: "r"(dst), "l"(map), "r"(x), "r"(y), "r"(smem_u32(mbar)), "l"(policy) : "memory");
+}
+TC_DEV void tma_store_2d_hint(const void* map, int x, int y, uint32_t src, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%1, %2}], [%3], %4;"
+        :: "l"(map), "r"(x), "r"(y), "r"(src), "l"(policy) : "memory");
+}
