@@ -346,6 +346,10 @@ def main():
     per_elem = (38 if b16 else 44) + (4 if a.sparsity > 0 else 0)
     k_ms, k_n = prof.get("apply_kron", (0.0, 0))
     k_avg = k_ms / max(k_n, 1)
+    # with bucketed owner-compute (N > 1) one step launches the kernel once
+    # per bucket: bytes and elements per launch are the step's share
+    k_lps = max(k_n / max(a.steps, 1), 1.0)
+    kron_elems = kron_elems / k_lps
     k_bytes = per_elem * kron_elems
     k_achieved = k_bytes / (k_avg * 1e-3) / 1e9 if k_avg > 0 else 0.0
     # DRAM bytes per launch from an ncu capture of the same kernel on the
@@ -496,8 +500,9 @@ def main():
                      "unit": "GB/s", "frac": round(k_achieved / hbm, 4),
                      "traffic": round(k_traffic) if k_traffic else None,
                      "kernel": "apply (Kronecker correction + Adan + state write-back), slot apply_kron",
-                     "algorithmic_bytes_per_launch": k_bytes,
-                     "bytes_per_elem": per_elem, "elems_per_launch": kron_elems,
+                     "algorithmic_bytes_per_launch": round(k_bytes),
+                     "bytes_per_elem": per_elem, "elems_per_launch": round(kron_elems),
+                     "launches_per_step": round(k_lps, 2),
                      "avg_launch_ms": round(k_avg, 3), "peak_source": pname,
                      "apply_sequence": {"kernels": "+".join(apply_slots),
                                         "algorithmic_bytes_per_step": abytes,

@@ -56,17 +56,58 @@ class FlatLayout:
         n = len(numels)
         self.bucket = [0] * n
         self.offsets = [0] * n
+        size = [_round_up(x, ALIGN) for x in numels]
+        # each rank's items, largest first (ties by index)
+        queue = [sorted((i for i in range(n) if owner[i] == r), key=lambda i: (-size[i], i))
+                 for r in range(world)]
         fill = {}
-        for r in range(world):
-            mine = [i for i in range(n) if owner[i] == r]
-            tot = sum(_round_up(numels[i], ALIGN) for i in mine)
-            acc = 0
-            for i in mine:
-                b = min(buckets - 1, int(acc * buckets // max(tot, 1)))
-                self.bucket[i] = b
-                self.offsets[i] = fill.get((r, b), 0)
-                fill[(r, b)] = self.offsets[i] + _round_up(numels[i], ALIGN)
-                acc += _round_up(numels[i], ALIGN)
+
+        def pick(q, cap):
+            """Largest-first fit of q's items into cap (the largest always)."""
+            took, f = [], 0
+            for i in q:
+                if not took or f + size[i] <= cap:
+                    took.append(i)
+                    f += size[i]
+            return took, f
+
+        # Buckets are filled for all ranks together so that each bucket's
+        # segment (the max over ranks) carries little padding: a bucket's
+        # segment is set by the rank that needs most for a target share of
+        # its remaining load (its largest item at least), then every rank
+        # packs up to it; the last bucket takes what is left.  A few target
+        # shares per bucket are tried and the layout with the smallest sum of
+        # segments is kept.  Within a bucket items keep model order.
+        def plan(queue, b):
+            if b == buckets - 1:
+                return (max(sum(size[i] for i in q) for q in queue), [list(q) for q in queue]),
+            base = max(sum(size[i] for i in q) for q in queue) / (buckets - b)
+            if base == 0:
+                return ((0, [[] for _ in queue]),) * (buckets - b)
+            best = None
+            for s in (0.8, 0.9, 1.0, 1.12, 1.25):
+                seg = max(pick(q, base * s)[1] if q else 0 for q in queue)
+                took = [pick(q, seg)[0] if q else [] for q in queue]
+                rest = [[i for i in q if i not in ts] for q, ts in zip(queue, map(set, took))]
+                tail = plan(rest, b + 1)
+                tot = max(sum(size[i] for i in t) for t in took) + sum(x[0] for x in tail)
+                # the first bucket's reduce-scatter and the last one's
+                # all-gather are the pipeline's exposed ends: large end
+                # segments are charged a little extra
+                tot += 0.1 * tail[-1][0]
+                if b == 0:
+                    tot += 0.1 * max(sum(size[i] for i in t) for t in took)
+                if best is None or tot < best[0]:
+                    best = (tot, ((max(sum(size[i] for i in t) for t in took), took),) + tail)
+            return best[1]
+
+        for b, (_, took) in enumerate(plan(queue, 0)):
+            for r in range(world):
+                f = 0
+                for i in sorted(took[r]):
+                    self.bucket[i], self.offsets[i] = b, f
+                    f += size[i]
+                fill[(r, b)] = f
         self.nb = buckets
         self.seg = [max([fill.get((r, b), 0) for r in range(world)] + [ALIGN])
                     for b in range(buckets)]

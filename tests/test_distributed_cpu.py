@@ -37,6 +37,20 @@ def test_flat_layout_disjoint_aligned():
         assert lay.shard == sum(lay.seg)
 
 
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_flat_layout_padding_llama_shapes(world):
+    """The bucket-major layout of the Llama-1B parameter set carries little
+    padding (each collective moves world x segment elements), every bucket
+    holds parameters of every rank that owns any, and items stay disjoint."""
+    numels = [int(torch.Size(s.shape).numel()) for s in workloads.c4().params]
+    owner = partition(numels, world)
+    lay = FlatLayout(numels, owner, world, 4)
+    assert lay.total <= 1.06 * sum(numels)
+    spans = sorted((lay.global_offset(i), lay.global_offset(i) + n) for i, n in enumerate(numels))
+    assert all(a1 <= b0 for (_, a1), (b0, _) in zip(spans, spans[1:]))
+    assert all(lay.offsets[i] + numels[i] <= lay.seg[lay.bucket[i]] for i in range(len(numels)))
+
+
 class _SGD:
     """Stand-in for the per-rank optimizer: p -= 0.1 * grad (grads are views
     into the reduce-scattered shard)."""
