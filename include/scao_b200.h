@@ -119,6 +119,14 @@ typedef struct { int32_t leaf, row0, nrows, pad0; } ScaoPanel;
 /* Flat chunk of a parameter (element range).                               */
 typedef struct { int32_t param, pad0; int64_t begin, end; } ScaoChunk;
 
+/* Diagonal strip of a block-diagonal parameter: a remainder block of width 1
+ * (1 x b or a x 1) of the recursive split, which the reference gives a
+ * diagonal sub-preconditioner (preconditioner.py:142-156, 232-236;
+ * precondition :506-510, curvature :332-339, natural norm :554-556).  Its
+ * elements are begin + j * stride, j < count (stride 1: a row, stride = the
+ * parameter's columns: a column).                                           */
+typedef struct { int32_t param, count, stride, pad0; int64_t begin; } ScaoStrip;
+
 /* Gradient filter (scao/optimizer.py:40-97, applied at :536-542) and
  * gradient noise (:544-545).  The filtered gradient
  *     grad * (mag_ema >= quantile(mag_ema, sparsity))
@@ -222,6 +230,10 @@ typedef struct {
     int32_t gnorm_host;          /* 1: the host maintains *global_norm_ema
                                     this step (the kernels only read it)    */
     ScaoFilterDev filt;          /* gradient filter and noise (mode 0: off) */
+    const ScaoStrip* strips;     /* diagonal strips of Kronecker params      */
+    float* strip_part;           /* per strip: |u|^2, |g|^2, |p_dec|^2, nat^2 */
+    int32_t n_strips;
+    int32_t pad6_;
 } ScaoPlanDev;
 
 /* ---------------------------------------------------------------------- */

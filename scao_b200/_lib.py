@@ -45,6 +45,8 @@ TILE_DT = np.dtype([("leaf", "<i4"), ("row0", "<i4"), ("col0", "<i4"), ("pad0", 
 PANEL_DT = np.dtype([("leaf", "<i4"), ("row0", "<i4"), ("nrows", "<i4"), ("pad0", "<i4")])
 CHUNK_DT = np.dtype([("param", "<i4"), ("pad0", "<i4"), ("begin", "<i8"), ("end", "<i8")],
                     align=True)
+STRIP_DT = np.dtype([("param", "<i4"), ("count", "<i4"), ("stride", "<i4"), ("pad0", "<i4"),
+                     ("begin", "<i8")], align=True)
 
 _P = C.c_void_p
 
@@ -90,6 +92,7 @@ class PlanDev(C.Structure):
         ("err", _P),
         ("tmaps", _P), ("tmaps_ok", C.c_int32), ("gnorm_host", C.c_int32),
         ("filt", FilterDev),
+        ("strips", _P), ("strip_part", _P), ("n_strips", C.c_int32), ("pad6_", C.c_int32),
     ]
 
 
@@ -98,6 +101,7 @@ def check_layout():
     assert STEP_DT.itemsize == 128, STEP_DT.itemsize
     assert LEAF_DT.itemsize == 160, LEAF_DT.itemsize
     assert CHUNK_DT.itemsize == 24, CHUNK_DT.itemsize
+    assert STRIP_DT.itemsize == 24, STRIP_DT.itemsize
     assert FILTER_PARAM_DT.itemsize == 80, FILTER_PARAM_DT.itemsize
     assert C.sizeof(FilterDev) == 120, C.sizeof(FilterDev)
 

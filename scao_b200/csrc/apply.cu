@@ -77,6 +77,29 @@ diag_pre_kernel(ScaoPlanDev P) {
 }
 
 // ---------------------------------------------------------------------------
+// diagonal strips of Kronecker params (width-1 blocks of the split): their
+// natural-norm^2 sum(g^2 / (sqrt(diag_ema) + eps)) (preconditioner.py:554-556)
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(NT)
+strip_pre_kernel(ScaoPlanDev P) {
+    const ScaoStrip sp = P.strips[blockIdx.x];
+    const ScaoParam& pr = P.params[sp.param];
+    const ScaoParamStep& S = P.step[sp.param];
+    if (S.phase != 2) return;
+    __shared__ float red[32];
+    const void* g = (const void*)S.g_ptr;
+    const float* de = P.diag_ema + pr.offset;
+    float nat = 0.f;
+    for (int j = threadIdx.x; j < sp.count; j += NT) {
+        const int64_t e = sp.begin + (int64_t)j * sp.stride;
+        const float gv = load_dt(g, e, pr.dtype);
+        nat += fdiv(fmul(gv, gv), fadd(sqrtf(de[e]), S.eps));
+    }
+    nat = block_sum(nat, red);
+    if (threadIdx.x == 0) P.strip_part[blockIdx.x * 4 + 3] = nat;
+}
+
+// ---------------------------------------------------------------------------
 // per leaf: reduce panels, natural norm, Delta, W = U_l Delta
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(NT)
@@ -202,6 +225,11 @@ param_pre_kernel(ScaoPlanDev P) {
             const float bn = sqrtf(P.leaf_nat2[l]);
             nat2 = fmaf(bn, bn, nat2);
         }
+        for (int s = threadIdx.x; s < P.n_strips; s += NT)
+            if (P.strips[s].param == pi) {
+                const float bn = sqrtf(P.strip_part[s * 4 + 3]);
+                nat2 = fmaf(bn, bn, nat2);
+            }
     } else {
         for (int c = pr.chunk_begin + threadIdx.x; c < pr.chunk_end; c += NT) {
             nat2 += P.chunk_part[c * 4 + 2];
@@ -364,6 +392,66 @@ apply_flat_kernel(ScaoPlanDev P) {
 }
 
 // ---------------------------------------------------------------------------
+// Phase 2 on the diagonal strips of Kronecker params: the diagonal
+// preconditioner g / ((diag_ema / bias)^(1/4) + 1e-8) (preconditioner.py:
+// 506-510), rounded to the parameter dtype like every block's output, then
+// the same Adan element step as the Kronecker tiles
+// ---------------------------------------------------------------------------
+template <bool FN>
+__global__ void __launch_bounds__(NT)
+strip_apply_kernel(ScaoPlanDev P) {
+    const ScaoStrip sp = P.strips[blockIdx.x];
+    const int pi = sp.param;
+    const ScaoParam& pr = P.params[pi];
+    const ScaoParamStep& S = P.step[pi];
+    if (S.phase != 2) return;
+    __shared__ float red[32];
+    const int dt = pr.dtype;
+    const void* g = (const void*)S.g_ptr;
+    const void* pp = (const void*)S.p_ptr;
+    float* M = P.exp_avg + pr.offset;
+    float* V = P.exp_avg_sq + pr.offset;
+    float* Dd = P.exp_avg_diff + pr.offset;
+    float* Pv = P.prev_grad + pr.offset;
+    const float* de = P.diag_ema + pr.offset;
+    const float* ps = P.param_scalars + pi * 8;
+    const bool clip = ps[PS_CLIP] != 0.f;
+    const float clipmul = ps[PS_CLIPMUL];
+    const ScaoFilterDev& FD = P.filt;
+    const float thr = (FN && FD.mode) ? FD.fp[pi].thr : 0.f;
+    float usq = 0.f, gsq = 0.f, psq = 0.f;
+    for (int j = threadIdx.x; j < sp.count; j += NT) {
+        const int64_t e = sp.begin + (int64_t)j * sp.stride;
+        const float gv = load_dt(g, e, dt);
+        const float den = fadd(powf(fdiv(de[e], S.diag_bias), 0.25f), 1e-8f);
+        const float gp = round_dt(fdiv(gv, den), dt);
+        float gf = gv;
+        if (FN)
+            gf = filt_grad(FD, gv, FD.mode ? FD.mag_ema[pr.offset + e] : 0.f, thr,
+                           FD.noise_on ? f4_get(noise_normal4(FD.noise_seed, pi, FD.noise_step, e >> 2),
+                                                (int)(e & 3)) : 0.f);
+        float m = M[e], v = V[e], d = Dd[e], pv = Pv[e];
+        float u = adan_elem(S, dt, gf, gp, m, v, d, pv, clip, clipmul);
+        if (FN && FD.gsnr_on) u = gsnr_mask(u, m, v, S.eps, FD.gsnr_thr);
+        usq = fmaf(u, u, usq);
+        gsq = fmaf(gv, gv, gsq);
+        const float pd = round_dt(fmul(load_dt(pp, e, dt), S.wd_mult), dt);
+        psq = fmaf(pd, pd, psq);
+        M[e] = m; V[e] = v; Dd[e] = d; Pv[e] = pv;
+        if (dt == SCAO_F32) P.upd32[pr.offset + e] = u;
+        else store_dt(P.upd + pr.offset, e, dt, u);
+    }
+    usq = block_sum(usq, red);
+    gsq = block_sum(gsq, red);
+    psq = block_sum(psq, red);
+    if (threadIdx.x == 0) {
+        P.strip_part[blockIdx.x * 4 + 0] = usq;
+        P.strip_part[blockIdx.x * 4 + 1] = gsq;
+        P.strip_part[blockIdx.x * 4 + 2] = psq;
+    }
+}
+
+// ---------------------------------------------------------------------------
 // per param: LARS trust ratio (optimizer.py:371-377) -> alpha
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(NT)
@@ -381,6 +469,12 @@ param_post_kernel(ScaoPlanDev P) {
             gsq += P.tile_part[t * 4 + 1];
             psq += P.tile_part[t * 4 + 2];
         }
+        for (int s = threadIdx.x; s < P.n_strips; s += NT)
+            if (P.strips[s].param == pi) {
+                usq += P.strip_part[s * 4 + 0];
+                gsq += P.strip_part[s * 4 + 1];
+                psq += P.strip_part[s * 4 + 2];
+            }
     } else {
         for (int c = pr.chunk_begin + threadIdx.x; c < pr.chunk_end; c += NT) {
             usq += P.chunk_part[c * 4 + 0];
@@ -1804,6 +1898,10 @@ extern "C" int scao_plan_step(const ScaoPlanDev* P, void* stream) {
         }
         SCAO_CHECK_LAUNCH();
     }
+    if (P->n_strips > 0) {
+        { ProfScope _ps(SLOT_DIAG_PRE, st); strip_pre_kernel<<<P->n_strips, NT, 0, st>>>(*P); }
+        SCAO_CHECK_LAUNCH();
+    }
     { ProfScope _ps(SLOT_PARAM_PRE, st); param_pre_kernel<<<P->n_params, NT, 0, st>>>(*P); }
     SCAO_CHECK_LAUNCH();
     if (P->n_tiles > 0) {
@@ -1837,6 +1935,12 @@ extern "C" int scao_plan_step(const ScaoPlanDev* P, void* stream) {
             if (fn) apply_flat_kernel<true><<<P->n_flat, NT, 0, st>>>(*P);
             else apply_flat_kernel<false><<<P->n_flat, NT, 0, st>>>(*P);
         }
+        SCAO_CHECK_LAUNCH();
+    }
+    if (P->n_strips > 0) {
+        { ProfScope _ps(SLOT_APPLY_FLAT, st);
+          if (fn) strip_apply_kernel<true><<<P->n_strips, NT, 0, st>>>(*P);
+          else strip_apply_kernel<false><<<P->n_strips, NT, 0, st>>>(*P); }
         SCAO_CHECK_LAUNCH();
     }
     { ProfScope _ps(SLOT_PARAM_POST, st); param_post_kernel<<<P->n_params, NT, 0, st>>>(*P); }

@@ -751,6 +751,20 @@ __global__ void diag_ema_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids,
     const ScaoParamStep& S = P.step[pi];
     const void* g = (const void*)S.g_ptr;
     float* d = P.diag_ema + pr.offset;
+    if (pr.mode == 1) {
+        // a Kronecker param: only its diagonal strips (width-1 blocks)
+        for (int s = 0; s < P.n_strips; ++s) {
+            const ScaoStrip sp = P.strips[s];
+            if (sp.param != pi) continue;
+            for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < sp.count;
+                 j += gridDim.x * blockDim.x) {
+                const int64_t e = sp.begin + (int64_t)j * sp.stride;
+                const float gv = load_dt(g, e, pr.dtype);
+                d[e] = __fadd_rn(__fmul_rn(d[e], rho_f), __fmul_rn(alpha_f, __fmul_rn(gv, gv)));
+            }
+        }
+        return;
+    }
     for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < pr.numel;
          e += (int64_t)gridDim.x * blockDim.x) {
         const float gv = load_dt(g, e, pr.dtype);

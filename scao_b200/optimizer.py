@@ -344,7 +344,8 @@ class SCAO(Optimizer):
                     bf = 1.0 - rho ** pc.precond_step
                     eig_leaves.extend(leaves)
                     eig_bias.extend([bf] * len(leaves))
-                else:
+                if not leaves or plan.param_strips[i]:
+                    # diagonal params, and the width-1 strips of Kronecker ones
                     curv_diag.setdefault(rho, []).append(i)
             row["lr"] = lr
             row["wd"] = wd

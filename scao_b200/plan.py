@@ -14,7 +14,7 @@ import numpy as np
 import torch
 
 from . import _lib
-from ._lib import CHUNK_DT, LEAF_DT, PANEL_DT, PARAM_DT, STEP_DT, TILE_DT
+from ._lib import CHUNK_DT, LEAF_DT, PANEL_DT, PARAM_DT, STEP_DT, STRIP_DT, TILE_DT
 
 TILE = 128       # apply tile edge (apply.cu TC_T)
 PANEL = 128      # projection panel rows
@@ -38,9 +38,11 @@ def to_2d_shape(shape):
 
 
 def split_blocks(m, n, mpd):
-    """Leaf blocks (row0, col0, a, b) of the recursive block-diagonal split of
-    preconditioner.py:142-194.  Raises for remainder blocks of width 1, which
-    the reference turns into diagonal sub-preconditioners."""
+    """Blocks (row0, col0, a, b) of the recursive block-diagonal split of
+    preconditioner.py:142-194.  A block of width 1 (a == 1 or b == 1, the
+    remainder of a dimension one above a multiple of max_precond_dim) is a
+    diagonal sub-preconditioner there (:142-156, 232-236): it is returned as
+    is and becomes a diagonal strip of the plan."""
     if max(m, n) <= mpd:
         return [(0, 0, m, n)]
     large, small = (m, n) if m >= n else (n, m)
@@ -48,21 +50,19 @@ def split_blocks(m, n, mpd):
     out, off = [], 0
     for bs in sizes:
         bm, bn = (bs, small) if m >= n else (small, bs)
-        if bm <= 1 or bn <= 1:
-            raise NotImplementedError(
-                f"block split of a {m}x{n} parameter at max_precond_dim={mpd} leaves a "
-                f"{bm}x{bn} block, which the reference preconditions diagonally; "
-                "not supported by scao_b200 yet")
-        for (r, c, a, b) in split_blocks(bm, bn, mpd):
+        sub = [(0, 0, bm, bn)] if bm <= 1 or bn <= 1 else split_blocks(bm, bn, mpd)
+        for (r, c, a, b) in sub:
             out.append((r + off, c, a, b) if m >= n else (r, c + off, a, b))
         off += bs
     return out
 
 
 def split_tree(m, n, mpd):
-    """Nesting of the block split: an int count of leaves for a Kronecker
-    block, or a list of sub-trees for a block-diagonal one (the reference's
-    ``_blocks`` hierarchy, preconditioner.py:163-194)."""
+    """Nesting of the block split: 1 for a Kronecker block, 0 for a diagonal
+    (width-1) block, or a list of sub-trees for a block-diagonal one (the
+    reference's ``_blocks`` hierarchy, preconditioner.py:163-194)."""
+    if m <= 1 or n <= 1:
+        return 0
     if max(m, n) <= mpd:
         return 1
     large, small = (m, n) if m >= n else (n, m)
@@ -97,8 +97,10 @@ class Plan:
         self.int8_ema = bool(int8_ema)
         self.n_params = len(params)
         ptab = np.zeros(self.n_params, PARAM_DT)
-        leaves, tiles, panels, chunks = [], [], [], []
+        leaves, tiles, panels, chunks, strips = [], [], [], [], []
         self.param_leaves = []
+        self.param_strips = []
+        self.param_blocks = []     # per param, in split order: ("L", leaf) / ("S", strip)
         self.param_trees = []
         off = 0
         fac_off = 0
@@ -126,10 +128,18 @@ class Plan:
             r["leaf_begin"] = len(leaves)
             r["tile_begin"] = len(tiles)
             r["chunk_begin"] = len(chunks)
-            mine = []
+            mine, mine_s, order = [], [], []
             if kron:
                 blocks = split_blocks(m, n, g["max_precond_dim"])
                 for (r0, c0, a, b) in blocks:
+                    if a == 1 or b == 1:
+                        # diagonal strip: a row (stride 1) or a column (stride n)
+                        order.append(("S", len(strips)))
+                        mine_s.append(len(strips))
+                        strips.append((i, b if a == 1 else a, 1 if a == 1 else n, 0,
+                                       r0 * n + c0))
+                        continue
+                    order.append(("L", len(leaves)))
                     kmin, kmax = k_bounds(a, b, g["k_min"], g["k_max"])
                     kpad = _round_up(max(kmax, 1), 8)
                     if kpad > 128:
@@ -179,7 +189,13 @@ class Plan:
                     mine.append(li)
                     self.eps_sparse.append(g["epsilon_sparse"])
                     self.rho_leaf.append(g["rho"])
+            if kron and not mine:
+                raise NotImplementedError(
+                    f"max_precond_dim={g['max_precond_dim']} leaves no Kronecker block in a "
+                    f"{m}x{n} parameter")
             self.param_leaves.append(mine)
+            self.param_strips.append(mine_s)
+            self.param_blocks.append(order)
             self.param_trees.append(split_tree(m, n, g["max_precond_dim"]) if kron else 0)
             r["leaf_end"] = len(leaves)
             r["tile_end"] = len(tiles)
@@ -193,6 +209,8 @@ class Plan:
         self.ttab = np.array(tiles, TILE_DT) if tiles else np.zeros(0, TILE_DT)
         self.pantab = np.array(panels, PANEL_DT) if panels else np.zeros(0, PANEL_DT)
         self.ctab = np.array(chunks, CHUNK_DT) if chunks else np.zeros(0, CHUNK_DT)
+        self.stab = np.array(strips, STRIP_DT) if strips else np.zeros(0, STRIP_DT)
+        self.n_strips = len(strips)
         self.kpad_max = kpad_max
         self.p_stride = kpad_max * kpad_max + 4
         self.n_leaves = len(leaves)
@@ -212,6 +230,8 @@ class Plan:
         self.t_tiles = self._dev(self.ttab) if len(self.ttab) else z(1)
         self.t_panels = self._dev(self.pantab) if len(self.pantab) else z(1)
         self.t_chunks = self._dev(self.ctab) if len(self.ctab) else z(1)
+        self.t_strips = self._dev(self.stab) if self.n_strips else z(1)
+        self.strip_part = z(self.n_strips * 4)
         self.step_host = torch.zeros(self.n_params * STEP_DT.itemsize, dtype=torch.uint8,
                                      pin_memory=torch.cuda.is_available())
         self.step_np = self.step_host.numpy().view(STEP_DT)
@@ -510,4 +530,5 @@ def PlanDev_from(plan):
     d.counters = ptr(plan.counters)
     d.diag_list, d.flat_list, d.p_list = ptr(plan.t_diag_list), ptr(plan.t_flat_list), ptr(plan.t_p_list)
     d.n_diag = plan.n_diag
+    d.strips, d.strip_part, d.n_strips = ptr(plan.t_strips), ptr(plan.strip_part), plan.n_strips
     return d

@@ -117,6 +117,46 @@ class LeafView:
             self._s(side, kk).copy_(S)
 
 
+class StripView:
+    """A width-1 block of the split (1 x b or a x 1): the reference's diagonal
+    sub-preconditioner (preconditioner.py:232-236), whose ``diag_ema`` is a
+    strided slice of the plan's diagonal arena."""
+
+    def __init__(self, plan, si, owner):
+        self.plan, self.si, self.owner = plan, si, owner
+        S = plan.stab[si]
+        self.count, self.stride = int(S["count"]), int(S["stride"])
+        self.begin = int(S["begin"])
+        self.pi = int(S["param"])
+        self.m, self.n = (1, self.count) if self.stride == 1 else (self.count, 1)
+        self.k_min = self.k_max = 1
+        self.use_kronecker = False
+        self.use_block_diagonal = False
+        self.use_int8_ema = plan.int8_ema
+
+    @property
+    def precond_step(self):
+        return self.owner.precond_step
+
+    @property
+    def k(self):
+        return 1
+
+    @property
+    def diag_ema(self):
+        o = int(self.plan.ptab[self.pi]["offset"]) + self.begin
+        return self.plan.diag_ema.as_strided((self.m, self.n),
+                                             (self.stride, 1) if self.stride != 1 else (self.count, 1),
+                                             o)
+
+    def state_dict(self):
+        return {"precond_step": self.precond_step, "k": 1, "use_kronecker": False,
+                "use_block_diagonal": False, "diag_ema": self.diag_ema.clone()}
+
+    def load_state_dict(self, st):
+        self.diag_ema.copy_(st["diag_ema"].reshape(self.m, self.n))
+
+
 class PrecondView:
     """``state["preconditioner"]`` of one parameter."""
 
@@ -133,27 +173,37 @@ class PrecondView:
             plan.ltab[leaves[0]]["a"] == self.m and plan.ltab[leaves[0]]["b"] == self.n
         self.use_block_diagonal = int(plan.ptab[pi]["mode"]) == 1 and not self.use_kronecker
         self._leaves = [LeafView(plan, li, self) for li in leaves]
-        self._blocks = self._leaves if self.use_block_diagonal else []
+        # every block of the split in order: Kronecker leaves and diagonal strips
+        self._views = [LeafView(plan, x, self) if kind == "L" else StripView(plan, x, self)
+                       for kind, x in plan.param_blocks[pi]]
+        self._blocks = self._views if self.use_block_diagonal else []
         # rank bounds of every node of the block tree (preconditioner.py:122-124)
         self._ktree = self._bounds_tree(self.m, self.n, group["max_precond_dim"],
-                                        group["k_min"], group["k_max"], iter(leaves)) \
-            if leaves else None
+                                        group["k_min"], group["k_max"],
+                                        iter(plan.param_blocks[pi])) if leaves else None
         self._k_mean = False     # an R5 assignment made every level a block mean
         self._k_plain = None     # R5-assigned k of a leaf-free (diagonal) parameter
 
     @staticmethod
-    def _bounds_tree(m, n, mpd, kmin, kmax, leaves):
+    def _bounds_tree(m, n, mpd, kmin, kmax, blocks):
+        """(k_min, k_max, child): child = a leaf index, None for a diagonal
+        strip (rank 1), or the list of sub-trees."""
         lo, hi = k_bounds(m, n, kmin, kmax)
+        if m <= 1 or n <= 1:
+            next(blocks)
+            return (1, 1, None)
         if max(m, n) <= mpd:
-            return (lo, hi, next(leaves))
+            return (lo, hi, next(blocks)[1])
         large, small = (m, n) if m >= n else (n, m)
         sizes = [mpd] * (large // mpd) + ([large % mpd] if large % mpd else [])
         kids = [PrecondView._bounds_tree(*((bs, small) if m >= n else (small, bs)), mpd, kmin,
-                                         kmax, leaves) for bs in sizes]
+                                         kmax, blocks) for bs in sizes]
         return (lo, hi, kids)
 
     def _walk_k(self, node, kvec):
         lo, hi, c = node
+        if c is None:
+            return 1
         if not isinstance(c, list):
             return int(kvec[c])
         sub = [self._walk_k(x, kvec) for x in c]
@@ -187,6 +237,8 @@ class PrecondView:
                 for x in c:
                     setk(x, k)
                 return
+            if c is None:
+                return
             if k < int(kvec[c]):
                 kvec[c] = k
                 changed = True
@@ -218,7 +270,7 @@ class PrecondView:
         return self.plan.state_view(self.plan.diag_ema, self.pi)
 
     def _tree_state(self, t, leaves):
-        if t == 1:
+        if t == 1 or t == 0:
             return next(leaves).state_dict()
         blocks = [self._tree_state(c, leaves) for c in t]
         k = blocks[0]["k"] if self.precond_step == 0 and not self._k_mean else \
@@ -227,7 +279,7 @@ class PrecondView:
                 "use_block_diagonal": True, "blocks": blocks}
 
     def _tree_load(self, t, st, leaves):
-        if t == 1:
+        if t == 1 or t == 0:
             next(leaves).load_state_dict(st)
             return
         for c, bs in zip(t, st["blocks"]):
@@ -237,13 +289,13 @@ class PrecondView:
         """Same schema as preconditioner.py:570-600, nested like the
         reference's ``_blocks`` hierarchy."""
         if self.use_block_diagonal or self.use_kronecker:
-            return self._tree_state(self.plan.param_trees[self.pi], iter(self._leaves))
+            return self._tree_state(self.plan.param_trees[self.pi], iter(self._views))
         return {"precond_step": self.precond_step, "k": 1, "use_kronecker": False,
                 "use_block_diagonal": False, "diag_ema": self.diag_ema.clone()}
 
     def load_state_dict(self, st):
         self.precond_step = int(st["precond_step"])
         if self.use_block_diagonal or self.use_kronecker:
-            self._tree_load(self.plan.param_trees[self.pi], st, iter(self._leaves))
+            self._tree_load(self.plan.param_trees[self.pi], st, iter(self._views))
         else:
             self.diag_ema.copy_(st["diag_ema"])

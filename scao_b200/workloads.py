@@ -91,11 +91,15 @@ def tiny(dtype="float32", max_precond_dim=4096, steps=40, grad_scale=1e-2,
     initialisation (the degenerate regime of the benchmark configs);
     ``grad_scale=1`` gives well-separated curvature spectra."""
     ps = _gpt_layers(1, 32, 128)
+    shapes = (extra or {}).get("_shapes")
+    if shapes:
+        ps = [ParamSpec(f"w{i}", tuple(s)) for i, s in enumerate(shapes)]
     kw = dict(lr=1e-3, betas=(0.9, 0.999), precond_freq=5, warmup_steps=8,
               blend_steps=10, min_precond_updates=1, k_min=4, k_max=8,
               use_int8_ema=int8, max_precond_dim=max_precond_dim, **_PARITY)
     kw.update(extra or {})
     scales = kw.pop("_grad_scales", None)
+    kw.pop("_shapes", None)
     return Workload(
         "tiny", ps, kw,
         grad_rank=4, grad_decay=0.7, param_dtype=dtype, steps=steps,

@@ -42,6 +42,8 @@ CASES = {
     "bf16_dyn": ("bfloat16", 48, 30, 1.0, True),
     "f32_r135": ("float32", 48, 30, 1.0, False),
     "bf16_gsnr": ("bfloat16", 4096, 30, 1.0, True),
+    "f32_strips": ("float32", 48, 30, 1.0, True),
+    "bf16_strips": ("bfloat16", 48, 30, 1.0, True),
 }
 
 # optimizer keyword overrides of a case: the gradient filter of
@@ -55,6 +57,11 @@ EXTRA = {
                      adaptive_rank=True, k_min=2, k_max=4,
                      _grad_scales=(1.0, 1.0, 0.05, 1.0, 1.0, 1.0)),
     "bf16_gsnr": dict(use_gsnr_clip=True, gsnr_threshold=0.3),
+    # width-1 remainder blocks of the split (diagonal sub-preconditioners,
+    # preconditioner.py:142-156, 232-236): a row strip, column strips, and
+    # both inside a nested split
+    "f32_strips": dict(_shapes=((49, 40), (40,), (40, 97), (97, 97))),
+    "bf16_strips": dict(_shapes=((49, 40), (40,), (40, 97), (97, 97)), sparsity=0.5),
 }
 
 
@@ -88,7 +95,12 @@ def run_case(scao_mod, name, dtype, mpd, steps, gs, int8):
         for key in ("exp_avg", "exp_avg_sq", "exp_avg_diff", "prev_grad"):
             out[f"{key}{i}"] = st[key].numpy()
         pc = st["preconditioner"]
-        leaves = [pc] if not pc.use_block_diagonal else list(pc._blocks)
+
+        def flat(node):
+            # every leaf of the (possibly nested) block tree, in order
+            return [x for b in node._blocks for x in flat(b)] if node.use_block_diagonal \
+                else [node]
+        leaves = flat(pc)
         for j, lf in enumerate(leaves):
             pre = f"leaf{i}_{j}_"
             out[pre + "precond_step"] = np.array(lf.precond_step)

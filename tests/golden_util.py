@@ -17,6 +17,8 @@ CASES = {
     "bf16_dyn": ("bfloat16", 48, 30, 1.0, True),
     "f32_r135": ("float32", 48, 30, 1.0, False),
     "bf16_gsnr": ("bfloat16", 4096, 30, 1.0, True),
+    "f32_strips": ("float32", 48, 30, 1.0, True),
+    "bf16_strips": ("bfloat16", 48, 30, 1.0, True),
 }
 
 # optimizer keyword overrides of a case: the gradient filter of
@@ -30,6 +32,11 @@ EXTRA = {
                      adaptive_rank=True, k_min=2, k_max=4,
                      _grad_scales=(1.0, 1.0, 0.05, 1.0, 1.0, 1.0)),
     "bf16_gsnr": dict(use_gsnr_clip=True, gsnr_threshold=0.3),
+    # width-1 remainder blocks of the split (diagonal sub-preconditioners,
+    # preconditioner.py:142-156, 232-236): a row strip, column strips, and
+    # both inside a nested split
+    "f32_strips": dict(_shapes=((49, 40), (40,), (40, 97), (97, 97))),
+    "bf16_strips": dict(_shapes=((49, 40), (40,), (40, 97), (97, 97)), sparsity=0.5),
 }
 
 

@@ -59,7 +59,7 @@ def test_struct_layouts_match_header(tmp_path):
     fields_filt = [f for f, _ in _lib.FilterDev._fields_]
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "scao_b200.h"',
              'int main(void) {']
-    for t in ("ScaoParam", "ScaoParamStep", "ScaoLeaf", "ScaoChunk", "ScaoFilterParam",
+    for t in ("ScaoParam", "ScaoParamStep", "ScaoLeaf", "ScaoChunk", "ScaoStrip", "ScaoFilterParam",
               "ScaoFilterDev", "ScaoPlanDev"):
         lines.append(f'printf("size {t} %zu\\n", sizeof({t}));')
     for f in fields_plan:
@@ -79,6 +79,7 @@ def test_struct_layouts_match_header(tmp_path):
     assert got[("size", "ScaoParamStep")] == _lib.STEP_DT.itemsize
     assert got[("size", "ScaoLeaf")] == _lib.LEAF_DT.itemsize
     assert got[("size", "ScaoChunk")] == _lib.CHUNK_DT.itemsize
+    assert got[("size", "ScaoStrip")] == _lib.STRIP_DT.itemsize
     assert got[("size", "ScaoFilterParam")] == _lib.FILTER_PARAM_DT.itemsize
     assert got[("size", "ScaoFilterDev")] == ctypes.sizeof(_lib.FilterDev)
     assert got[("size", "ScaoPlanDev")] == ctypes.sizeof(_lib.PlanDev)

@@ -164,7 +164,10 @@ def test_optimizer_matches_reference_run(name):
         assert rel_err(st["exp_avg_diff"].cpu().numpy(), G[f"exp_avg_diff{i}"]) < TOL, i
         pc = st["preconditioner"]
         sd = pc.state_dict()
-        leaves = sd["blocks"] if sd["use_block_diagonal"] else [sd]
+
+        def flat(d):
+            return [x for b in d["blocks"] for x in flat(b)] if d["use_block_diagonal"] else [d]
+        leaves = flat(sd)
         for j, lf in enumerate(leaves):
             pre = f"leaf{i}_{j}_"
             assert lf["k"] == int(G[pre + "k"])

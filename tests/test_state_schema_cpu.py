@@ -12,7 +12,9 @@ from scao_b200.preconditioner import PrecondView
 
 REF = "/root/reference"
 
-SHAPES = [((96, 128), 48), ((100, 30), 48), ((50, 7), 48), ((16,), 48), ((33, 200), 64)]
+SHAPES = [((96, 128), 48), ((100, 30), 48), ((50, 7), 48), ((16,), 48), ((33, 200), 64),
+          # width-1 remainders: diagonal sub-preconditioners inside the split
+          ((49, 40), 48), ((40, 97), 48), ((97, 97), 48)]
 
 
 def _ours(shape, mpd, int8):
@@ -51,3 +53,30 @@ def test_nested_schema_without_reference():
     assert all(b["use_block_diagonal"] and len(b["blocks"]) == 2 for b in d["blocks"])
     leaf = d["blocks"][0]["blocks"][0]
     assert leaf["use_kronecker"] and leaf["L_ema_q"].dtype == torch.int8
+
+
+@pytest.mark.parametrize("shape,mpd", [((49, 40), 48), ((40, 97), 48), ((97, 97), 48),
+                                       ((3, 2049), 1024)])
+def test_strips_and_leaves_tile_the_parameter(shape, mpd):
+    """Kronecker leaves and diagonal strips cover every element once; strip
+    diag_ema views address exactly their elements."""
+    import numpy as np
+    p = torch.zeros(shape)
+    g = dict(max_precond_dim=mpd, k_min=4, k_max=8, epsilon_sparse=0.05, rho=0.999)
+    plan = Plan([p], [g], torch.device("cpu"), True)
+    m, n = shape
+    cover = np.zeros(m * n, np.int32)
+    for L in plan.ltab:
+        r0, c0, a, b = (int(L[k]) for k in ("row0", "col0", "a", "b"))
+        for r in range(r0, r0 + a):
+            cover[r * n + c0: r * n + c0 + b] += 1
+    for S in plan.stab:
+        cover[int(S["begin"]) + np.arange(int(S["count"])) * int(S["stride"])] += 1
+    assert (cover == 1).all()
+    pv = PrecondView(plan, 0, g)
+    strips = [v for v in pv._views if not v.use_kronecker]
+    assert len(strips) == plan.n_strips > 0
+    for v in strips:
+        v.diag_ema.fill_(1.0)
+    assert int(plan.diag_ema.sum().item()) == sum(int(S["count"]) for S in plan.stab)
+    assert pv.k_host(plan.k.numpy()) >= 1
