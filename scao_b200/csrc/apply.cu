@@ -1694,6 +1694,7 @@ proj_tc_kernel(ScaoPlanDev P, int* err) {
     const ScaoParamStep& S = P.step[L.param];
     if (S.phase != 2) return;
     const ScaoParam& pr = P.params[L.param];
+    if (proj_fast(L, S, pr)) return;         // handled by proj_bf16_kernel / proj_tma_kernel
     const int dt = pr.dtype;
     const int Kp = (L.kpad + 15) & ~15;
     constexpr int KB = 64;
@@ -1723,7 +1724,6 @@ proj_tc_kernel(ScaoPlanDev P, int* err) {
     const int64_t base = (int64_t)(L.row0 + pn.row0) * L.ld + L.col0;
     const bool vec = ((L.ld & 7) == 0) && ((L.col0 & 7) == 0) && ((S.g_ptr & 15) == 0) &&
                      ((S.p_ptr & 15) == 0);
-    if (proj_fast(L, S, pr)) return;         // handled by proj_bf16_kernel
     float psq = 0.f;
     const int nkb = (L.b + KB - 1) / KB;
     bool ok = true;
@@ -1866,7 +1866,9 @@ extern "C" int scao_plan_step(const ScaoPlanDev* P, void* stream) {
         { ProfScope _ps(SLOT_PROJ, st);
           if (!P->tmaps_ok || P->proj_fallback)
               proj_bf16_kernel<<<P->n_panels, 128, proj_bf16_smem(P->kpad_max), st>>>(*P, P->err);
-          if (P->kron_dtypes & ~(1 << SCAO_BF16))
+          // fp32 / fp16 leaves, and bf16 leaves whose rows are not 16-byte
+          // aligned (both outside the TMA / cp.async paths)
+          if ((P->kron_dtypes & ~(1 << SCAO_BF16)) || !P->tmaps_ok || P->proj_fallback)
               proj_tc_kernel<<<P->n_panels, 128, proj_tc_smem(P->kpad_max), st>>>(*P, P->err); }
         SCAO_CHECK_LAUNCH();
     }
