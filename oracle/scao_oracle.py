@@ -478,8 +478,10 @@ class OracleSCAO:
 
     def __init__(self, params, dtype="float32", groups=None, lookahead_k=5,
                  lookahead_alpha=0.5, threads=1, **kw):
-        self.dtype = dtype
-        self.params = [round_to(np.array(p, dtype=F32), dtype) for p in params]
+        # one parameter dtype for all, or a list with one per parameter
+        self.dtypes = list(dtype) if isinstance(dtype, (list, tuple)) else [dtype] * len(params)
+        self.dtype = self.dtypes[0] if self.dtypes else dtype
+        self.params = [round_to(np.array(p, dtype=F32), d) for p, d in zip(params, self.dtypes)]
         d = dict(_DEFAULTS)
         self.sparsity = float(kw.pop("sparsity", 0.0))
         self.dynamic_sparsity = bool(kw.pop("dynamic_sparsity", False))
@@ -562,7 +564,8 @@ class OracleSCAO:
                 if i not in self.slow:
                     self.slow[i] = p.copy()
                 s = self.slow[i]
-                s = round_to(s + round_to(a * round_to(p - s, self.dtype), self.dtype), self.dtype)
+                dt = self.dtypes[i]
+                s = round_to(s + round_to(a * round_to(p - s, dt), dt), dt)
                 self.slow[i] = s
                 self.params[i] = s.copy()
 
@@ -580,7 +583,7 @@ class OracleSCAO:
                 self._step_param(i, group, grads[i])
 
     def _step_param(self, i, group, gr):
-        dt = self.dtype
+        dt = self.dtypes[i]
         lr = group["lr"]
         beta1, beta2 = group["betas"]
         beta3 = group["beta3"]
@@ -660,14 +663,13 @@ class OracleSCAO:
                 (np.sqrt(v / F32(bc2)) + F32(eps))
             if self.gsnr:                               # R4, optimizer.py:637-638
                 upd = gsnr_clip(upd, m, v, eps, self.gsnr_thr)
-            trust = self._lars(p, upd, lars, wd) if lars > 0 else 1.0
+            trust = self._lars(p, upd, lars, wd, dt) if lars > 0 else 1.0
             p = add_alpha(p, round_to(upd, dt), -(lr * trust), dt)
             st.update(m=m, v=v, d=d, prev=prev)
             self.params[i] = p
 
-    def _lars(self, p, upd, lars, wd):
+    def _lars(self, p, upd, lars, wd, dt):
         """optimizer.py:371-377 with parameter-dtype scalar roundings."""
-        dt = self.dtype
         pn = F32(round_to(np.array([norm_f32(p)], F32), dt)[0])
         un = norm_f32(upd)
         if pn == 0 or un == 0:

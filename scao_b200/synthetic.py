@@ -44,13 +44,17 @@ def _signfix_qr(a):
 
 def init_params(workload, seed=0, device="cpu"):
     """N(0, 0.02^2) parameter tensors for a workload, in its dtype."""
-    dt = torch_dtype(workload.param_dtype)
     out = []
     for i, spec in enumerate(workload.params):
         g = _gen(device, seed, 7, i)
         x = torch.randn(spec.shape, generator=g, device=device, dtype=torch.float64) * 0.02
-        out.append(x.to(dt))
+        out.append(x.to(param_dtype(workload, i)))
     return out
+
+
+def param_dtype(workload, i):
+    """torch dtype of parameter i (its own, else the workload's)."""
+    return torch_dtype(workload.params[i].dtype or workload.param_dtype)
 
 
 class LowRankGradients:
@@ -92,7 +96,7 @@ class LowRankGradients:
             if self.UV[i] is None:
                 x = torch.randn(spec.shape, generator=g, device=self.device,
                                 dtype=torch.float64) * self.noise
-                grads.append(x.to(self.dtype))
+                grads.append(x.to(param_dtype(self.w, i)))
                 continue
             U, V = self.UV[i]
             rr = U.shape[1]
@@ -101,7 +105,7 @@ class LowRankGradients:
                              dtype=torch.float64) * self.noise
             if self.w.grad_scales is not None:
                 x *= self.w.grad_scales[i]
-            grads.append(x.to(self.dtype))
+            grads.append(x.to(param_dtype(self.w, i)))
             m, n = spec.shape
             zu = torch.randn(U.shape, generator=g, device=self.device,
                              dtype=torch.float64) / m ** 0.5

@@ -20,6 +20,7 @@ class ParamSpec:
     name: str
     shape: tuple
     adam_only: bool = False
+    dtype: str = None        # overrides the workload's param_dtype
 
 
 @dataclass
@@ -94,12 +95,15 @@ def tiny(dtype="float32", max_precond_dim=4096, steps=40, grad_scale=1e-2,
     shapes = (extra or {}).get("_shapes")
     if shapes:
         ps = [ParamSpec(f"w{i}", tuple(s)) for i, s in enumerate(shapes)]
+    for s, d in zip(ps, (extra or {}).get("_dtypes") or ()):
+        s.dtype = d
     kw = dict(lr=1e-3, betas=(0.9, 0.999), precond_freq=5, warmup_steps=8,
               blend_steps=10, min_precond_updates=1, k_min=4, k_max=8,
               use_int8_ema=int8, max_precond_dim=max_precond_dim, **_PARITY)
     kw.update(extra or {})
     scales = kw.pop("_grad_scales", None)
     kw.pop("_shapes", None)
+    kw.pop("_dtypes", None)
     return Workload(
         "tiny", ps, kw,
         grad_rank=4, grad_decay=0.7, param_dtype=dtype, steps=steps,

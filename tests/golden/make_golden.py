@@ -44,6 +44,7 @@ CASES = {
     "bf16_gsnr": ("bfloat16", 4096, 30, 1.0, True),
     "f32_strips": ("float32", 48, 30, 1.0, True),
     "bf16_strips": ("bfloat16", 48, 30, 1.0, True),
+    "mixed": ("float32", 48, 30, 1.0, True),
 }
 
 # optimizer keyword overrides of a case: the gradient filter of
@@ -62,6 +63,9 @@ EXTRA = {
     # both inside a nested split
     "f32_strips": dict(_shapes=((49, 40), (40,), (40, 97), (97, 97))),
     "bf16_strips": dict(_shapes=((49, 40), (40,), (40, 97), (97, 97)), sparsity=0.5),
+    # one optimizer over parameters of different dtypes
+    "mixed": dict(_dtypes=("float32", "bfloat16", "float32", "float16", "float16",
+                           "bfloat16")),
 }
 
 

@@ -38,7 +38,8 @@ def run_oracle(name):
     w = workloads.tiny(dtype=dt, max_precond_dim=mpd, steps=steps,
                        grad_scale=gs, int8=i8, extra=EXTRA.get(name))
     p0 = [p.float().numpy() for p in synthetic.init_params(w)]
-    opt = O.OracleSCAO(p0, dtype=dt, **w.scao_kwargs)
+    dts = [str(synthetic.param_dtype(w, i)).replace("torch.", "") for i in range(len(p0))]
+    opt = O.OracleSCAO(p0, dtype=dts, **w.scao_kwargs)
     gen = synthetic.LowRankGradients(w)
     ks = []
     for _ in range(steps):
