@@ -1,0 +1,58 @@
+"""Host utilities exported for API compatibility (scao/utils.py:17-151),
+checked against the reference's own functions when its checkout is present
+and against their defining properties otherwise."""
+import os
+import sys
+
+import pytest
+import torch
+
+import scao_b200
+from scao_b200 import utils
+
+REF = "/root/reference"
+
+
+def _spd(m, seed):
+    g = torch.Generator().manual_seed(seed)
+    X = torch.randn(m, m, generator=g, dtype=torch.float64)
+    return (X @ X.T / m + 0.1 * torch.eye(m, dtype=torch.float64)).float()
+
+
+@pytest.mark.parametrize("m", [1, 5, 64])
+def test_neg_quarter_eigh_property(m):
+    A = _spd(m, m)
+    X = utils.matrix_power_neg_quarter(A).double()
+    # X^4 A = I
+    P = X @ X @ X @ X @ A.double()
+    assert torch.allclose(P, torch.eye(m, dtype=torch.float64), atol=1e-3)
+
+
+def test_low_rank_factors():
+    U = torch.eye(6, 3)
+    S = torch.tensor([16.0, 1.0, 0.0])
+    U2, s = utils.low_rank_matrix_power_neg_quarter(U, S)
+    assert U2 is U
+    assert torch.allclose(s, torch.tensor([0.5, 1.0, 1e-8 ** -0.25]))
+
+
+def test_exports():
+    for name in ("adaptive_rank", "matrix_power_neg_quarter", "newton_schulz_root_inv",
+                 "low_rank_matrix_power_neg_quarter"):
+        assert callable(getattr(scao_b200, name))
+
+
+@pytest.mark.skipif(not os.path.isdir(REF), reason="reference checkout not present")
+@pytest.mark.parametrize("ns", [False, True])
+@pytest.mark.parametrize("m", [4, 32])
+def test_neg_quarter_matches_reference(m, ns):
+    sys.path.insert(0, REF)
+    from scao import utils as ru
+    A = _spd(m, 100 + m)
+    ref = ru.matrix_power_neg_quarter(A, use_newton_schulz=ns)
+    got = utils.matrix_power_neg_quarter(A, use_newton_schulz=ns)
+    if ns:
+        # same iteration, same operation order: identical in float32
+        assert torch.equal(got, ref)
+    else:
+        assert torch.allclose(got, ref, rtol=1e-4, atol=1e-5)
