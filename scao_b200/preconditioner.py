@@ -157,6 +157,29 @@ class StripView:
         self.diag_ema.copy_(st["diag_ema"].reshape(self.m, self.n))
 
 
+class _BlockNode:
+    """An inner node of a nested block-diagonal split (a block whose own
+    larger dimension still exceeds max_precond_dim, preconditioner.py:163-194)."""
+
+    use_kronecker = False
+    use_block_diagonal = True
+
+    def __init__(self, owner, kids):
+        self.owner = owner
+        self._blocks = [_BlockNode(owner, x) if isinstance(x, list) else x for x in kids]
+
+    @property
+    def precond_step(self):
+        return self.owner.precond_step
+
+    @property
+    def k(self):
+        ks = [b.k for b in self._blocks]
+        if self.owner.precond_step == 0 and not self.owner._k_mean:
+            return ks[0]
+        return sum(ks) // max(len(ks), 1)
+
+
 class PrecondView:
     """``state["preconditioner"]`` of one parameter."""
 
@@ -176,13 +199,24 @@ class PrecondView:
         # every block of the split in order: Kronecker leaves and diagonal strips
         self._views = [LeafView(plan, x, self) if kind == "L" else StripView(plan, x, self)
                        for kind, x in plan.param_blocks[pi]]
-        self._blocks = self._views if self.use_block_diagonal else []
+        # the reference's ``_blocks`` hierarchy: children of the top split
+        # (leaf / strip views, or nodes of a nested split)
+        self._blocks = [_BlockNode(self, x) if isinstance(x, list) else x
+                        for x in self._nest(plan.param_trees[pi], iter(self._views))] \
+            if self.use_block_diagonal else []
         # rank bounds of every node of the block tree (preconditioner.py:122-124)
         self._ktree = self._bounds_tree(self.m, self.n, group["max_precond_dim"],
                                         group["k_min"], group["k_max"],
                                         iter(plan.param_blocks[pi])) if leaves else None
         self._k_mean = False     # an R5 assignment made every level a block mean
         self._k_plain = None     # R5-assigned k of a leaf-free (diagonal) parameter
+
+    @staticmethod
+    def _nest(t, views):
+        """Views of tree t: a leaf / strip view, or the list of its children."""
+        if t == 1 or t == 0:
+            return next(views)
+        return [PrecondView._nest(c, views) for c in t]
 
     @staticmethod
     def _bounds_tree(m, n, mpd, kmin, kmax, blocks):
