@@ -546,6 +546,22 @@ class SCAO(Optimizer):
         """Single-stream implementation: nothing is pending on a side stream."""
         return None
 
+    def sync_preconditioner(self, process_group=None) -> None:
+        """optimizer.py:686-710: broadcast the moments, step counters and
+        preconditioner state of rank 0 to every rank (after a checkpoint was
+        loaded on rank 0 only)."""
+        import warnings
+
+        import torch.distributed as dist
+        if not dist.is_available() or not dist.is_initialized():
+            warnings.warn("sync_preconditioner() called but distributed is not initialised.",
+                          RuntimeWarning, stacklevel=2)
+            return
+        if self._plan is None:
+            return
+        ps, _ = self._flat()
+        broadcast_plan_state(self._plan, [self.state[p] for p in ps], process_group)
+
     # ------------------------------------------------------------------
     # checkpoint (optimizer.py:732-776)
     # ------------------------------------------------------------------
@@ -623,3 +639,23 @@ class SCAO(Optimizer):
 
 def C_stream(stream):
     return stream.cuda_stream
+
+
+def broadcast_plan_state(plan, states, group=None):
+    """Rank 0's optimizer state onto every rank, in place: the moment arenas
+    (exp_avg, exp_avg_sq, exp_avg_diff -- prev_grad is not synchronised, as in
+    the reference), each parameter's ``step`` and ``precond_step``, and the
+    preconditioner arenas (factors and their absmax, eigenvectors and their
+    bf16 operand tiles, eigenvalues, ranks, diagonal EMA)
+    (optimizer.py:686-710, preconditioner.py:647-720)."""
+    import torch.distributed as dist
+    for t in (plan.exp_avg, plan.exp_avg_sq, plan.exp_avg_diff):
+        dist.broadcast(t, src=0, group=group)
+    counters = torch.tensor([[st.get("step", 0), st["preconditioner"].precond_step]
+                             for st in states], dtype=torch.int64, device=plan.device)
+    dist.broadcast(counters, src=0, group=group)
+    for st, (step, pstep) in zip(states, counters.tolist()):
+        st["step"] = int(step)
+        st["preconditioner"].precond_step = int(pstep)
+    for t in (plan.fac, plan.absmax, plan.u, plan.ev, plan.k, plan.diag_ema, plan.ua, plan.ut):
+        dist.broadcast(t, src=0, group=group)

@@ -2,6 +2,7 @@
 import os
 import socket
 
+import numpy as np
 import pytest
 import torch
 import torch.distributed as dist
@@ -108,3 +109,58 @@ def test_sharded_step_two_gloo_ranks():
     assert all(ok for _, ok, _ in res)
     owned = sorted(i for _, _, m in res for i in m)
     assert owned == list(range(len(workloads.tiny().params)))
+
+
+def _sync_worker(rank, world, port, q):
+    """Plans on the host (arenas only, no kernels): rank 0's state after
+    broadcast_plan_state on every rank."""
+    from scao_b200.optimizer import broadcast_plan_state
+    from scao_b200.plan import Plan
+    from scao_b200.preconditioner import PrecondView
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        g = dict(max_precond_dim=48, k_min=4, k_max=8, epsilon_sparse=0.05, rho=0.999)
+        params = [torch.zeros(49, 40), torch.zeros(40), torch.zeros(64, 48)]
+        plan = Plan(params, [g] * 3, torch.device("cpu"), True)
+        states = [{"step": 10 * (rank + 1) + i, "preconditioner": PrecondView(plan, i, g)}
+                  for i in range(3)]
+        for i, st in enumerate(states):
+            st["preconditioner"].precond_step = rank + i
+        gen = torch.Generator().manual_seed(rank)
+        arenas = ("exp_avg", "exp_avg_sq", "exp_avg_diff", "prev_grad", "fac", "absmax", "u",
+                  "ev", "k", "diag_ema", "ua", "ut")
+        for name in arenas:
+            t = getattr(plan, name)
+            t.copy_((torch.rand(t.shape, generator=gen) * 100).to(t.dtype))
+        # numpy copies travel through the queue by value
+        before = {n: getattr(plan, n).numpy().copy() for n in arenas}
+        broadcast_plan_state(plan, states)
+        got = {n: getattr(plan, n).numpy().copy() for n in arenas}
+        q.put((rank, [st["step"] for st in states],
+               [st["preconditioner"].precond_step for st in states], before, got))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sync_preconditioner_broadcasts_rank0_state():
+    """optimizer.py:686-710: moments, counters and preconditioner state from
+    rank 0; prev_grad stays per rank (the reference does not broadcast it)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_sync_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted((q.get(timeout=120) for _ in procs), key=lambda x: x[0])
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    (_, s0, p0, b0, g0), (_, s1, p1, b1, g1) = res
+    assert s0 == s1 == [10, 11, 12] and p0 == p1 == [0, 1, 2]
+    for name in g0:
+        eq = np.array_equal
+        if name == "prev_grad":
+            assert eq(g1[name], b1[name]) and not eq(g1[name], b0[name])
+        else:
+            assert eq(g1[name], b0[name]) and eq(g0[name], b0[name]), name
