@@ -56,3 +56,16 @@ def test_neg_quarter_matches_reference(m, ns):
         assert torch.equal(got, ref)
     else:
         assert torch.allclose(got, ref, rtol=1e-4, atol=1e-5)
+
+
+def test_seam_refuses_cpu():
+    """scao_b200.cuda has no CPU fallback (the reference's routes to PyTorch)."""
+    from scao_b200 import cuda as seam
+    z = torch.zeros(4, 4)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        seam.fused_kronecker_precond(torch.zeros(4, 2), torch.ones(2), torch.zeros(4, 2),
+                                     torch.ones(2), z)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        seam.low_rank_precond_mm(torch.zeros(4, 2), torch.ones(2), z)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        seam.int8_ema_update(torch.zeros(4, dtype=torch.int8), 1.0, torch.zeros(4), 0.9)
