@@ -52,6 +52,14 @@ class LeafView:
     def k(self):
         return int(self.plan.k[self.li].item())
 
+    def __getattr__(self, name):
+        # the reference's tensor attributes (U_l, S_l, L_ema_q, ...), as copies
+        if name in PrecondView._KRON_ATTRS:
+            st = self.state_dict()
+            if name in st:
+                return st[name]
+        raise AttributeError(name)
+
     def _fac(self, side):
         L = self.plan.ltab[self.li]
         n = self.m if side == 0 else self.n
@@ -210,6 +218,18 @@ class PrecondView:
                                         iter(plan.param_blocks[pi])) if leaves else None
         self._k_mean = False     # an R5 assignment made every level a block mean
         self._k_plain = None     # R5-assigned k of a leaf-free (diagonal) parameter
+
+    # the reference's tensor attributes of a single Kronecker block (copies)
+    _KRON_ATTRS = ("U_l", "S_l", "U_r", "S_r", "L_ema_q", "L_ema_scale", "R_ema_q",
+                   "R_ema_scale", "L_ema", "R_ema")
+
+    def __getattr__(self, name):
+        d = self.__dict__
+        if d.get("use_kronecker") and name in PrecondView._KRON_ATTRS:
+            st = d["_views"][0].state_dict()
+            if name in st:
+                return st[name]
+        raise AttributeError(name)
 
     @staticmethod
     def _nest(t, views):

@@ -57,15 +57,6 @@ class SparsePreconditioner(PrecondView):
         self._scratch = None
         self._keep = None
 
-    # -- the reference's attribute names for a single Kronecker block ----
-    def __getattr__(self, name):
-        d = self.__dict__
-        if d.get("use_kronecker") and name in ("U_l", "S_l", "U_r", "S_r", "L_ema_q",
-                                                "L_ema_scale", "R_ema_q", "R_ema_scale",
-                                                "L_ema", "R_ema"):
-            return d["_views"][0].state_dict()[name]
-        raise AttributeError(name)
-
     # ------------------------------------------------------------------
     def _cuda(self, t):
         if self.device.type != "cuda" or t.device != self.device:
