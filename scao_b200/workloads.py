@@ -34,6 +34,9 @@ class Workload:
     steps: int = 100
     grad_scale: float = 1e-2
     grad_scales: tuple = None     # optional per-parameter multipliers
+    # optional (param, modulus, remainder) triples: parameter `param` has no
+    # gradient at the steps t with t % modulus == remainder
+    grad_skip: tuple = None
     notes: str = ""
 
     @property
@@ -102,12 +105,18 @@ def tiny(dtype="float32", max_precond_dim=4096, steps=40, grad_scale=1e-2,
               use_int8_ema=int8, max_precond_dim=max_precond_dim, **_PARITY)
     kw.update(extra or {})
     scales = kw.pop("_grad_scales", None)
+    skip = kw.pop("_skip", None)
     kw.pop("_shapes", None)
     kw.pop("_dtypes", None)
     return Workload(
         "tiny", ps, kw,
         grad_rank=4, grad_decay=0.7, param_dtype=dtype, steps=steps,
-        grad_scale=grad_scale, grad_scales=scales)
+        grad_scale=grad_scale, grad_scales=scales, grad_skip=skip)
+
+
+def has_grad(workload, i, t):
+    """False when parameter i gets no gradient at step t (``grad_skip``)."""
+    return not any(i == p and t % mod == rem for p, mod, rem in (workload.grad_skip or ()))
 
 
 def c1() -> Workload:

@@ -45,6 +45,7 @@ CASES = {
     "f32_strips": ("float32", 48, 30, 1.0, True),
     "bf16_strips": ("bfloat16", 48, 30, 1.0, True),
     "mixed": ("float32", 48, 30, 1.0, True),
+    "bf16_skip": ("bfloat16", 48, 30, 1.0, True),
 }
 
 # optimizer keyword overrides of a case: the gradient filter of
@@ -66,6 +67,9 @@ EXTRA = {
     # one optimizer over parameters of different dtypes
     "mixed": dict(_dtypes=("float32", "bfloat16", "float32", "float16", "float16",
                            "bfloat16")),
+    # parameters without a gradient at some steps (skipped by the step,
+    # still moved by lookahead, left out of the global-norm average)
+    "bf16_skip": dict(_skip=((2, 3, 1), (0, 4, 2), (5, 7, 3))),
 }
 
 
@@ -87,8 +91,8 @@ def run_case(scao_mod, name, dtype, mpd, steps, gs, int8):
     for t in range(steps):
         grads = gen.next()
         digests.append(grad_digest(grads))
-        for p, g in zip(params, grads):
-            p.grad = g.clone()
+        for i, (p, g) in enumerate(zip(params, grads)):
+            p.grad = g.clone() if workloads.has_grad(w, i, t) else None
         opt.step()
         ks.append([opt.state[p]["preconditioner"].k for p in params])
     out = {"steps": np.array(steps), "digests": np.array(digests),

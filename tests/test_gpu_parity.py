@@ -139,9 +139,9 @@ def run_gpu(name, steps=None):
     opt = SCAO(params, **w.scao_kwargs)
     gen = synthetic.LowRankGradients(w)
     ks = []
-    for _ in range(steps):
-        for p, g in zip(params, gen.next()):
-            p.grad = g.to(DEV)
+    for t in range(steps):
+        for i, (p, g) in enumerate(zip(params, gen.next())):
+            p.grad = g.to(DEV) if workloads.has_grad(w, i, t) else None
         opt.step()
         ks.append([opt.state[p]["preconditioner"].k for p in params])
     torch.cuda.synchronize()

@@ -42,8 +42,9 @@ def run_oracle(name):
     opt = O.OracleSCAO(p0, dtype=dts, **w.scao_kwargs)
     gen = synthetic.LowRankGradients(w)
     ks = []
-    for _ in range(steps):
-        opt.step([g.float().numpy() for g in gen.next()])
+    for t in range(steps):
+        opt.step([g.float().numpy() if workloads.has_grad(w, i, t) else None
+                  for i, g in enumerate(gen.next())])
         ks.append([opt.state[i]["precond"].k for i in range(len(p0))])
     return p0, opt, np.array(ks)
 
