@@ -8,8 +8,6 @@ one kernel launch per phase covers every parameter.
 """
 from __future__ import annotations
 
-import ctypes as C
-
 import numpy as np
 import torch
 

@@ -12,7 +12,7 @@ express "Adam-only", so the unchanged API is used.
 """
 from __future__ import annotations
 
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 
 
 @dataclass

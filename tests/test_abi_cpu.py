@@ -50,7 +50,6 @@ def test_struct_layouts_match_header(tmp_path):
     with the ctypes / numpy mirrors."""
     import shutil
     import subprocess
-    import numpy as np
     cc = shutil.which("gcc") or shutil.which("cc")
     if cc is None:
         import pytest

@@ -8,7 +8,6 @@ parameters.  The cp.async kernel itself is pinned to the reference through
 the golden runs."""
 import os
 
-import numpy as np
 import pytest
 import torch
 

@@ -4,13 +4,12 @@ Bars (from the north star): int8 quantisation bit-exact on identical fp32
 inputs; ranks equal; eigen-subspaces within 1e-3 rad principal angle;
 parameter updates and moments within relative L2 1e-3.
 """
-import ctypes
 
 import numpy as np
 import pytest
 import torch
 
-from golden_util import CASES, EXTRA, load, principal_angle, rel_err, subspace_angle
+from golden_util import CASES, EXTRA, load, rel_err, subspace_angle
 from oracle import scao_oracle as O
 from scao_b200 import SCAO, _lib, synthetic, workloads
 

@@ -3,7 +3,7 @@ package itself (tests/golden/make_golden.py).  CPU only."""
 import numpy as np
 import pytest
 
-from golden_util import CASES, EXTRA, load, principal_angle, rel_err, subspace_angle
+from golden_util import CASES, EXTRA, load, principal_angle, rel_err
 from oracle import scao_oracle as O
 from scao_b200 import synthetic, workloads
 

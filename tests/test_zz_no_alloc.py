@@ -8,7 +8,6 @@ bit (the int8 requant is exact), on consecutive calls that reuse the array.
 This file is collected last so a stop-at-first-failure run has already run
 everything else.
 """
-import numpy as np
 import pytest
 import torch
 
