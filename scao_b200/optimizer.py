@@ -514,16 +514,11 @@ class SCAO(Optimizer):
         return float(self._plan.global_norm_ema.item())
 
     def collect_metrics(self) -> dict:
-        step = max((s.get("step", 0) for s in self.state.values()), default=0)
-        ranks = self.current_ranks()
-        m = {"step": step}
-        if ranks:
-            ks = list(ranks.values())
-            m["scao/rank_mean"] = sum(ks) / len(ks)
-            m["scao/rank_min"] = min(ks)
-            m["scao/rank_max"] = max(ks)
-            m["scao/layers"] = len(ks)
-        m["scao/precond_freq"] = self.param_groups[0].get("precond_freq", -1)
+        """The callback metrics of optimizer.py:492-499: scao.logging's
+        collect_metrics plus the noise level, the global grad-norm EMA and the
+        warmup flag."""
+        from .logging import collect_metrics
+        m = collect_metrics(self)
         m["noise_std"] = self._noise_std
         m["global_norm_ema"] = self._global_norm_ema
         m["warmup_active"] = self._in_warmup_global
