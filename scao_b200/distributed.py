@@ -12,7 +12,11 @@ curvature factors and its eigenfactors -- is owned by exactly one rank:
 
 Because the step is independent per parameter (the LARS trust ratio and the
 curvature clip are per-parameter reductions), the result is identical to the
-single-GPU step on the averaged gradient.  ``sync_preconditioners`` and
+single-GPU step on the averaged gradient.  One exception: the global
+grad-norm EMA (optimizer.py:439-446) is kept by each rank's optimizer over the
+parameters that rank owns; it only steers the optional R1 adaptive warmup, R2
+dynamic sparsity and R5 adaptive rank, which therefore see a per-rank average
+under this wrapper.  ``sync_preconditioners`` and
 ``wrap_scao_for_fsdp`` keep the reference's API for replicated optimizers.
 """
 from __future__ import annotations
