@@ -205,7 +205,7 @@ def main():
                     help="N>1: SMs the persistent kernels leave to the collectives")
     ap.add_argument("--workload", default="llama-1b", choices=["llama-1b", "gpt2m-train"],
                     help="gpt2m-train: the GPT-2-medium data-parallel training step "
-                         "(BASELINE config 2) instead of the headline optimizer step")
+                         "(benchmark configuration C3) instead of the headline optimizer step")
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3)
     if a.workload == "gpt2m-train":

@@ -1,5 +1,5 @@
 """GPT-2-shaped language model and one data-parallel training step with the
-SCAO optimizer -- the caller of the optimizer step in BASELINE config 3
+SCAO optimizer -- the caller of the optimizer step in benchmark configuration C3
 (GPT-2-medium: 24 layers, d = 1024, 16 heads, d_ff = 4096, vocab 50257,
 8 x 1024 tokens, bf16 autocast, fp32 optimizer state).
 

@@ -2,7 +2,7 @@
 
 Each workload is a list of parameter shapes in torch layout (out x in) plus the
 SCAO keyword arguments it is run with.  Shapes follow the benchmark
-configurations of the reference (BASELINE configs C1..C5); the seeded gradient
+configurations C1..C5 of the reference's published numbers; the seeded gradient
 generator for them lives in ``scao_b200.synthetic``.
 
 An entry ``adam_only=True`` marks a parameter that sits in a param group whose
@@ -120,7 +120,7 @@ def has_grad(workload, i, t):
 
 
 def c1() -> Workload:
-    """4-layer d=256 GPT, CPU-runnable, 100 steps."""
+    """Configuration C1: 4-layer d=256 GPT, CPU-runnable, 100 steps."""
     ps = _gpt_layers(4, 256, 1024)
     return Workload(
         "c1-gpt-4L-d256", ps,
@@ -131,7 +131,7 @@ def c1() -> Workload:
 
 
 def c2() -> Workload:
-    """GPT-2-small shapes, embedding Adam-only."""
+    """Configuration C2: GPT-2-small shapes, embedding Adam-only."""
     ps = [ParamSpec("wte", (50257, 768), adam_only=True)] + _gpt_layers(12, 768, 3072)
     return Workload(
         "c2-gpt2-small", ps,
@@ -142,7 +142,7 @@ def c2() -> Workload:
 
 
 def c4(n_layers: int = 16) -> Workload:
-    """Llama-1B shapes, bf16 params, fp32 state."""
+    """Configuration C4: Llama-1B shapes, bf16 params, fp32 state."""
     ps = [ParamSpec("embed", (32000, 2048), adam_only=True)]
     ps += _llama_layers(n_layers, 2048, 32, 8, 64, 8192)
     ps += [ParamSpec("final_norm", (2048,))]
@@ -155,7 +155,7 @@ def c4(n_layers: int = 16) -> Workload:
 
 
 def c5(n_layers: int = 36) -> Workload:
-    """Qwen2.5-3B shapes, bf16 params."""
+    """Configuration C5: Qwen2.5-3B shapes, bf16 params."""
     ps = [ParamSpec("embed", (151936, 2048), adam_only=True)]
     ps += _llama_layers(n_layers, 2048, 16, 2, 128, 11008)
     ps += [ParamSpec("final_norm", (2048,))]

@@ -1,4 +1,4 @@
-"""BASELINE config 0 at full size (4-layer d=256 GPT set, int8 EMA, 100 steps):
+"""Benchmark configuration C1 at full size (4-layer d=256 GPT set, int8 EMA, 100 steps):
 the CUDA optimizer against the oracle on the same seeded gradients -- ranks
 equal at every step, parameter updates and moments within 1e-3 relative L2."""
 import numpy as np
