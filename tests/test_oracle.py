@@ -1,5 +1,7 @@
 """Pin the numpy oracle against golden vectors produced by the reference
 package itself (tests/golden/make_golden.py).  CPU only."""
+import os
+
 import numpy as np
 import pytest
 
@@ -115,3 +117,35 @@ def test_quantile_matches_torch():
         ref = np.float32(torch.quantile(torch.from_numpy(x), q).item())
         assert O.quantile_f32(x, q) == ref, (t, n, q)
     assert np.isnan(O.quantile_f32(np.array([1, np.nan, 2], np.float32), 0.5))
+
+
+@pytest.mark.skipif(not os.path.isdir("/root/reference"), reason="reference checkout not present")
+def test_oracle_matches_reference_at_config_c1():
+    """Benchmark configuration C1 at full size (4-layer d=256 GPT set, int8 EMA,
+    100 steps): the reference package itself against the oracle on the same
+    seeded gradients -- ranks equal at every step, parameter updates and
+    moments far inside the 1e-3 parity bar.  The GPU tests compare the CUDA
+    path with the oracle on this same run."""
+    import sys
+    import torch
+    sys.path.insert(0, "/root/reference")
+    import scao
+    w = workloads.c1()
+    p0 = synthetic.init_params(w)
+    params = [torch.nn.Parameter(p.clone()) for p in p0]
+    ref = scao.SCAO(params, **w.scao_kwargs)
+    orc = O.OracleSCAO([p.float().numpy() for p in p0], dtype="float32", **w.scao_kwargs)
+    gen = synthetic.LowRankGradients(w)
+    for _ in range(w.steps):
+        gs = gen.next()
+        for p, g in zip(params, gs):
+            p.grad = g.clone()
+        ref.step()
+        orc.step([g.float().numpy() for g in gs])
+        assert [ref.state[p]["preconditioner"].k for p in params] == \
+            [orc.state[i]["precond"].k for i in range(len(params))]
+    for i, p in enumerate(params):
+        a0 = p0[i].float().numpy()
+        assert rel_err(orc.params[i] - a0, p.detach().numpy() - a0) < 1e-6, i
+        assert rel_err(orc.state[i]["m"], ref.state[p]["exp_avg"].numpy()) < 1e-6, i
+        assert rel_err(orc.state[i]["v"], ref.state[p]["exp_avg_sq"].numpy()) < 1e-6, i
