@@ -120,7 +120,8 @@ def test_quantile_matches_torch():
 
 
 @pytest.mark.skipif(not os.path.isdir("/root/reference"), reason="reference checkout not present")
-def test_oracle_matches_reference_at_config_c1():
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
+def test_oracle_matches_reference_at_config_c1(dtype):
     """Benchmark configuration C1 at full size (4-layer d=256 GPT set, int8 EMA,
     100 steps): the reference package itself against the oracle on the same
     seeded gradients -- ranks equal at every step, parameter updates and
@@ -131,10 +132,11 @@ def test_oracle_matches_reference_at_config_c1():
     sys.path.insert(0, "/root/reference")
     import scao
     w = workloads.c1()
+    w.param_dtype = dtype
     p0 = synthetic.init_params(w)
     params = [torch.nn.Parameter(p.clone()) for p in p0]
     ref = scao.SCAO(params, **w.scao_kwargs)
-    orc = O.OracleSCAO([p.float().numpy() for p in p0], dtype="float32", **w.scao_kwargs)
+    orc = O.OracleSCAO([p.float().numpy() for p in p0], dtype=dtype, **w.scao_kwargs)
     gen = synthetic.LowRankGradients(w)
     for _ in range(w.steps):
         gs = gen.next()
@@ -144,8 +146,11 @@ def test_oracle_matches_reference_at_config_c1():
         orc.step([g.float().numpy() for g in gs])
         assert [ref.state[p]["preconditioner"].k for p in params] == \
             [orc.state[i]["precond"].k for i in range(len(params))]
+    # bf16: the parameters come out bit-identical; the fp32 moments carry the
+    # float32 summation-order differences of the preconditioner GEMMs
+    mtol = 1e-6 if dtype == "float32" else 1e-3
     for i, p in enumerate(params):
         a0 = p0[i].float().numpy()
-        assert rel_err(orc.params[i] - a0, p.detach().numpy() - a0) < 1e-6, i
-        assert rel_err(orc.state[i]["m"], ref.state[p]["exp_avg"].numpy()) < 1e-6, i
-        assert rel_err(orc.state[i]["v"], ref.state[p]["exp_avg_sq"].numpy()) < 1e-6, i
+        assert rel_err(orc.params[i] - a0, p.detach().float().numpy() - a0) < 1e-6, i
+        assert rel_err(orc.state[i]["m"], ref.state[p]["exp_avg"].numpy()) < mtol, i
+        assert rel_err(orc.state[i]["v"], ref.state[p]["exp_avg_sq"].numpy()) < mtol, i
