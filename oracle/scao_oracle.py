@@ -68,6 +68,12 @@ def add_alpha(p, x, alpha, dtype):
     return round_to(fma(a, x, p), dtype)
 
 
+def norm_dt(x, dtype):
+    """float(t.norm()) of a tensor of that dtype: torch accumulates in float32
+    and returns the norm in the tensor's own dtype (rounded for bf16 / fp16)."""
+    return float(round_to(np.array([norm_f32(x)], F32), dtype)[0])
+
+
 def norm_f32(x):
     """Frobenius norm with float32 output (torch ``Tensor.norm``)."""
     x = np.asarray(x, dtype=F32)
@@ -387,9 +393,9 @@ class OracleSparseFilter:
     def set_global_norm_ref(self, g):
         self.global_ref = max(g, 1e-8)
 
-    def __call__(self, grad):
+    def __call__(self, grad, dtype="float32"):
         if self.dynamic:
-            layer = float(norm_f32(grad))
+            layer = norm_dt(grad, dtype)
             self.norm_ema = self.norm_coeff * self.norm_ema + (1.0 - self.norm_coeff) * layer
             ratio = self.norm_ema / self.global_ref
             margin = 0.2 * (1.0 - min(ratio, 2.0) / 2.0)
@@ -540,7 +546,7 @@ class OracleSCAO:
     def step(self, grads):
         """optimizer.py:452-503."""
         self.global_step += 1
-        norms = [float(norm_f32(g)) for g in grads if g is not None]
+        norms = [norm_dt(g, self.dtypes[i]) for i, g in enumerate(grads) if g is not None]
         avg = 0.0
         if norms:
             avg = sum(norms) / len(norms)
@@ -598,11 +604,11 @@ class OracleSCAO:
             step = st["step"]
             raw = np.asarray(gr, dtype=F32)       # p.grad (param dtype values)
             grad = raw
-            grad_norm = float(norm_f32(raw))     # optimizer.py:532
+            grad_norm = norm_dt(raw, dt)         # optimizer.py:532
             if self.sparsity > 0.0:              # optimizer.py:536-542
                 if i not in self.filters:
                     self.filters[i] = OracleSparseFilter(self.sparsity, self.dynamic_sparsity)
-                grad = self.filters[i](grad)
+                grad = self.filters[i](grad, dt)
             p = self.params[i]
             if wd != 0.0:
                 p = round_to(p * F32(1.0 - lr * wd), dt)

@@ -518,7 +518,9 @@ __global__ void global_norm_kernel(ScaoPlanDev P) {
         const int m = min(1024, P.n_params - p0);
         for (int i = threadIdx.x; i < m; i += blockDim.x) {
             live[i] = P.step[p0 + i].phase != 0;
-            nrm[i] = sqrtf(P.param_scalars[(p0 + i) * 8 + PS_GNORM2]);
+            // per-parameter norm in the gradient's dtype, as float(p.grad.norm())
+            nrm[i] = round_dt(sqrtf(P.param_scalars[(p0 + i) * 8 + PS_GNORM2]),
+                              P.params[p0 + i].dtype);
         }
         __syncthreads();
         if (threadIdx.x == 0)
@@ -2006,7 +2008,8 @@ grad_norm_param_kernel(ScaoPlanDev P, float* out) {
     float s = 0.f;
     for (int c = pr.chunk_begin + threadIdx.x; c < pr.chunk_end; c += NT) s += P.chunk_part[c * 4 + 3];
     s = block_sum(s, red);
-    if (threadIdx.x == 0) out[pi] = sqrtf(s);
+    // float(p.grad.norm()): float32 accumulation, result in the gradient's dtype
+    if (threadIdx.x == 0) out[pi] = round_dt(sqrtf(s), pr.dtype);
 }
 
 }  // namespace

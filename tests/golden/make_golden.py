@@ -48,6 +48,12 @@ CASES = {
     "bf16_skip": ("bfloat16", 48, 30, 1.0, True),
 }
 
+# golden runs the oracle is pinned against whose GPU parity run is still to be
+# recorded (same fields as CASES)
+ORACLE_ONLY = {
+    "bf16_r1235": ("bfloat16", 48, 30, 1.0, True),
+}
+
 # optimizer keyword overrides of a case: the gradient filter of
 # optimizer.py:40-97 (static and R2-dynamic), R1 adaptive warmup, R3 lazy
 # curvature trigger, R5 adaptive rank, R4 gSNR clip
@@ -70,6 +76,12 @@ EXTRA = {
     # parameters without a gradient at some steps (skipped by the step,
     # still moved by lookahead, left out of the global-norm average)
     "bf16_skip": dict(_skip=((2, 3, 1), (0, 4, 2), (5, 7, 3))),
+    # bf16 with R1 + R2 + R3 + R5: per-parameter norms are rounded to bf16
+    # (float(p.grad.norm()) of a bf16 gradient) before the host policies see them
+    "bf16_r1235": dict(adaptive_warmup=True, warmup_patience=2, warmup_stability_threshold=0.5,
+                       lazy_precond=True, lazy_delta_threshold=0.02, lazy_max_skip=4,
+                       adaptive_rank=True, k_min=2, k_max=4, sparsity=0.6,
+                       dynamic_sparsity=True, _grad_scales=(1.0, 1.0, 0.05, 1.0, 1.0, 1.0)),
 }
 
 
@@ -186,7 +198,7 @@ def main():
     if not a.only:
         quant_cases(utils)
         rank_cases(utils)
-    for name, args in CASES.items():
+    for name, args in {**CASES, **ORACLE_ONLY}.items():
         if not a.only or name in a.only:
             run_case(scao, name, *args)
 

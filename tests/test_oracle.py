@@ -5,7 +5,7 @@ import os
 import numpy as np
 import pytest
 
-from golden_util import CASES, EXTRA, load, principal_angle, rel_err
+from golden_util import CASES, EXTRA, ORACLE_ONLY, load, principal_angle, rel_err
 from oracle import scao_oracle as O
 from scao_b200 import synthetic, workloads
 
@@ -36,7 +36,7 @@ def test_bf16_rounding_matches_torch():
 
 
 def run_oracle(name):
-    dt, mpd, steps, gs, i8 = CASES[name]
+    dt, mpd, steps, gs, i8 = {**CASES, **ORACLE_ONLY}[name]
     w = workloads.tiny(dtype=dt, max_precond_dim=mpd, steps=steps,
                        grad_scale=gs, int8=i8, extra=EXTRA.get(name))
     p0 = [p.float().numpy() for p in synthetic.init_params(w)]
@@ -51,7 +51,7 @@ def run_oracle(name):
     return p0, opt, np.array(ks)
 
 
-@pytest.mark.parametrize("name", list(CASES))
+@pytest.mark.parametrize("name", list(CASES) + list(ORACLE_ONLY))
 def test_oracle_matches_reference_run(name):
     G = load("run_" + name)
     p0, opt, ks = run_oracle(name)
