@@ -393,9 +393,9 @@ class OracleSparseFilter:
     def set_global_norm_ref(self, g):
         self.global_ref = max(g, 1e-8)
 
-    def __call__(self, grad, dtype="float32"):
+    def __call__(self, grad):
         if self.dynamic:
-            layer = norm_dt(grad, dtype)
+            layer = float(norm_f32(grad))        # grad = p.grad.float() (optimizer.py:531)
             self.norm_ema = self.norm_coeff * self.norm_ema + (1.0 - self.norm_coeff) * layer
             ratio = self.norm_ema / self.global_ref
             margin = 0.2 * (1.0 - min(ratio, 2.0) / 2.0)
@@ -546,6 +546,7 @@ class OracleSCAO:
     def step(self, grads):
         """optimizer.py:452-503."""
         self.global_step += 1
+        # optimizer.py:439-446: p.grad.norm() in the gradient's own dtype
         norms = [norm_dt(g, self.dtypes[i]) for i, g in enumerate(grads) if g is not None]
         avg = 0.0
         if norms:
@@ -604,11 +605,11 @@ class OracleSCAO:
             step = st["step"]
             raw = np.asarray(gr, dtype=F32)       # p.grad (param dtype values)
             grad = raw
-            grad_norm = norm_dt(raw, dt)         # optimizer.py:532
+            grad_norm = float(norm_f32(raw))     # of p.grad.float(), optimizer.py:531-532
             if self.sparsity > 0.0:              # optimizer.py:536-542
                 if i not in self.filters:
                     self.filters[i] = OracleSparseFilter(self.sparsity, self.dynamic_sparsity)
-                grad = self.filters[i](grad, dt)
+                grad = self.filters[i](grad)
             p = self.params[i]
             if wd != 0.0:
                 p = round_to(p * F32(1.0 - lr * wd), dt)

@@ -2008,8 +2008,9 @@ grad_norm_param_kernel(ScaoPlanDev P, float* out) {
     float s = 0.f;
     for (int c = pr.chunk_begin + threadIdx.x; c < pr.chunk_end; c += NT) s += P.chunk_part[c * 4 + 3];
     s = block_sum(s, red);
-    // float(p.grad.norm()): float32 accumulation, result in the gradient's dtype
-    if (threadIdx.x == 0) out[pi] = round_dt(sqrtf(s), pr.dtype);
+    // float32 norm (of p.grad.float(), optimizer.py:531-532); the host rounds
+    // it to the gradient's dtype where the reference does (the average, :440)
+    if (threadIdx.x == 0) out[pi] = sqrtf(s);
 }
 
 }  // namespace

@@ -124,7 +124,7 @@ filt_global_kernel(ScaoPlanDev P) {
         const int m = min(1024, P.n_params - p0);
         for (int i = threadIdx.x; i < m; i += blockDim.x) {
             live[i] = P.step[p0 + i].phase != 0;
-            // float(p.grad.norm()): rounded to the gradient's dtype
+            // float(p.grad.norm()) of optimizer.py:440: in the gradient's dtype
             nrm[i] = round_dt(sqrtf(P.filt.fp[p0 + i].gsq), P.params[p0 + i].dtype);
         }
         __syncthreads();
@@ -149,7 +149,7 @@ filt_global_kernel(ScaoPlanDev P) {
         double q = FD.base;
         if (FD.mode == 2) {
             if (!F->first) F->global_ref = fmax(gema, 1e-8);
-            const double layer = (double)round_dt(sqrtf(F->gsq), P.params[pi].dtype);
+            const double layer = (double)sqrtf(F->gsq);   // of p.grad.float() (:531)
             F->norm_ema = __dadd_rn(__dmul_rn(FD.norm_coeff, F->norm_ema),
                                     __dmul_rn(1.0 - FD.norm_coeff, layer));
             const double ratio = F->norm_ema / F->global_ref;

@@ -290,7 +290,10 @@ class SCAO(Optimizer):
         norms = kvec = None
         if self._host_norms:
             norms, kvec = self._grad_norms_and_ranks(plan)
-            live = [float(norms[i]) for i in range(len(ps)) if grads[i] is not None]
+            # the average takes p.grad.norm() in the gradient's dtype
+            # (optimizer.py:440); R3 / R5 use the float32 norm (:531-532)
+            avg_norms = _in_param_dtypes(norms, ps)
+            live = [float(avg_norms[i]) for i in range(len(ps)) if grads[i] is not None]
             avg = sum(live) / len(live) if live else 0.0
             if live:
                 self._gema = 0.95 * self._gema + 0.05 * avg           # optimizer.py:445
@@ -630,6 +633,15 @@ class SCAO(Optimizer):
             ws._stable_count = int(runtime.get("warmup_stable_count", ws._stable_count))
             ws._early_exit_step = runtime.get("warmup_early_exit_step", ws._early_exit_step)
         self._lookahead_init = False
+
+
+def _in_param_dtypes(norms, params):
+    """float32 values rounded (RNE) to each parameter's dtype."""
+    out = np.asarray(norms, np.float32).copy()
+    for dt in {p.dtype for p in params} - {torch.float32}:
+        idx = [i for i, p in enumerate(params) if p.dtype == dt]
+        out[idx] = torch.from_numpy(out[idx]).to(dt).float().numpy()
+    return out
 
 
 def C_stream(stream):
