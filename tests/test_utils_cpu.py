@@ -69,3 +69,19 @@ def test_seam_refuses_cpu():
         seam.low_rank_precond_mm(torch.zeros(4, 2), torch.ones(2), z)
     with pytest.raises(RuntimeError, match="CUDA"):
         seam.int8_ema_update(torch.zeros(4, dtype=torch.int8), 1.0, torch.zeros(4), 0.9)
+
+
+def test_average_norms_in_param_dtype():
+    """The global grad-norm average takes p.grad.norm() in the gradient's dtype
+    (optimizer.py:440): float32 norms rounded like torch's own casts."""
+    import numpy as np
+    from scao_b200.optimizer import _in_param_dtypes
+    ps = [torch.zeros(1, dtype=d) for d in (torch.bfloat16, torch.float32, torch.float16)]
+    x = np.array([32.2302131652832, 1.2345678, 1.2345678], np.float32)
+    got = _in_param_dtypes(x, ps)
+    g = torch.randn(1000, generator=torch.Generator().manual_seed(0))
+    assert got[0] == float(torch.tensor(x[0]).bfloat16()) == 32.25
+    assert got[1] == x[1] and got[2] == float(np.float16(x[2]))
+    # what the reference's float(p.grad.norm()) returns for a bf16 gradient
+    assert float(g.bfloat16().norm()) == float(_in_param_dtypes(
+        np.array([g.bfloat16().float().norm().item()], np.float32), ps[:1])[0])
