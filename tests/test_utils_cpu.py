@@ -85,3 +85,37 @@ def test_average_norms_in_param_dtype():
     # what the reference's float(p.grad.norm()) returns for a bf16 gradient
     assert float(g.bfloat16().norm()) == float(_in_param_dtypes(
         np.array([g.bfloat16().float().norm().item()], np.float32), ps[:1])[0])
+
+
+@pytest.mark.skipif(not os.path.isdir(REF), reason="reference checkout not present")
+def test_host_policies_match_reference_classes():
+    """R1 warmup scheduler and R3 lazy trigger (optimizer.py:104-214): the
+    host classes against the reference's own on random norm sequences
+    (drifting, flat, jumping), decision for decision."""
+    import numpy as np
+    sys.path.insert(0, REF)
+    from scao import optimizer as ro
+    from scao_b200 import optimizer as so
+    rng = np.random.default_rng(7)
+    for trial in range(40):
+        kind = trial % 4
+        n = 200
+        if kind == 0:
+            x = np.abs(1 + 0.01 * np.cumsum(rng.standard_normal(n)))
+        elif kind == 1:
+            x = np.full(n, 0.5) + 1e-4 * rng.standard_normal(n)
+        elif kind == 2:
+            x = np.abs(rng.standard_normal(n)) + 0.1
+        else:
+            x = np.where(rng.random(n) < 0.1, 5.0, 1.0) * (1 + 0.02 * rng.standard_normal(n))
+        kw = dict(warmup_steps=int(rng.integers(20, 150)),
+                  stability_threshold=float(rng.choice([0.01, 0.05, 0.2])),
+                  patience=int(rng.integers(1, 8)), min_warmup=int(rng.integers(5, 30)))
+        a, b = ro._AdaptiveWarmupScheduler(**kw), so._AdaptiveWarmupScheduler(**kw)
+        for t, v in enumerate(x, 1):
+            assert a.update(t, float(v)) == b.update(t, float(v)), (trial, t)
+        assert (a.exited_early, a.actual_warmup_steps) == (b.exited_early, b.actual_warmup_steps)
+        tk = dict(delta_threshold=float(rng.choice([0.02, 0.1, 0.5])),
+                  max_skip=int(rng.integers(1, 30)))
+        c, d = ro._LazyPrecondTrigger(**tk), so._LazyPrecondTrigger(**tk)
+        assert [c.should_update(float(v)) for v in x] == [d.should_update(float(v)) for v in x]
