@@ -119,3 +119,23 @@ def test_host_policies_match_reference_classes():
                   max_skip=int(rng.integers(1, 30)))
         c, d = ro._LazyPrecondTrigger(**tk), so._LazyPrecondTrigger(**tk)
         assert [c.should_update(float(v)) for v in x] == [d.should_update(float(v)) for v in x]
+
+
+@pytest.mark.skipif(not os.path.isdir(REF), reason="reference checkout not present")
+@pytest.mark.parametrize("name", ["scao_sub1b", "scao_1b", "scao_3b", "scao_7b", "scao_40b",
+                                  "scao_125b"])
+def test_presets_configure_like_reference(name):
+    """optimizer.py:958-1002 (the module's final definitions): same group
+    hyperparameters and the same extensions switched on."""
+    sys.path.insert(0, REF)
+    import scao
+    import scao_b200
+    ref = getattr(scao, name)([torch.nn.Parameter(torch.zeros(4, 4))])
+    ours = getattr(scao_b200, name)([torch.nn.Parameter(torch.zeros(4, 4))])
+    rg = {k: v for k, v in ref.param_groups[0].items() if k != "params"}
+    og = {k: v for k, v in ours.param_groups[0].items() if k != "params"}
+    assert rg == {k: og[k] for k in rg}
+    for attr in ("_sparsity", "_dynamic_sparsity", "_adaptive_warmup", "_lazy_precond",
+                 "_use_gsnr_clip", "_adaptive_rank", "_noise_std", "_lookahead_k",
+                 "_lookahead_alpha"):
+        assert getattr(ref, attr) == getattr(ours, attr), attr
