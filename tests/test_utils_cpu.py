@@ -139,3 +139,25 @@ def test_presets_configure_like_reference(name):
                  "_use_gsnr_clip", "_adaptive_rank", "_noise_std", "_lookahead_k",
                  "_lookahead_alpha"):
         assert getattr(ref, attr) == getattr(ours, attr), attr
+
+
+@pytest.mark.skipif(not os.path.isdir(REF), reason="reference checkout not present")
+def test_constructor_defaults_and_errors_match_reference():
+    """optimizer.py:258-304: same defaults in every param group, same
+    attributes of the extensions, same ValueError cases."""
+    sys.path.insert(0, REF)
+    import scao
+    import scao_b200
+    mk = lambda: [torch.nn.Parameter(torch.zeros(3, 3))]
+    ref, ours = scao.SCAO(mk()), scao_b200.SCAO(mk())
+    assert ref.defaults == {k: ours.defaults[k] for k in ref.defaults}
+    for attr in ("_sparsity", "_dynamic_sparsity", "_adaptive_warmup", "_lazy_precond",
+                 "_use_gsnr_clip", "_adaptive_rank", "_noise_std", "_noise_anneal",
+                 "_lookahead_k", "_lookahead_alpha", "_global_step"):
+        assert getattr(ref, attr) == getattr(ours, attr), attr
+    for bad in (dict(lr=-1.0), dict(betas=(1.0, 0.9)), dict(betas=(0.9, -0.1)),
+                dict(beta3=1.5)):
+        with pytest.raises(ValueError):
+            scao.SCAO(mk(), **bad)
+        with pytest.raises(ValueError):
+            scao_b200.SCAO(mk(), **bad)
