@@ -161,3 +161,16 @@ def test_constructor_defaults_and_errors_match_reference():
             scao.SCAO(mk(), **bad)
         with pytest.raises(ValueError):
             scao_b200.SCAO(mk(), **bad)
+
+
+@pytest.mark.skipif(not os.path.isdir(REF), reason="reference checkout not present")
+def test_state_dict_top_level_schema_matches_reference():
+    """optimizer.py:732-756: same top-level keys, runtime keys and group keys."""
+    sys.path.insert(0, REF)
+    import scao
+    import scao_b200
+    mk = lambda: [torch.nn.Parameter(torch.zeros(3, 3))]
+    r, o = scao.SCAO(mk()).state_dict(), scao_b200.SCAO(mk()).state_dict()
+    assert sorted(r) == sorted(o)
+    assert sorted(r["_scao_runtime"]) == sorted(o["_scao_runtime"])
+    assert r["param_groups"][0].keys() == o["param_groups"][0].keys()
