@@ -164,3 +164,18 @@ def test_sync_preconditioner_broadcasts_rank0_state():
             assert eq(g1[name], b1[name]) and not eq(g1[name], b0[name])
         else:
             assert eq(g1[name], b0[name]) and eq(g0[name], b0[name]), name
+
+
+def test_replicated_helpers_single_process():
+    """scao/tests/test_optimizer.py:686-720 on the host: without an initialised
+    process group the helpers are silent no-ops; the FSDP wrapper returns the
+    optimizer with its step patched."""
+    from scao_b200 import SCAO
+    from scao_b200.distributed import sync_preconditioners, wrap_scao_for_fsdp
+    assert not dist.is_initialized()
+    opt = SCAO([torch.nn.Parameter(torch.zeros(64, 256))], lr=1e-3, max_precond_dim=64)
+    sync_preconditioners(opt)
+    with pytest.warns(RuntimeWarning):
+        opt.sync_preconditioner()
+    wrapped = wrap_scao_for_fsdp(opt)
+    assert wrapped is opt and callable(wrapped.step)
