@@ -37,6 +37,8 @@ class Workload:
     # optional (param, modulus, remainder) triples: parameter `param` has no
     # gradient at the steps t with t % modulus == remainder
     grad_skip: tuple = None
+    # optional param groups: ((indices, {overrides}), ...) covering every parameter
+    groups: tuple = None
     notes: str = ""
 
     @property
@@ -106,12 +108,13 @@ def tiny(dtype="float32", max_precond_dim=4096, steps=40, grad_scale=1e-2,
     kw.update(extra or {})
     scales = kw.pop("_grad_scales", None)
     skip = kw.pop("_skip", None)
+    groups = kw.pop("_groups", None)
     kw.pop("_shapes", None)
     kw.pop("_dtypes", None)
     return Workload(
         "tiny", ps, kw,
         grad_rank=4, grad_decay=0.7, param_dtype=dtype, steps=steps,
-        grad_scale=grad_scale, grad_scales=scales, grad_skip=skip)
+        grad_scale=grad_scale, grad_scales=scales, grad_skip=skip, groups=groups)
 
 
 def has_grad(workload, i, t):
@@ -168,3 +171,18 @@ def c5(n_layers: int = 36) -> Workload:
 
 
 WORKLOADS = {"tiny": tiny, "c1": c1, "c2": c2, "c4": c4, "c5": c5}
+
+
+def param_groups(workload, params):
+    """The torch optimizer's first argument for a workload: its parameters, or
+    one group dict per ``groups`` entry (indices into ``params`` + overrides)."""
+    if not workload.groups:
+        return list(params)
+    return [dict(params=[params[i] for i in idx], **ov) for idx, ov in workload.groups]
+
+
+def oracle_groups(workload):
+    """The same groups as index lists for the oracle (None: one group)."""
+    if not workload.groups:
+        return None
+    return [dict(params=list(idx), **ov) for idx, ov in workload.groups]

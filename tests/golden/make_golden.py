@@ -52,6 +52,9 @@ CASES = {
 # recorded (same fields as CASES)
 ORACLE_ONLY = {
     "bf16_r1235": ("bfloat16", 48, 30, 1.0, True),
+    "f32_groups": ("float32", 48, 30, 1.0, True),
+    "bf16_la": ("bfloat16", 4096, 30, 1.0, False),
+    "f32_k128": ("float32", 4096, 24, 1.0, True),
 }
 
 # optimizer keyword overrides of a case: the gradient filter of
@@ -76,12 +79,22 @@ EXTRA = {
     # parameters without a gradient at some steps (skipped by the step,
     # still moved by lookahead, left out of the global-norm average)
     "bf16_skip": dict(_skip=((2, 3, 1), (0, 4, 2), (5, 7, 3))),
-    # bf16 with R1 + R2 + R3 + R5: per-parameter norms are rounded to bf16
-    # (float(p.grad.norm()) of a bf16 gradient) before the host policies see them
+    # bf16 with R1 + R2 + R3 + R5: the global grad-norm average takes
+    # float(p.grad.norm()) of the bf16 gradients, rounded to bf16
     "bf16_r1235": dict(adaptive_warmup=True, warmup_patience=2, warmup_stability_threshold=0.5,
                        lazy_precond=True, lazy_delta_threshold=0.02, lazy_max_skip=4,
                        adaptive_rank=True, k_min=2, k_max=4, sparsity=0.6,
                        dynamic_sparsity=True, _grad_scales=(1.0, 1.0, 0.05, 1.0, 1.0, 1.0)),
+    # param groups with their own lr, weight decay, betas, rank bounds, clip
+    # and warmup (the optimizer reads every group's values each step)
+    "f32_groups": dict(_groups=(((0, 1, 2), dict(lr=2e-3, weight_decay=0.1, betas=(0.85, 0.99),
+                                                   k_max=6)),
+                                ((3, 4, 5), dict(lr=5e-4, weight_decay=0.0, tau=None, k_min=2,
+                                                   warmup_steps=12, beta3=0.9)))),
+    # lookahead every 2 steps with alpha 0.8, LARS off, fp32 factors
+    "bf16_la": dict(lookahead_k=2, lookahead_alpha=0.8, lars_coeff=0.0),
+    # the largest rank the kernels take (k_max 128: kpad 128)
+    "f32_k128": dict(_shapes=((300, 272), (272,)), k_min=8, k_max=128, epsilon_sparse=0.01),
 }
 
 
@@ -97,7 +110,7 @@ def run_case(scao_mod, name, dtype, mpd, steps, gs, int8):
                        grad_scale=gs, int8=int8, extra=EXTRA.get(name))
     params0 = synthetic.init_params(w, seed=0)
     params = [torch.nn.Parameter(p.clone()) for p in params0]
-    opt = scao_mod.SCAO(params, **w.scao_kwargs)
+    opt = scao_mod.SCAO(workloads.param_groups(w, params), **w.scao_kwargs)
     gen = synthetic.LowRankGradients(w, seed=0)
     digests, ks = [], []
     for t in range(steps):

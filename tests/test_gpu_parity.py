@@ -135,7 +135,7 @@ def run_gpu(name, steps=None):
                        extra=EXTRA.get(name))
     p0 = synthetic.init_params(w)
     params = [torch.nn.Parameter(p.clone().to(DEV)) for p in p0]
-    opt = SCAO(params, **w.scao_kwargs)
+    opt = SCAO(workloads.param_groups(w, params), **w.scao_kwargs)
     gen = synthetic.LowRankGradients(w)
     ks = []
     for t in range(steps):

@@ -41,7 +41,7 @@ def run_oracle(name):
                        grad_scale=gs, int8=i8, extra=EXTRA.get(name))
     p0 = [p.float().numpy() for p in synthetic.init_params(w)]
     dts = [str(synthetic.param_dtype(w, i)).replace("torch.", "") for i in range(len(p0))]
-    opt = O.OracleSCAO(p0, dtype=dts, **w.scao_kwargs)
+    opt = O.OracleSCAO(p0, dtype=dts, groups=workloads.oracle_groups(w), **w.scao_kwargs)
     gen = synthetic.LowRankGradients(w)
     ks = []
     for t in range(steps):
@@ -59,8 +59,12 @@ def test_oracle_matches_reference_run(name):
     for i in range(len(p0)):
         st = opt.state[i]
         # Parameter update and moments: relative L2 <= 1e-3 is the parity
-        # bar; the oracle sits orders of magnitude inside it.
-        assert rel_err(opt.params[i] - p0[i], G[f"p{i}"] - p0[i]) < 1e-4
+        # bar; the oracle sits orders of magnitude inside it.  bf16_la (LARS
+        # off, lookahead alpha 0.8, fp32 factors): the fp32 eigen solves differ
+        # at ~1e-5 and updates of several bf16 ulps turn that into rare
+        # rounding flips (0.2-0.5 % of the elements), so only the parity bar.
+        ptol = 1e-3 if name == "bf16_la" else 1e-4
+        assert rel_err(opt.params[i] - p0[i], G[f"p{i}"] - p0[i]) < ptol
         assert rel_err(st["m"], G[f"exp_avg{i}"]) < 1e-4
         assert rel_err(st["v"], G[f"exp_avg_sq{i}"]) < 1e-4
         assert rel_err(st["d"], G[f"exp_avg_diff{i}"]) < 1e-4
