@@ -55,6 +55,7 @@ ORACLE_ONLY = {
     "f32_groups": ("float32", 48, 30, 1.0, True),
     "bf16_la": ("bfloat16", 4096, 30, 1.0, False),
     "f32_k128": ("float32", 4096, 24, 1.0, True),
+    "f32_minpu": ("float32", 48, 30, 1.0, True),
 }
 
 # optimizer keyword overrides of a case: the gradient filter of
@@ -95,6 +96,9 @@ EXTRA = {
     "bf16_la": dict(lookahead_k=2, lookahead_alpha=0.8, lars_coeff=0.0),
     # the largest rank the kernels take (k_max 128: kpad 128)
     "f32_k128": dict(_shapes=((300, 272), (272,)), k_min=8, k_max=128, epsilon_sparse=0.01),
+    # Phase 2 gated by min_precond_updates (3 curvature updates, the third one
+    # made inside the warmup branch of the step that reaches it)
+    "f32_minpu": dict(min_precond_updates=3, precond_freq=4, warmup_steps=4),
 }
 
 
