@@ -76,10 +76,11 @@ class LowRankGradients:
             r, dtype=torch.float64, device=self.device)
         self.UV = []
         for i, spec in enumerate(workload.params):
-            if len(spec.shape) != 2:
+            if len(spec.shape) < 2:
                 self.UV.append(None)
                 continue
-            m, n = spec.shape
+            # parameters of 3+ dims get the low-rank gradient of their (d0, rest) view
+            m, n = spec.shape[0], int(torch.Size(spec.shape[1:]).numel())
             rr = min(r, m, n)
             g = _gen(self.device, seed, 11, i)
             U = _signfix_qr(torch.randn(m, rr, generator=g, device=self.device,
@@ -105,8 +106,8 @@ class LowRankGradients:
                              dtype=torch.float64) * self.noise
             if self.w.grad_scales is not None:
                 x *= self.w.grad_scales[i]
-            grads.append(x.to(param_dtype(self.w, i)))
-            m, n = spec.shape
+            grads.append(x.reshape(spec.shape).to(param_dtype(self.w, i)))
+            m, n = x.shape
             zu = torch.randn(U.shape, generator=g, device=self.device,
                              dtype=torch.float64) / m ** 0.5
             zv = torch.randn(V.shape, generator=g, device=self.device,

@@ -31,6 +31,7 @@ ORACLE_ONLY = {
     "bf16_la": ("bfloat16", 4096, 30, 1.0, False),
     "f32_k128": ("float32", 4096, 24, 1.0, True),
     "f32_minpu": ("float32", 48, 30, 1.0, True),
+    "f32_nd": ("float32", 48, 30, 1.0, True),
 }
 
 # optimizer keyword overrides of a case: the gradient filter of
@@ -74,6 +75,8 @@ EXTRA = {
     # Phase 2 gated by min_precond_updates (3 curvature updates, the third one
     # made inside the warmup branch of the step that reaches it)
     "f32_minpu": dict(min_precond_updates=3, precond_freq=4, warmup_steps=4),
+    # parameters of 3 and 4 dims (conv-like) flattened to (d0, rest) (utils.py:208-219)
+    "f32_nd": dict(_shapes=((16, 4, 6), (24,), (8, 3, 3, 3), (6, 8, 10))),
 }
 
 
