@@ -206,18 +206,56 @@ def rank_cases(utils):
     print("wrote rank")
 
 
+def ckpt_case(scao_mod, steps_before=12, steps_after=10):
+    """A checkpoint of the reference after ``steps_before`` steps of the tiny
+    fp32 int8 workload (Phase 2 reached), saved as its state_dict without the
+    pickled preconditioner objects (everything the schema needs is in
+    ``_scao_precond``), and the reference's state ``steps_after`` steps later:
+    the GPU test loads the checkpoint into scao_b200.SCAO and continues."""
+    w = workloads.tiny(dtype="float32", max_precond_dim=48, steps=steps_before + steps_after,
+                       grad_scale=1.0, int8=True)
+    params = [torch.nn.Parameter(p.clone()) for p in synthetic.init_params(w, seed=0)]
+    opt = scao_mod.SCAO(params, **w.scao_kwargs)
+    gen = synthetic.LowRankGradients(w, seed=0)
+    for t in range(steps_before):
+        for p, g in zip(params, gen.next()):
+            p.grad = g.clone()
+        opt.step()
+    sd = opt.state_dict()
+    sd["state"] = {i: {k: v for k, v in st.items() if k != "preconditioner"}
+                   for i, st in sd["state"].items()}
+    torch.save({"state_dict": sd, "params": [p.detach().clone() for p in params]},
+               os.path.join(HERE, "ckpt_tiny_f32.pt"))
+    for t in range(steps_after):
+        for p, g in zip(params, gen.next()):
+            p.grad = g.clone()
+        opt.step()
+    out = {"steps_before": np.array(steps_before), "steps_after": np.array(steps_after)}
+    for i, p in enumerate(params):
+        out[f"p{i}"] = p.detach().numpy()
+        out[f"exp_avg{i}"] = opt.state[p]["exp_avg"].numpy()
+        out[f"k{i}"] = np.array(opt.state[p]["preconditioner"].k)
+    np.savez_compressed(os.path.join(HERE, "ckpt_tiny_f32_after.npz"), **out)
+    print("wrote ckpt")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="reference checkout root")
     ap.add_argument("--only", nargs="*", help="regenerate only these run cases")
+    ap.add_argument("--ckpt", action="store_true", help="regenerate only the checkpoint case")
     a = ap.parse_args()
     sys.path.insert(0, a.ref)
     import scao  # noqa: E402  (the reference package)
     from scao import utils  # noqa: E402
     torch.set_num_threads(min(8, os.cpu_count() or 1))
+    if a.ckpt:
+        ckpt_case(scao)
+        return
     if not a.only:
         quant_cases(utils)
         rank_cases(utils)
+        ckpt_case(scao)
     for name, args in {**CASES, **ORACLE_ONLY}.items():
         if not a.only or name in a.only:
             run_case(scao, name, *args)
