@@ -80,3 +80,30 @@ def test_strips_and_leaves_tile_the_parameter(shape, mpd):
         v.diag_ema.fill_(1.0)
     assert int(plan.diag_ema.sum().item()) == sum(int(S["count"]) for S in plan.stab)
     assert pv.k_host(plan.k.numpy()) >= 1
+
+
+def test_reference_checkpoint_schema_matches_ours():
+    """The committed reference checkpoint (make_golden.py --ckpt) has, per
+    parameter, the same nested preconditioner schema as ours -- keys, block
+    nesting, factor shapes and dtypes -- so load_state_dict can take it."""
+    from golden_util import HERE
+    from scao_b200 import workloads
+    d = torch.load(os.path.join(HERE, "ckpt_tiny_f32.pt"))
+    w = workloads.tiny(dtype="float32", max_precond_dim=48, grad_scale=1.0, int8=True)
+    g = dict(dict(epsilon_sparse=0.05, rho=0.999), **w.scao_kwargs)
+    plan = Plan([torch.zeros(s.shape) for s in w.params], [g] * len(w.params),
+                torch.device("cpu"), True)
+
+    def shape_only(x):
+        if isinstance(x, dict):
+            return {k: shape_only(v) for k, v in x.items()
+                    if k not in ("k", "precond_step", "U_l", "S_l", "U_r", "S_r")}
+        if isinstance(x, list):
+            return [shape_only(v) for v in x]
+        if torch.is_tensor(x):
+            return (tuple(x.shape), x.dtype)
+        return type(x).__name__ if isinstance(x, float) else x
+
+    for i in range(len(w.params)):
+        ours = PrecondView(plan, i, g).state_dict()
+        assert shape_only(d["state_dict"]["_scao_precond"][i]) == shape_only(ours), i
