@@ -186,6 +186,16 @@ class SCAO(Optimizer):
     # ------------------------------------------------------------------
     # plan / state
     # ------------------------------------------------------------------
+    def add_param_group(self, param_group: dict) -> None:
+        """torch.optim.Optimizer.add_param_group.  Groups can be added until
+        the first step; the device plan (arenas, tables, filter and
+        lookahead state) is laid out for the parameter set of that step."""
+        if getattr(self, "_plan", None) is not None:
+            raise NotImplementedError(
+                "scao_b200.SCAO: add_param_group after the first step is not supported; "
+                "pass every parameter group to the constructor (or add them before stepping)")
+        super().add_param_group(param_group)
+
     def _flat(self):
         ps, gs = [], []
         for g in self.param_groups:

@@ -174,3 +174,17 @@ def test_state_dict_top_level_schema_matches_reference():
     assert sorted(r) == sorted(o)
     assert sorted(r["_scao_runtime"]) == sorted(o["_scao_runtime"])
     assert r["param_groups"][0].keys() == o["param_groups"][0].keys()
+
+
+def test_add_param_group_before_first_step_only():
+    """Groups added before the first step join the plan with the defaults
+    filled in; after it (plan laid out) the call raises instead of failing
+    later inside the step."""
+    import scao_b200
+    o = scao_b200.SCAO([torch.nn.Parameter(torch.zeros(3, 3))])
+    o.add_param_group({"params": [torch.nn.Parameter(torch.zeros(4))], "lr": 1e-2})
+    assert len(o.param_groups) == 2 and o.param_groups[1]["lr"] == 1e-2
+    assert o.param_groups[1]["k_max"] == o.defaults["k_max"]
+    o._plan = object()          # stands for the plan the first step builds
+    with pytest.raises(NotImplementedError):
+        o.add_param_group({"params": [torch.nn.Parameter(torch.zeros(2))]})
