@@ -12,11 +12,11 @@ curvature factors and its eigenfactors -- is owned by exactly one rank:
 
 Because the step is independent per parameter (the LARS trust ratio and the
 curvature clip are per-parameter reductions), the result is identical to the
-single-GPU step on the averaged gradient.  One exception: the global
-grad-norm EMA (optimizer.py:439-446) is kept by each rank's optimizer over the
-parameters that rank owns; it only steers the optional R1 adaptive warmup, R2
-dynamic sparsity and R5 adaptive rank, which therefore see a per-rank average
-under this wrapper.  ``sync_preconditioners`` and
+single-GPU step on the averaged gradient.  The global grad-norm
+EMA (optimizer.py:439-446), which steers the optional R1 adaptive warmup, R2
+dynamic sparsity and R5 adaptive rank, is an average over all parameters:
+when one of them is on, the owners exchange their per-parameter norms each
+step (one small all-reduce) before any bucket steps.  ``sync_preconditioners`` and
 ``wrap_scao_for_fsdp`` keep the reference's API for replicated optimizers.
 """
 from __future__ import annotations
@@ -182,6 +182,16 @@ class ShardedSCAO:
                      if self.nccl else None)
         self.skip_comm = False       # measurement only: compute without collectives
         self.skip_compute = False    # measurement only: collectives without compute
+        # R1 / R2-dynamic / R5 steer by the global grad-norm EMA, an average
+        # over ALL parameters: the owners exchange their norms each step
+        # (one small all-reduce) and every inner optimizer takes that average
+        self.norm_sync = any(o is not None and (getattr(o, "_host_norms", False) or
+                                                getattr(o, "_dynamic_sparsity", False))
+                             for o in self.inner)
+        if self.norm_sync:
+            for o in self.inner:
+                if o is not None:
+                    o._host_norms = True      # the host keeps the EMA (from the average)
 
     def owned_specs(self):
         return [self.specs[i] for i in self.my]
@@ -232,6 +242,29 @@ class ShardedSCAO:
             self.params[i].grad = self.my_g[o:o + self.params[i].numel()].view_as(self.params[i])
         self.cur = flat
 
+    # global grad-norm average ---------------------------------------------
+    def _share_norm_average(self):
+        """optimizer.py:439-446 over all parameters: each owner contributes
+        float(p.grad.norm()) of its averaged gradients (in the gradient's
+        dtype), one all-reduce makes the full list known everywhere, and the
+        average is summed in parameter order; every inner optimizer uses it
+        this step."""
+        from .optimizer import _in_param_dtypes
+        n = len(self.params)
+        vec = torch.zeros(n, dtype=torch.float64, device=self.device)
+        if self.my:
+            mine = [self.params[i] for i in self.my]
+            f32 = torch.stack([torch.linalg.vector_norm(p.grad.float()) for p in mine])
+            rounded = _in_param_dtypes(f32.cpu().numpy(), mine)
+            vec[self.my] = torch.from_numpy(rounded.astype("float64")).to(self.device)
+        dist.all_reduce(vec, group=self.group)
+        norms = vec.cpu().tolist()
+        avg = sum(norms) / n if n else 0.0
+        for o in self.inner:
+            if o is not None:
+                o._norm_average = (lambda a, c: (lambda _live: (a, c)))(avg, n)
+        return avg
+
     # step -------------------------------------------------------------------
     def step(self):
         self.global_step += 1
@@ -245,9 +278,12 @@ class ShardedSCAO:
                 dist.all_reduce(tmp, group=self.group)
                 seg = self.layout.seg[b]
                 mine_g.copy_(tmp[self.rank * seg:(self.rank + 1) * seg] / self.world)
+            if self.norm_sync:
+                self._share_norm_average()
+            for b in range(nb):
                 if self.inner[b] is not None:
                     self.inner[b].step()
-                full_p, _, _ = self._views(self.flat_p, b)
+                full_p, mine_p, _ = self._views(self.flat_p, b)
                 parts = list(full_p.chunk(self.world))
                 dist.all_gather(parts, mine_p.clone(), group=self.group)
                 full_p.copy_(torch.cat(parts))
@@ -263,6 +299,11 @@ class ShardedSCAO:
                     dist.reduce_scatter_tensor(mine_g, full_g, op=dist.ReduceOp.AVG,
                                                group=self.group)
                 ev_rs[b].record(C)
+        if self.norm_sync:
+            # the average needs every bucket's gradients: no step starts before
+            for b in range(nb):
+                D.wait_event(ev_rs[b])
+            self._share_norm_average()
         for b in range(nb):
             D.wait_event(ev_rs[b])
             if self.inner[b] is not None and not self.skip_compute:

@@ -180,6 +180,9 @@ class SCAO(Optimizer):
         self._eig_max_iters = int(eig_max_iters)
         self._eig_tol = float(eig_tol)
         self._plan: Plan | None = None
+        # set by an owner-compute wrapper: the global grad-norm average over
+        # all ranks' parameters for this step (callable(local norms) -> (avg, n))
+        self._norm_average = None
         self._ema_scratch = None
         self._last_eig_status = None
 
@@ -304,8 +307,12 @@ class SCAO(Optimizer):
             # (optimizer.py:440); R3 / R5 use the float32 norm (:531-532)
             avg_norms = _in_param_dtypes(norms, ps)
             live = [float(avg_norms[i]) for i in range(len(ps)) if grads[i] is not None]
-            avg = sum(live) / len(live) if live else 0.0
-            if live:
+            if self._norm_average is not None:
+                # owner-compute across ranks: the all-parameter average
+                avg, n_live = self._norm_average(live)
+            else:
+                avg, n_live = (sum(live) / len(live) if live else 0.0), len(live)
+            if n_live:
                 self._gema = 0.95 * self._gema + 0.05 * avg           # optimizer.py:445
             plan.global_norm_ema.fill_(self._gema)
         warm_max = max((g.get("warmup_steps", 100) for g in self.param_groups), default=100)

@@ -179,3 +179,62 @@ def test_replicated_helpers_single_process():
         opt.sync_preconditioner()
     wrapped = wrap_scao_for_fsdp(opt)
     assert wrapped is opt and callable(wrapped.step)
+
+
+class _NormProbe(_SGD):
+    """Inner stand-in with a host-norm extension switched on: records the
+    global grad-norm average the wrapper hands it each step."""
+    _host_norms = True
+
+    def __init__(self, pairs):
+        super().__init__(pairs)
+        self._norm_average = None
+        self.seen = []
+
+    def step(self):
+        self.seen.append(self._norm_average(None))
+        super().step()
+
+
+def _norm_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        w = workloads.tiny()
+        torch.manual_seed(0)
+        params = [torch.randn(s.shape) for s in w.params]
+        gen = torch.Generator().manual_seed(5)
+        base = [torch.randn(s.shape, generator=gen) for s in w.params]
+        opt = ShardedSCAO(params, w, _NormProbe, buckets=2)
+        assert opt.norm_sync
+        res = []
+        for t in range(2):
+            grads = [b * (rank + 1) * (t + 1) for b in base]
+            opt.load_grads(grads)
+            opt.step()
+            avg_g = [b * (1 + world) / 2.0 * (t + 1) for b in base]
+            want = sum(float(torch.linalg.vector_norm(g.float())) for g in avg_g) / len(avg_g)
+            got = [o.seen[-1] for o in opt.inner if o is not None]
+            res.append((want, got))
+        q.put((rank, res))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_global_norm_average_over_all_parameters():
+    """With R1 / R2-dynamic / R5 on, every inner optimizer of every rank gets
+    the average of all parameters' norms (optimizer.py:439-446), not of the
+    ones it owns."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_norm_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for _, steps in res:
+        for want, got in steps:
+            assert got and all(abs(a - want) <= 1e-6 * want and n == 6 for a, n in got)
