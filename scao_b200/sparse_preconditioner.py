@@ -13,7 +13,9 @@ The diagonal blocks' elementwise formula and the k x k projection of
 ``natural_grad_norm`` are small tensor expressions on the device.
 
 CUDA tensors only: construction works anywhere (the checkpoint schema can be
-inspected on the host), the compute methods raise on a CPU tensor.
+inspected on the host), the compute methods raise on a CPU tensor.  The
+kernels read gradients in the parameter's dtype: a float32 gradient passed for
+a bf16 parameter is rounded to bf16 first (the reference takes it as float32).
 """
 from __future__ import annotations
 
