@@ -227,7 +227,10 @@ class ShardedSCAO:
     def flat_grad_from_params(self):
         """Training-loop entry: gather every parameter's local .grad (as left
         by backward) into the flat buffer, then point the owned parameters'
-        .grad back at their shard of the reduced gradient."""
+        .grad back at their shard of the reduced gradient.  With
+        ``attach_grad_hooks`` the hooks have done this already (no-op)."""
+        if getattr(self, "_pending", None) is not None:
+            return
         if getattr(self, "_train_flat", None) is None:
             self._train_flat = torch.zeros(self.layout.total, dtype=self.dtype, device=self.device)
         flat = self._train_flat
@@ -241,6 +244,79 @@ class ShardedSCAO:
             o = self.layout.shard_offset(i)
             self.params[i].grad = self.my_g[o:o + self.params[i].numel()].view_as(self.params[i])
         self.cur = flat
+
+    # reduce-scatter overlapped with backward -------------------------------
+    def attach_grad_hooks(self):
+        """For training loops with one backward per step: every parameter's
+        gradient is copied into the flat buffer as soon as autograd has
+        accumulated it (a post-accumulate-grad hook, which then drops the
+        local .grad), and a bucket's reduce-scatter is queued -- NCCL: on the
+        communication stream -- when its last gradient has arrived, so the
+        gradient reduction overlaps the rest of backward.  ``step()`` reduces
+        the buckets still pending (parameters that got no gradient count as
+        zero).  With gradient accumulation over several backward passes use
+        ``flat_grad_from_params`` instead."""
+        lay = self.layout
+        if getattr(self, "_train_flat", None) is None:
+            self._train_flat = torch.zeros(lay.total, dtype=self.dtype, device=self.device)
+        self._bucket_size = [sum(1 for i in range(len(self.params)) if lay.bucket[i] == b)
+                             for b in range(lay.nb)]
+        self._pending = None
+        from functools import partial
+        self._hooks = [p.register_post_accumulate_grad_hook(partial(self._grad_ready, i))
+                       for i, p in enumerate(self.params)]
+
+    def _grad_ready(self, i, p):
+        if self._pending is None:            # first gradient of this backward
+            self._pending = list(self._bucket_size)
+            self._got = [False] * len(self.params)
+            self._ev_rs = [None] * self.layout.nb
+        o = self.layout.global_offset(i)
+        self._train_flat[o:o + p.numel()].copy_(p.grad.reshape(-1))
+        self._got[i] = True
+        p.grad = None
+        b = self.layout.bucket[i]
+        self._pending[b] -= 1
+        if self._pending[b] == 0:
+            self._reduce_bucket(b)
+
+    def _reduce_bucket(self, b):
+        full_g, _, mine_g = self._views(self._train_flat, b)
+        if self.nccl:
+            D = torch.cuda.current_stream(self.device)
+            ready = torch.cuda.Event()
+            ready.record(D)
+            with torch.cuda.stream(self.comm):
+                self.comm.wait_event(ready)
+                if not self.skip_comm:
+                    dist.reduce_scatter_tensor(mine_g, full_g, op=dist.ReduceOp.AVG,
+                                               group=self.group)
+                done = torch.cuda.Event()
+                done.record(self.comm)
+            self._ev_rs[b] = done
+        else:
+            tmp = full_g.clone()
+            dist.all_reduce(tmp, group=self.group)
+            seg = self.layout.seg[b]
+            mine_g.copy_(tmp[self.rank * seg:(self.rank + 1) * seg] / self.world)
+            self._ev_rs[b] = True
+        self._pending[b] = -1
+
+    def _finish_hooked_reduction(self):
+        """Reduce the buckets whose gradients did not all arrive, then point
+        the owned parameters' .grad at their reduced shard."""
+        lay = self.layout
+        for b in range(lay.nb):
+            if self._pending[b] != -1:
+                for i in range(len(self.params)):
+                    if lay.bucket[i] == b and not self._got[i]:
+                        o = lay.global_offset(i)
+                        self._train_flat[o:o + self.params[i].numel()].zero_()
+                self._reduce_bucket(b)
+        for i in self.my:
+            o = lay.shard_offset(i)
+            self.params[i].grad = self.my_g[o:o + self.params[i].numel()].view_as(self.params[i])
+        self.cur = self._train_flat
 
     # global grad-norm average ---------------------------------------------
     def _share_norm_average(self):
@@ -268,11 +344,23 @@ class ShardedSCAO:
     # step -------------------------------------------------------------------
     def step(self):
         self.global_step += 1
+        hooked = getattr(self, "_pending", None) is not None
+        if hooked:
+            self._finish_hooked_reduction()
         if self.cur is None:
             raise RuntimeError("no gradients staged (load_grads / flat_grad_from_params)")
+        try:
+            self._step(hooked)
+        finally:
+            if hooked:
+                self._pending = None
+
+    def _step(self, hooked):
         nb = self.layout.nb
         if not self.nccl:
             for b in range(nb):
+                if hooked:
+                    break                       # reduced during backward
                 full_g, mine_p, mine_g = self._views(self.cur, b)
                 tmp = full_g.clone()
                 dist.all_reduce(tmp, group=self.group)
@@ -291,14 +379,17 @@ class ShardedSCAO:
         D = torch.cuda.current_stream(self.device)
         C = self.comm
         C.wait_stream(D)
-        ev_rs = [torch.cuda.Event() for _ in range(nb)]
-        with torch.cuda.stream(C):
-            for b in range(nb):
-                full_g, _, mine_g = self._views(self.cur, b)
-                if not self.skip_comm:
-                    dist.reduce_scatter_tensor(mine_g, full_g, op=dist.ReduceOp.AVG,
-                                               group=self.group)
-                ev_rs[b].record(C)
+        if hooked:
+            ev_rs = self._ev_rs                 # queued during backward
+        else:
+            ev_rs = [torch.cuda.Event() for _ in range(nb)]
+            with torch.cuda.stream(C):
+                for b in range(nb):
+                    full_g, _, mine_g = self._views(self.cur, b)
+                    if not self.skip_comm:
+                        dist.reduce_scatter_tensor(mine_g, full_g, op=dist.ReduceOp.AVG,
+                                                   group=self.group)
+                    ev_rs[b].record(C)
         if self.norm_sync:
             # the average needs every bucket's gradients: no step starts before
             for b in range(nb):

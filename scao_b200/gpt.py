@@ -12,6 +12,8 @@ positions, LM head tied to the token embedding, N(0, 0.02^2) init.
 on one GPU ``opt.step()``; across ranks the owner-compute ``ShardedSCAO``
 (gradient reduce-scatter with averaging, owned step, parameter all-gather),
 which is the data-parallel step -- every rank ends with identical weights.
+After ``sharded.attach_grad_hooks()`` the gradient reduce-scatter of each
+bucket starts during backward instead of after it.
 """
 from __future__ import annotations
 

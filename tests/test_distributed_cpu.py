@@ -238,3 +238,64 @@ def test_sharded_global_norm_average_over_all_parameters():
     for _, steps in res:
         for want, got in steps:
             assert got and all(abs(a - want) <= 1e-6 * want and n == 6 for a, n in got)
+
+
+def _hook_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import torch.nn as nn
+        from scao_b200.workloads import ParamSpec, Workload
+
+        def model_and_inputs():
+            torch.manual_seed(0)
+            m = nn.Sequential(nn.Linear(16, 32), nn.ReLU(), nn.Linear(32, 8))
+            xs = [torch.randn(4, 16, generator=torch.Generator().manual_seed(10 + r))
+                  for r in range(world)]
+            return m, xs
+
+        # expected: SGD on the gradient averaged over the ranks' batches
+        m_ref, xs = model_and_inputs()
+        grads = []
+        for x in xs:
+            m_ref.zero_grad()
+            m_ref(x).pow(2).mean().backward()
+            grads.append([p.grad.clone() for p in m_ref.parameters()])
+        want = [p.detach() - 0.1 * sum(g[i] for g in grads) / world
+                for i, p in enumerate(m_ref.parameters())]
+
+        m, xs = model_and_inputs()
+        params = list(m.parameters())
+        wl = Workload("mlp", [ParamSpec(f"p{i}", tuple(p.shape)) for i, p in enumerate(params)],
+                      {}, 1, 1.0)
+        opt = ShardedSCAO(params, wl, _SGD, buckets=2)
+        opt.attach_grad_hooks()
+        m.zero_grad(set_to_none=True)
+        m(xs[rank]).pow(2).mean().backward()
+        # every bucket holding parameters was reduced before step() (a bucket
+        # the layout leaves empty is reduced in step(), on every rank alike)
+        reduced_in_backward = all(x == -1 for x, n in zip(opt._pending, opt._bucket_size) if n) \
+            and any(opt._bucket_size)
+        opt.step()
+        err = max(float((p.detach() - w).abs().max()) for p, w in zip(params, want))
+        q.put((rank, reduced_in_backward, err, opt._pending is None))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_reduce_scatter_overlapped_with_backward():
+    """attach_grad_hooks: every bucket is reduced during backward (as its
+    last gradient arrives) and the step equals SGD on the rank-averaged
+    gradient."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_hook_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for _, in_bwd, err, reset in res:
+        assert in_bwd and reset and err < 1e-6, (in_bwd, err)
