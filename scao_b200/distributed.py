@@ -412,6 +412,29 @@ class ShardedSCAO:
     def _global_step(self):
         return self.global_step
 
+    # checkpoint -------------------------------------------------------------
+    def state_dict(self):
+        """This rank's shard of the optimizer state: the state of the
+        parameters it owns (one inner optimizer per bucket, in the
+        reference's schema), with the layout it belongs to.  Each rank saves
+        its own; the parameters themselves are the model's (views into the
+        flat parameter buffer)."""
+        return {"world_size": self.world, "rank": self.rank, "owner": list(self.owner),
+                "buckets": self.layout.nb, "global_step": self.global_step,
+                "inner": [o.state_dict() if o is not None else None for o in self.inner]}
+
+    def load_state_dict(self, state):
+        """Load this rank's shard saved by ``state_dict`` under the same
+        world size, ownership and bucket layout."""
+        if (state["world_size"], state["rank"], list(state["owner"]), state["buckets"]) != \
+                (self.world, self.rank, list(self.owner), self.layout.nb):
+            raise ValueError("sharded optimizer checkpoint of a different layout "
+                             "(world size, rank, ownership or buckets)")
+        self.global_step = int(state["global_step"])
+        for o, s in zip(self.inner, state["inner"]):
+            if o is not None:
+                o.load_state_dict(s)
+
 
 # ---------------------------------------------------------------------------
 # reference-API helpers for replicated optimizers (scao/distributed.py)

@@ -299,3 +299,81 @@ def test_reduce_scatter_overlapped_with_backward():
         assert p.exitcode == 0
     for _, in_bwd, err, reset in res:
         assert in_bwd and reset and err < 1e-6, (in_bwd, err)
+
+
+class _Momentum:
+    """Stateful inner stand-in: heavy-ball SGD with a checkpointable buffer."""
+
+    def __init__(self, pairs):
+        self.ps = [p for p, _ in pairs]
+        self.buf = [torch.zeros_like(p) for p in self.ps]
+
+    def step(self):
+        for p, b in zip(self.ps, self.buf):
+            b.mul_(0.9).add_(p.grad)
+            p.data.add_(b, alpha=-0.1)
+
+    def state_dict(self):
+        return {"buf": [b.clone() for b in self.buf]}
+
+    def load_state_dict(self, st):
+        for b, s in zip(self.buf, st["buf"]):
+            b.copy_(s)
+
+
+def _ckpt_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        w = workloads.tiny()
+
+        def fresh():
+            torch.manual_seed(0)
+            params = [torch.randn(s.shape) for s in w.params]
+            return params, ShardedSCAO(params, w, _Momentum, buckets=2)
+
+        grads = [[torch.full(s.shape, float(t + rank + 1)) for s in w.params] for t in range(3)]
+        pa, a = fresh()
+        for t in range(3):
+            a.load_grads(grads[t])
+            a.step()
+        pb, b = fresh()
+        for t in range(2):
+            b.load_grads(grads[t])
+            b.step()
+        sd = b.state_dict()
+        saved_p = [p.detach().clone() for p in pb]
+        pc, c = fresh()
+        for p, s in zip(pc, saved_p):
+            p.data.copy_(s)
+        c.load_state_dict(sd)
+        c.load_grads(grads[2])
+        c.step()
+        err = max(float((x - y).abs().max()) for x, y in zip(pa, pc))
+        bad = False
+        try:
+            sd2 = dict(sd, buckets=3)
+            c.load_state_dict(sd2)
+        except ValueError:
+            bad = True
+        q.put((rank, err, bad, c.global_step))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_checkpoint_resume():
+    """Each rank saves its shard; a fresh wrapper that loads it (and the
+    parameters) continues exactly like the uninterrupted run; a checkpoint of
+    another layout is refused."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ckpt_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for _, err, bad, gs in res:
+        assert err == 0.0 and bad and gs == 3
