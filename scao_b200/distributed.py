@@ -193,6 +193,13 @@ class ShardedSCAO:
                 if o is not None:
                     o._host_norms = True      # the host keeps the EMA (from the average)
 
+    @property
+    def param_groups(self):
+        """The param groups of this rank's inner optimizers (the same dicts):
+        learning-rate changes made here reach the step, e.g.
+        ``for g in sharded.param_groups: g["lr"] = lr``."""
+        return [g for o in self.inner if o is not None for g in getattr(o, "param_groups", [])]
+
     def owned_specs(self):
         return [self.specs[i] for i in self.my]
 

@@ -350,6 +350,7 @@ def _ckpt_worker(rank, world, port, q):
         c.load_grads(grads[2])
         c.step()
         err = max(float((x - y).abs().max()) for x, y in zip(pa, pc))
+        assert c.param_groups == []           # stand-ins carry no param groups
         bad = False
         try:
             sd2 = dict(sd, buckets=3)
