@@ -1836,8 +1836,8 @@ extern "C" int scao_plan_step(const ScaoPlanDev* P, void* stream) {
     }
     const bool fn = P->filt.mode != 0 || P->filt.noise_on != 0 || P->filt.gsnr_on != 0;
     if (P->n_panels > 0) {
-        static bool pattr = false;
-        if (!pattr) {
+        static PerDeviceOnce pattr;
+        if (pattr.first()) {
             cudaFuncSetAttribute(proj_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)proj_tc_smem(128));
             cudaFuncSetAttribute(apply_kron_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1851,14 +1851,12 @@ extern "C" int scao_plan_step(const ScaoPlanDev* P, void* stream) {
             cudaFuncSetAttribute(proj_bf16_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
             cudaFuncSetAttribute(proj_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
             cudaFuncSetAttribute(apply_kron_tc_kernel<false>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-            pattr = true;
         }
         if (P->tmaps_ok) {
-            static bool tattr = false;
-            if (!tattr) {
+            static PerDeviceOnce tattr;
+            if (tattr.first()) {
                 cudaFuncSetAttribute(proj_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)proj_tma_smem(128));
-                tattr = true;
             }
             const int g = scao_persistent_grid(P, P->n_panels);
             ProfScope _ps(SLOT_PROJ, st);
@@ -1881,21 +1879,19 @@ extern "C" int scao_plan_step(const ScaoPlanDev* P, void* stream) {
     if (P->n_leaves > 0) {
         const int kp = P->kpad_max;
         const size_t sm = (size_t)(kp * kp + 4 * kp) * 4;
-        static bool attr = false;
-        if (!attr) {
+        static PerDeviceOnce attr;
+        if (attr.first()) {
             cudaFuncSetAttribute(leaf_coef_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (128 * 128 + 4 * 128) * 4);
-            attr = true;
         }
         { ProfScope _ps(SLOT_LEAF_COEF, st); leaf_coef_kernel<<<P->n_leaves, NT, sm, st>>>(*P); }
         SCAO_CHECK_LAUNCH();
         {
             const size_t smw = (size_t)(kp * ((kp + 15) & ~15) + TC_T * (((kp + 15) & ~15) + 4)) * 4;
-            static bool wattr = false;
-            if (!wattr) {
+            static PerDeviceOnce wattr;
+            if (wattr.first()) {
                 cudaFuncSetAttribute(leaf_w_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)((128 * 128 + 128 * 132) * 4));
-                wattr = true;
             }
             ProfScope _ps(SLOT_LEAF_COEF, st);
             leaf_w_kernel<<<dim3(P->max_leaf_rows_tiles, P->n_leaves), 256, smw, st>>>(*P);
@@ -1910,8 +1906,8 @@ extern "C" int scao_plan_step(const ScaoPlanDev* P, void* stream) {
     SCAO_CHECK_LAUNCH();
     if (P->n_tiles > 0) {
         { ProfScope _ps(SLOT_APPLY_KRON, st);
-          static bool aattr = false;
-          if (!aattr) {
+          static PerDeviceOnce aattr;
+          if (aattr.first()) {
               // the largest launch size over kpad_max
               size_t m0 = 0, m1 = 0;
               for (int k = 16; k <= 128; k += 16) {
@@ -1920,7 +1916,6 @@ extern "C" int scao_plan_step(const ScaoPlanDev* P, void* stream) {
               }
               cudaFuncSetAttribute(apply_tma_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m0);
               cudaFuncSetAttribute(apply_tma_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m1);
-              aattr = true;
           }
           const int g = scao_persistent_grid(P, P->n_tiles);
           if (P->tmaps_ok) {

@@ -7,6 +7,20 @@
 
 #include "../../include/scao_b200.h"
 
+// Kernel attributes (cudaFuncSetAttribute) belong to the function in the
+// current device's context: a launcher sets them once per device.
+struct PerDeviceOnce {
+    bool done[64] = {};
+    // true for the first call on the current device
+    bool first() {
+        int d = 0;
+        if (cudaGetDevice(&d) != cudaSuccess || d < 0 || d >= 64) return true;
+        if (done[d]) return false;
+        done[d] = true;
+        return true;
+    }
+};
+
 #define SCAO_DEV __device__ __forceinline__
 
 // per-parameter scalar slots of ScaoPlanDev::param_scalars (8 floats each)

@@ -615,13 +615,12 @@ extern "C" int scao_plan_eigen(const ScaoPlanDev* P, const int32_t* leaf_ids, in
     if (n_iter == 0) max_iters = 0;
     const size_t jsm = jacobi_smem(smax);
     const size_t csm = (size_t)2 * smax * (smax + 1) * 4;
-    static bool attr_done = false;
-    if (!attr_done) {
+    static PerDeviceOnce attr_done;
+    if (attr_done.first()) {
         cudaFuncSetAttribute(eig_jacobi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)jacobi_smem(SMAX));
         cudaFuncSetAttribute(eig_cholinv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)((size_t)2 * SMAX * (SMAX + 1) * 4));
-        attr_done = true;
     }
     const int tiles_nn = ((nmax + TM - 1) / TM) * ((smax + TN - 1) / TN);
     const int tiles_ss = ((smax + TM - 1) / TM) * ((smax + TN - 1) / TN);

@@ -840,11 +840,10 @@ extern "C" int scao_plan_curvature(const ScaoPlanDev* P, const int32_t* leaf_ids
         const int32_t* ids = leaf_ids + j0 / 2;
         dim3 grid(tiles, np);
         if (tma_on) {
-            static bool tattr = false;
-            if (!tattr) {
+            static PerDeviceOnce tattr;
+            if (tattr.first()) {
                 cudaFuncSetAttribute(gram_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)gram_tma_smem());
-                tattr = true;
             }
             const int64_t work = (int64_t)np * tpp;
             const int g = scao_persistent_grid(P, work);
@@ -854,13 +853,12 @@ extern "C" int scao_plan_curvature(const ScaoPlanDev* P, const int32_t* leaf_ids
         }
         SCAO_CHECK_LAUNCH();
         if (fallback) {
-            static bool attr = false;
-            if (!attr) {
+            static PerDeviceOnce attr;
+            if (attr.first()) {
                 cudaFuncSetAttribute(gram_ema_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)gram_tc_smem());
                 cudaFuncSetAttribute(gram_ema_tc_kernel,
                                      cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-                attr = true;
             }
             const int nt2 = (int)((mx + GT - 1) / GT);
             ProfScope _ps2(SLOT_GRAM_EMA, st);
