@@ -88,3 +88,25 @@ def test_struct_layouts_match_header(tmp_path):
         assert got[("filt", f)] == getattr(_lib.FilterDev, f).offset, f
     for f in _lib.FILTER_PARAM_DT.names:
         assert got[("fparam", f)] == _lib.FILTER_PARAM_DT.fields[f][1], f
+
+
+def test_cpp_consumer_compiles_against_header():
+    """The C++ host of tests/cabi (no Python, no torch) compiles against
+    include/scao_b200.h and links against the library; it runs on a GPU in
+    test_gpu_cabi_cpp.py."""
+    import shutil
+    import subprocess
+    import tempfile
+    cxx = shutil.which("g++")
+    if cxx is None:
+        import pytest
+        pytest.skip("no host C++ compiler")
+    cuda_inc = "/usr/local/cuda/include"
+    lib = _lib.lib()._name
+    with tempfile.TemporaryDirectory() as d:
+        exe = os.path.join(d, "consumer")
+        subprocess.check_call([cxx, "-std=c++17", "-O1", "-I", os.path.join(ROOT, "include"),
+                               "-I", cuda_inc, os.path.join(ROOT, "tests", "cabi", "consumer.cpp"),
+                               lib, "-L/usr/local/cuda/lib64", "-lcudart",
+                               "-Wl,-rpath," + os.path.dirname(lib), "-o", exe])
+        assert os.path.exists(exe)
