@@ -16,15 +16,24 @@ const char* kNames[SLOT_COUNT] = {
 std::atomic<int64_t> g_launches{0};
 std::atomic<int> g_enabled{0};
 std::mutex g_mu;
-struct Pending { int slot; cudaEvent_t a, b; };
+struct Pending { int slot; cudaEvent_t a, b; int dev; };
 std::vector<Pending> g_pending;
-std::vector<cudaEvent_t> g_pool;
+// finished events for reuse, by device (an event records only on streams of
+// the device it was created on)
+std::vector<cudaEvent_t> g_pool[64];
 cudaEvent_t g_open[SLOT_COUNT];
 double g_ms[SLOT_COUNT];
 int64_t g_cnt[SLOT_COUNT];
 
+int cur_device() {
+    int d = 0;
+    if (cudaGetDevice(&d) != cudaSuccess || d < 0 || d >= 64) d = 0;
+    return d;
+}
+
 cudaEvent_t get_event() {
-    if (!g_pool.empty()) { cudaEvent_t e = g_pool.back(); g_pool.pop_back(); return e; }
+    std::vector<cudaEvent_t>& pool = g_pool[cur_device()];
+    if (!pool.empty()) { cudaEvent_t e = pool.back(); pool.pop_back(); return e; }
     cudaEvent_t e;
     cudaEventCreate(&e);
     return e;
@@ -46,7 +55,7 @@ void scao_prof_end(int slot, cudaStream_t st) {
     std::lock_guard<std::mutex> lk(g_mu);
     cudaEvent_t e = get_event();
     cudaEventRecord(e, st);
-    g_pending.push_back({slot, g_open[slot], e});
+    g_pending.push_back({slot, g_open[slot], e, cur_device()});
 }
 
 extern "C" int64_t scao_launch_count(void) { return g_launches.load(); }
@@ -61,8 +70,8 @@ extern "C" int scao_prof_read(double* ms, int64_t* counts, int nslots) {
         cudaEventElapsedTime(&t, p.a, p.b);
         g_ms[p.slot] += t;
         g_cnt[p.slot] += 1;
-        g_pool.push_back(p.a);
-        g_pool.push_back(p.b);
+        g_pool[p.dev].push_back(p.a);
+        g_pool[p.dev].push_back(p.b);
     }
     g_pending.clear();
     for (int i = 0; i < nslots && i < SLOT_COUNT; ++i) {
