@@ -43,10 +43,11 @@ def fused_kronecker_precond(U_l, s_l_inv4, U_r, s_r_inv4, G):
     L = _lib.lib()
     scratch = torch.empty(int(L.scao_fused_precond_scratch_bytes(m, n, k)), dtype=torch.uint8,
                           device=dev)
-    _lib.check(L.scao_fused_kronecker_precond(Ul.data_ptr(), sl.data_ptr(), Ur.data_ptr(),
-                                              sr.data_ptr(), Gc.data_ptr(), out.data_ptr(),
-                                              _CODE[G.dtype], m, n, k, scratch.data_ptr(),
-                                              _stream(dev)), "scao_fused_kronecker_precond")
+    with torch.cuda.device(dev):
+        _lib.check(L.scao_fused_kronecker_precond(Ul.data_ptr(), sl.data_ptr(), Ur.data_ptr(),
+                                                  sr.data_ptr(), Gc.data_ptr(), out.data_ptr(),
+                                                  _CODE[G.dtype], m, n, k, scratch.data_ptr(),
+                                                  _stream(dev)), "scao_fused_kronecker_precond")
     return out
 
 
@@ -61,10 +62,11 @@ def low_rank_precond_mm(U, s, G, left: bool = True):
     L = _lib.lib()
     scratch = torch.empty(int(L.scao_low_rank_precond_mm_scratch_bytes(m, n, k, int(left))),
                           dtype=torch.uint8, device=dev)
-    _lib.check(L.scao_low_rank_precond_mm(Uc.data_ptr(), sc.data_ptr(), Gc.data_ptr(),
-                                          out.data_ptr(), m, n, k, int(left),
-                                          scratch.data_ptr(), _stream(dev)),
-               "scao_low_rank_precond_mm")
+    with torch.cuda.device(dev):
+        _lib.check(L.scao_low_rank_precond_mm(Uc.data_ptr(), sc.data_ptr(), Gc.data_ptr(),
+                                              out.data_ptr(), m, n, k, int(left),
+                                              scratch.data_ptr(), _stream(dev)),
+                   "scao_low_rank_precond_mm")
     return out
 
 
@@ -81,7 +83,8 @@ def int8_ema_update(ema_q, ema_scale: float, new_val, rho: float):
     s_out = torch.empty(1, dtype=torch.float64, device=dev)
     L = _lib.lib()
     scratch = torch.empty(int(L.scao_int8_ema_scratch_bytes(n)), dtype=torch.uint8, device=dev)
-    _lib.check(L.scao_int8_ema_update(q.data_ptr(), float(ema_scale), nv.data_ptr(), float(rho),
-                                      n, q_out.data_ptr(), s_out.data_ptr(), scratch.data_ptr(),
-                                      _stream(dev)), "scao_int8_ema_update")
+    with torch.cuda.device(dev):
+        _lib.check(L.scao_int8_ema_update(q.data_ptr(), float(ema_scale), nv.data_ptr(), float(rho),
+                                          n, q_out.data_ptr(), s_out.data_ptr(), scratch.data_ptr(),
+                                          _stream(dev)), "scao_int8_ema_update")
     return q_out.view(ema_q.shape), float(s_out.item())

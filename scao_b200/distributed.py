@@ -465,7 +465,8 @@ def sync_preconditioners(optimizer, process_group=None):
         dist.all_reduce(t, group=process_group)
         t.div_(world)
     if plan.int8_ema:
-        _requant_average(plan, process_group, world)
+        with torch.cuda.device(plan.device):      # library launches on the plan's device
+            _requant_average(plan, process_group, world)
     else:
         dist.all_reduce(plan.fac, group=process_group)
         plan.fac.div_(world)

@@ -263,6 +263,11 @@ class SCAO(Optimizer):
             self._build_plan()
             if self._plan is None:
                 return loss
+        # the library launches on the current device: make it the plan's
+        with torch.cuda.device(self._plan.device):
+            return self._device_step(loss)
+
+    def _device_step(self, loss):
         plan = self._plan
         L = _lib.lib()
         if plan.step_event is not None:

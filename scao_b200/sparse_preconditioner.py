@@ -44,7 +44,10 @@ class SparsePreconditioner(PrecondView):
                      max_precond_dim=max_precond_dim)
         if p.device.type == "cuda":
             _lib.lib()
-        plan = Plan([p], [group], p.device, bool(use_int8_ema))
+            with torch.cuda.device(p.device):      # the plan launches on its device
+                plan = Plan([p], [group], p.device, bool(use_int8_ema))
+        else:
+            plan = Plan([p], [group], p.device, bool(use_int8_ema))
         super().__init__(plan, 0, group)
         self.epsilon_sparse = epsilon_sparse
         self.use_newton_schulz = use_newton_schulz
@@ -73,6 +76,10 @@ class SparsePreconditioner(PrecondView):
         """preconditioner.py:297-361: factor EMAs (int8 or fp32) and the eigen
         update of every Kronecker block, the diagonal EMA of the others."""
         self._cuda(grad)
+        with torch.cuda.device(self.device):
+            self._update_curvature(grad)
+
+    def _update_curvature(self, grad):
         plan = self.plan
         L = _lib.lib()
         # the kernels read the gradient in the parameter dtype
@@ -146,6 +153,10 @@ class SparsePreconditioner(PrecondView):
         """preconditioner.py:457-521: every block in float32, reassembled,
         returned in the gradient's dtype."""
         self._cuda(grad)
+        with torch.cuda.device(self.device):
+            return self._precondition(grad)
+
+    def _precondition(self, grad):
         g2 = self._grad2d(grad).to(torch.float32)
         if not self._views:                                 # diagonal parameter
             return self._diag_out(g2, self.diag_ema.reshape(self.m, self.n)) \
