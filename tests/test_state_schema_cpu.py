@@ -107,3 +107,64 @@ def test_reference_checkpoint_schema_matches_ours():
     for i in range(len(w.params)):
         ours = PrecondView(plan, i, g).state_dict()
         assert shape_only(d["state_dict"]["_scao_precond"][i]) == shape_only(ours), i
+
+
+def test_plan_tables_cover_random_shapes():
+    """The plan's tables for random parameter sets (remainders of width 1,
+    nested splits, 1-D and 3-D parameters): leaves and strips tile every
+    matrix exactly once, tiles tile every leaf, panels cover its rows, flat
+    chunks cover every parameter, arena offsets are 8-element aligned."""
+    import numpy as np
+    from scao_b200 import plan as P
+    rng = np.random.default_rng(3)
+    for trial in range(40):
+        mpd = int(rng.choice([16, 48, 64, 128]))
+        shapes = []
+        for _ in range(int(rng.integers(1, 5))):
+            kind = rng.integers(0, 4)
+            if kind == 0:
+                shapes.append((int(rng.integers(1, 300)),))
+            elif kind == 1:
+                shapes.append((int(mpd * rng.integers(1, 4) + rng.choice([0, 1, 7])),
+                               int(rng.integers(2, 3 * mpd))))
+            elif kind == 2:
+                shapes.append((int(rng.integers(2, 3 * mpd)),
+                               int(mpd * rng.integers(1, 4) + rng.choice([0, 1, 5]))))
+            else:
+                shapes.append((int(rng.integers(2, 20)), int(rng.integers(1, 6)),
+                               int(rng.integers(2, 9))))
+        g = dict(max_precond_dim=mpd, k_min=4, k_max=16, epsilon_sparse=0.05, rho=0.999)
+        params = [torch.zeros(s) for s in shapes]
+        try:
+            plan = Plan(params, [g] * len(params), torch.device("cpu"), True)
+        except NotImplementedError:
+            continue            # a split leaving no Kronecker block at all
+        for i, p in enumerate(params):
+            r = plan.ptab[i]
+            assert int(r["offset"]) % 8 == 0
+            n = p.numel()
+            cov = np.zeros(n, np.int32)
+            for c in plan.ctab[int(r["chunk_begin"]):int(r["chunk_end"])]:
+                cov[int(c["begin"]):int(c["end"])] += 1
+            assert (cov == 1).all(), (shapes[i], mpd)
+            if int(r["mode"]) != 1:
+                continue
+            m, ncol = P.to_2d_shape(tuple(p.shape))
+            cov = np.zeros(m * ncol, np.int32)
+            for li in plan.param_leaves[i]:
+                L = plan.ltab[li]
+                r0, c0, a, b = (int(L[k]) for k in ("row0", "col0", "a", "b"))
+                assert a > 1 and b > 1
+                for rr in range(r0, r0 + a):
+                    cov[rr * ncol + c0: rr * ncol + c0 + b] += 1
+                tcov = np.zeros((a, b), np.int32)
+                for t in plan.ttab[int(L["tile_begin"]):int(L["tile_end"])]:
+                    tr, tc = int(t["row0"]), int(t["col0"])
+                    tcov[tr:tr + P.TILE, tc:tc + P.TILE] += 1
+                assert (tcov == 1).all()
+                rows = sum(int(pn["nrows"]) for pn in plan.pantab[int(L["panel_begin"]):int(L["panel_end"])])
+                assert rows == a
+            for si in plan.param_strips[i]:
+                S = plan.stab[si]
+                cov[int(S["begin"]) + np.arange(int(S["count"])) * int(S["stride"])] += 1
+            assert (cov == 1).all(), (shapes[i], mpd)
