@@ -119,54 +119,77 @@ class ClockSampler:
 # reference (CPU) arm
 # ---------------------------------------------------------------------------
 
-def cpu_reference(workload, steps, warmup, sample_layers=1):
-    """Time the oracle's CPU restatement of the reference step on one
-    transformer layer (bounded sample) and scale to the full parameter set."""
-    from oracle.scao_oracle import OracleSCAO
+def reference_arm(workload, steps, warmup, device="cpu", layers=1):
+    """Time the reference package's own ``scao.SCAO.step()`` (the unmodified
+    install under baseline/_ref; its CUDA extension is not built, so on CUDA
+    tensors it runs its PyTorch fallback) on a bounded sample of the workload:
+    the embedding + final norm (Adam-only group) and ``layers`` transformer
+    layers, each sample its own optimizer with the workload's settings.  Both
+    are primed through the 20 Adam-warmup steps + ``warmup`` steps untimed,
+    then ``steps`` steps are timed (same global steps, hence the same
+    curvature cadence, as the GPU arm); a step of the full set is
+    t(embedding part) + (16 / layers) * t(layer sample)."""
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isfile(os.path.join(ref, "scao", "__init__.py")):
+        return None
+    if ref not in sys.path:
+        sys.path.insert(0, ref)
+    import warnings
+    warnings.filterwarnings("ignore", category=RuntimeWarning)
+    import scao  # the reference package
     from scao_b200 import synthetic, workloads
 
-    w_s = workloads.c4(n_layers=sample_layers)
-    w_s.params = [p for p in w_s.params if p.name not in ("embed", "final_norm")]
     threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
-    p0 = [p.float().numpy() for p in synthetic.init_params(w_s)]
-    kw = dict(w_s.scao_kwargs)
-    kw.update(warmup_steps=0, min_precond_updates=0)
-    opt = OracleSCAO(p0, dtype=w_s.param_dtype, threads=threads, **kw)
-    gen = synthetic.LowRankGradients(w_s)
-    grads = [g.float().numpy() for g in gen.next()]
-    pf = kw["precond_freq"]
-    t_reg, t_curv = [], []
-    total = steps + warmup
-    for i in range(total):
-        curv = (opt.global_step + 1) % pf == 0
-        t0 = time.perf_counter()
-        opt.step(grads)
-        dt = (time.perf_counter() - t0) * 1e3
-        if i >= warmup:
-            (t_curv if curv else t_reg).append(dt)
-    if not t_reg:
-        t_reg = [float("nan")]
-    reg = statistics.mean(t_reg)
-    # curvature step = regular step + update_curvature (EMA GEMMs + eigh per
-    # block) of every parameter; time the latter directly on the sample
-    if not t_curv:
-        def upd(i):
-            opt.state[i]["precond"].update_curvature(grads[i])
-        t0 = time.perf_counter()
-        if opt._pool is not None:
-            list(opt._pool.map(upd, range(len(grads))))
-        else:
-            for i in range(len(grads)):
-                upd(i)
-        t_curv = [reg + (time.perf_counter() - t0) * 1e3]
-    curv = statistics.mean(t_curv)
-    scale = workload.numel / w_s.numel
-    amort = ((pf - 1) * reg + curv) / pf * scale
-    sample = (f"{sample_layers} of 16 transformer layers ({w_s.numel / 1e6:.1f}M elems, "
-              f"{len(w_s.params)} params); regular step {reg:.0f} ms, curvature step "
-              f"{curv:.0f} ms on the sample; amortised ((pf-1)*reg+curv)/pf and scaled "
-              f"x{scale:.2f} by element count to the full {workload.numel / 1e9:.3f}B set")
-    return amort, threads, sample, reg * scale, curv * scale
+    if device == "cpu":
+        torch.set_num_threads(threads)
+    n_layers = sum(1 for p in workload.params if p.name.endswith(".Wq"))
+    w_l = workloads.c4(n_layers=layers)
+    w_l.params = [p for p in w_l.params if p.name not in ("embed", "final_norm")]
+    w_e = workloads.c4(n_layers=0)
+    samples = []
+    for w_s, groups_of in ((w_e, lambda ps: [{"params": ps, "warmup_steps": 10 ** 9}]),
+                           (w_l, lambda ps: ps)):
+        p0 = synthetic.init_params(w_s, device=device)
+        params = [torch.nn.Parameter(p) for p in p0]
+        opt = scao.SCAO(groups_of(params), **w_s.scao_kwargs)
+        gen = synthetic.LowRankGradients(w_s, device=device)
+        sets = [gen.next() for _ in range(3)]
+        samples.append((params, opt, sets))
+    pf = workload.scao_kwargs["precond_freq"]
+    n_prime = workload.scao_kwargs["warmup_steps"] + warmup
+
+    def one(k):
+        out = []
+        for params, opt, sets in samples:
+            for p, g in zip(params, sets[k % 3]):
+                p.grad = g
+            if device != "cpu":
+                torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            opt.step()
+            if device != "cpu":
+                torch.cuda.synchronize()
+            out.append((time.perf_counter() - t0) * 1e3)
+        return out
+
+    for k in range(n_prime):
+        one(k)
+    per, curv = [], []
+    scale = n_layers / layers
+    for k in range(steps):
+        te, tl = one(n_prime + k)
+        per.append(te + scale * tl)
+        curv.append((n_prime + k + 1) % pf == 0)
+    reg = [t for t, c in zip(per, curv) if not c]
+    cur = [t for t, c in zip(per, curv) if c]
+    sample = (f"reference scao.SCAO.step() on {device} tensors: the embedding + final norm "
+              f"(Adam-only group) and {layers} of {n_layers} transformer layers, each its own "
+              f"optimizer, primed {n_prime} steps, {steps} timed; per step "
+              f"t(embedding part) + {scale:g} x t(layer sample)")
+    return {"ms_per_step": statistics.mean(per), "cores": threads if device == "cpu" else None,
+            "sample": sample, "steps": steps, "warmup": warmup,
+            "regular_step_ms": statistics.mean(reg) if reg else None,
+            "curvature_step_ms": statistics.mean(cur) if cur else None}
 
 
 # ---------------------------------------------------------------------------
@@ -190,7 +213,16 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=16, help="debug: fewer layers")
     ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--nondegenerate-steps", type=int, default=30,
+                    help="after the timed region: steps with s0=1 gradients (factors off "
+                         "127*I, iterative eigensolve on every curvature step), timed apart")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gpu-fallback", action="store_true",
+                    help="--impl reference: skip timing the reference's PyTorch path on the GPU")
+    ap.add_argument("--grad-scale", type=float, default=None,
+                    help="leading singular value s0 of the synthetic gradients (default 1e-2, "
+                         "the benchmark configuration; 1.0 moves the int8 factors off 127*I so "
+                         "every curvature step runs the iterative eigensolver)")
     ap.add_argument("--json-out", default=None)
     ap.add_argument("--profile-range", action="store_true",
                     help="cudaProfilerStart/Stop around the timed steps (ncu --profile-from-start off)")
@@ -213,6 +245,8 @@ def main():
 
     from scao_b200 import workloads
     workload = workloads.c4(n_layers=a.layers)
+    if a.grad_scale is not None:
+        workload.grad_scale = a.grad_scale
     workload.scao_kwargs.update(sparsity=a.sparsity, noise_std_init=a.noise,
                                 dynamic_sparsity=a.dynamic_sparsity)
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -224,23 +258,42 @@ def main():
            "warmup_steps": 20, "blend_steps": 50, "grad_rank": workload.grad_rank,
            "l2": "inputs larger than L2 (2.1 GB grads, 16.6 GB fp32 state per step)",
            "sparsity": a.sparsity, "dynamic_sparsity": a.dynamic_sparsity,
-           "noise_std_init": a.noise}
+           "noise_std_init": a.noise, "grad_scale": workload.grad_scale}
 
     if a.impl == "reference":
         if rank != 0:
             return
-        amort, cores, sample, reg, curv = cpu_reference(workload, steps=2, warmup=1)
-        line = {"impl": "reference", "metric": METRIC, "value": round(amort, 3), "unit": UNIT,
+        r = reference_arm(workload, a.steps, a.warmup)
+        if r is not None:
+            kind, val, cores, sample = "reference", r["ms_per_step"], r["cores"], r["sample"]
+            extra = {"regular_step_ms": r["regular_step_ms"],
+                     "curvature_step_ms": r["curvature_step_ms"]}
+        else:
+            # reference package not installed: the oracle's numpy restatement
+            amort, cores, sample, reg, curv = cpu_reference(workload, steps=2, warmup=1)
+            kind, val = "port", amort
+            sample += " (2 timed steps after 1 warm-up step; reference package not installed)"
+            extra = {"regular_step_ms": reg, "curvature_step_ms": curv}
+        line = {"impl": "reference", "metric": METRIC, "value": round(val, 3), "unit": UNIT,
                 "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
-                "ms_per_step": round(amort, 3), "higher_is_better": False,
+                "ms_per_step": round(val, 3), "higher_is_better": False,
                 "scaling": "strong", "vs_baseline": None, "dtype": "f32",
                 "data": "synthetic", "config": cfg,
-                "cpu_baseline": {"value": round(amort, 3), "unit": UNIT, "cores": cores,
-                                 "kind": "port", "sample": sample,
-                                 "regular_step_ms": round(reg, 1),
-                                 "curvature_step_ms": round(curv, 1)},
-                "e2e": {"value": round(amort, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "cpu_baseline": {"value": round(val, 3), "unit": UNIT, "cores": cores,
+                                 "kind": kind, "sample": sample,
+                                 **{k: round(v, 1) for k, v in extra.items() if v is not None}},
+                "e2e": {"value": round(val, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
+        if r is not None and torch.cuda.is_available() and not a.no_gpu_fallback:
+            # the reference's own GPU path (PyTorch fallback + cuSOLVER eigh) on
+            # one B200, same sample rule: 10 steps after the warmup, one of them
+            # a curvature step
+            torch.cuda.set_device(local)
+            g = reference_arm(workload, 10, 0, device=f"cuda:{local}")
+            line["reference_gpu_fallback"] = {
+                "value": round(g["ms_per_step"], 3), "unit": UNIT, "sample": g["sample"],
+                "regular_step_ms": round(g["regular_step_ms"], 3),
+                "curvature_step_ms": round(g["curvature_step_ms"], 3)}
         print(json.dumps(line), flush=True)
         return
 
@@ -485,6 +538,15 @@ def main():
                  "note": "3 steps each after the timed region; compute-only steps include "
                          "curvature steps when the cadence lands on them"}
 
+    eig_slots = ("eig_prep", "eig_diag", "eig_gemm", "eig_jacobi", "eig_residual",
+                 "eig_cholinv", "eig_rank")
+    eig_ms = sum(prof.get(s_, (0.0, 0))[0] for s_ in eig_slots)
+    diag_path = all(prof.get(s_, (0.0, 0))[1] == 0 for s_ in ("eig_gemm", "eig_jacobi"))
+
+    nondeg = None
+    if world == 1 and a.nondegenerate_steps > 0 and workload.grad_scale < 0.5:
+        nondeg = nondegenerate_leg(a, opt, params, workload, dev, stream, L)
+
     if rank != 0:
         return
     line = {
@@ -509,6 +571,9 @@ def main():
                                         "achieved_gbs": round(achieved, 1),
                                         "frac": round(achieved / hbm, 4)}},
         "gemm_roofline": gemm,
+        "eigensolve_ms_per_curvature_step": round(eig_ms / n_curv, 3) if n_curv else None,
+        "eigensolve_diagonal_shortcut": bool(diag_path),
+        **({"nondegenerate": nondeg} if nondeg else {}),
         "kernels": kern,
         "gpu_launches": int(launches),
         **({"comm_compute_split": split} if split else {}),
@@ -517,13 +582,78 @@ def main():
     if e2e:
         line["e2e"] = e2e
     if world == 1 and not a.no_cpu_baseline:
-        amort, cores, sample, creg, ccurv = cpu_reference(workload, steps=2, warmup=1)
-        line["cpu_baseline"] = {"value": round(amort, 1), "unit": UNIT, "cores": cores,
-                                "kind": "port", "sample": sample}
+        # the reference package on the host cores: steps 21-30 (nine regular
+        # steps and one curvature step) after the 20 Adam-warmup steps
+        r = reference_arm(workload, 10, 0)
+        if r is not None:
+            line["cpu_baseline"] = {"value": round(r["ms_per_step"], 1), "unit": UNIT,
+                                    "cores": r["cores"], "kind": "reference",
+                                    "sample": r["sample"],
+                                    "regular_step_ms": round(r["regular_step_ms"], 1),
+                                    "curvature_step_ms": round(r["curvature_step_ms"], 1)}
+        else:
+            amort, cores, sample, creg, ccurv = cpu_reference(workload, steps=2, warmup=1)
+            line["cpu_baseline"] = {"value": round(amort, 1), "unit": UNIT, "cores": cores,
+                                    "kind": "port", "sample": sample}
     print(json.dumps(line), flush=True)
     if a.json_out:
         with open(a.json_out, "w") as f:
             json.dump(line, f, indent=1)
+
+
+def nondegenerate_leg(a, opt, params, workload, dev, stream, L):
+    """Continue the optimizer with s0 = 1 gradients (the int8 factors leave
+    127*I at the first curvature update, so every later curvature step runs
+    the iterative eigensolver on all 1024 / 512 factors) and time
+    ``--nondegenerate-steps`` steps with CUDA events; the eigensolve is timed
+    per curvature step from the library's kernel events."""
+    from scao_b200 import _lib, synthetic
+    gen = synthetic.LowRankGradients(workload, seed=1, device=dev, s0=1.0)
+    sets = [gen.next() for _ in range(3)]
+    pf = workload.scao_kwargs["precond_freq"]
+    # untimed up to and through one curvature step (leaves the 127*I regime)
+    k = 0
+    while True:
+        for p, g in zip(params, sets[k % 3]):
+            p.grad = g
+        opt.step()
+        k += 1
+        if opt._global_step % pf == 0:
+            break
+    torch.cuda.synchronize()
+    reg, curv, eig = [], [], []
+    eig_slots = ("eig_prep", "eig_diag", "eig_gemm", "eig_jacobi", "eig_residual",
+                 "eig_cholinv", "eig_rank")
+    for _ in range(a.nondegenerate_steps):
+        for p, g in zip(params, sets[k % 3]):
+            p.grad = g
+        k += 1
+        is_curv = (opt._global_step + 1) % pf == 0
+        L.scao_prof_reset()
+        L.scao_prof_enable(1)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        opt.step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        L.scao_prof_enable(0)
+        t = e0.elapsed_time(e1)
+        if is_curv:
+            curv.append(t)
+            pr = _lib.prof_read()
+            eig.append(sum(pr.get(s_, (0.0, 0))[0] for s_ in eig_slots))
+        else:
+            reg.append(t)
+    r = statistics.mean(reg) if reg else None
+    c = statistics.mean(curv) if curv else None
+    return {"grad_scale": 1.0, "steps": a.nondegenerate_steps,
+            "regular_step_ms": round(r, 3) if r else None,
+            "curvature_step_ms": [round(x, 3) for x in curv],
+            "eigensolve_ms": [round(x, 3) for x in eig],
+            "amortised_ms": round(((pf - 1) * r + c) / pf, 3) if (r and c) else None,
+            "note": "after the timed region: s0=1 gradients, first curvature step untimed; each "
+                    "step timed alone (CUDA events, synchronised), eigensolve = eig_* kernels"}
 
 
 def build_opt_list(workload, params_specs, scao_cls):

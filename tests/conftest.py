@@ -9,5 +9,3 @@ if ROOT not in sys.path:
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200, sm_100a)")
     config.addinivalue_line("markers", "slow: longer CPU test")
-    config.addinivalue_line("markers", "gpu_pending: GPU parity checks whose first B200 run "
-                            "is still to be recorded (run with -m gpu_pending)")

@@ -18,6 +18,7 @@ workload of ``scao_b200.workloads`` with gradients from
 from __future__ import annotations
 
 import argparse
+import copy
 import hashlib
 import os
 import sys
@@ -226,6 +227,13 @@ def ckpt_case(scao_mod, steps_before=12, steps_after=10):
                    for i, st in sd["state"].items()}
     torch.save({"state_dict": sd, "params": [p.detach().clone() for p in params]},
                os.path.join(HERE, "ckpt_tiny_f32.pt"))
+    # the reference itself resumes from its own (full) checkpoint: a fresh
+    # optimizer loads it, so state the checkpoint does not hold (the
+    # lookahead slow weights) starts afresh, as it does for any resumed run
+    full = copy.deepcopy(opt.state_dict())
+    params = [torch.nn.Parameter(p.detach().clone()) for p in params]
+    opt = scao_mod.SCAO(params, **w.scao_kwargs)
+    opt.load_state_dict(full)
     for t in range(steps_after):
         for p, g in zip(params, gen.next()):
             p.grad = g.clone()

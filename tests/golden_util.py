@@ -23,8 +23,8 @@ CASES = {
     "bf16_skip": ("bfloat16", 48, 30, 1.0, True),
 }
 
-# golden runs the oracle is pinned against whose GPU parity run is still to be
-# recorded (same fields as CASES)
+# golden runs with a GPU check of their own (tests/test_gpu_goldens_extra.py);
+# same fields as CASES
 ORACLE_ONLY = {
     "bf16_r1235": ("bfloat16", 48, 30, 1.0, True),
     "f32_groups": ("float32", 48, 30, 1.0, True),
@@ -119,3 +119,14 @@ def subspace_angle(U, U_ref, S_ref, rel_gap=1e-2):
     if j == 0:
         return 0.0
     return principal_angle(np.asarray(U)[:, :j], np.asarray(U_ref)[:, :j])
+
+
+def reference_root():
+    """Directory holding the reference's ``scao`` package, for the CPU checks
+    that import it: ``$SCAO_REFERENCE`` if set, else the offline install under
+    ``baseline/_ref`` of this checkout; None when neither holds it."""
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    for d in (os.environ.get("SCAO_REFERENCE"), os.path.join(repo, "baseline", "_ref")):
+        if d and os.path.isfile(os.path.join(d, "scao", "__init__.py")):
+            return d
+    return None

@@ -1,7 +1,4 @@
-"""GPU parity checks written against fixtures and the oracle whose first run on
-a B200 is still to be recorded.  They carry their own marker (``-m
-gpu_pending``), so ``-m gpu`` does not select them until they have run green,
-and they skip on hosts without CUDA.
+"""GPU parity checks beyond the core golden set:
 
 * the golden runs of ``ORACLE_ONLY`` (the oracle matches the reference on them
   on CPU): param groups, lookahead without LARS, k_max 128, the
@@ -20,7 +17,7 @@ from oracle import scao_oracle as O
 from scao_b200 import SCAO, synthetic, workloads
 from scao_b200.workloads import ParamSpec, Workload
 
-pytestmark = [pytest.mark.gpu_pending,
+pytestmark = [pytest.mark.gpu,
               pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA GPU")]
 
 DEV = "cuda:0"

@@ -5,7 +5,7 @@ import os
 import numpy as np
 import pytest
 
-from golden_util import CASES, EXTRA, ORACLE_ONLY, load, principal_angle, rel_err
+from golden_util import CASES, EXTRA, ORACLE_ONLY, load, principal_angle, rel_err, reference_root
 from oracle import scao_oracle as O
 from scao_b200 import synthetic, workloads
 
@@ -123,7 +123,7 @@ def test_quantile_matches_torch():
     assert np.isnan(O.quantile_f32(np.array([1, np.nan, 2], np.float32), 0.5))
 
 
-@pytest.mark.skipif(not os.path.isdir("/root/reference"), reason="reference checkout not present")
+@pytest.mark.skipif(reference_root() is None, reason="reference package not present")
 @pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
 def test_oracle_matches_reference_at_config_c1(dtype):
     """Benchmark configuration C1 at full size (4-layer d=256 GPT set, int8 EMA,
@@ -133,7 +133,7 @@ def test_oracle_matches_reference_at_config_c1(dtype):
     path with the oracle on this same run."""
     import sys
     import torch
-    sys.path.insert(0, "/root/reference")
+    sys.path.insert(0, reference_root())
     import scao
     w = workloads.c1()
     w.param_dtype = dtype

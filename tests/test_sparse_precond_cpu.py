@@ -10,7 +10,9 @@ import torch
 
 from scao_b200 import SparsePreconditioner
 
-REF = "/root/reference"
+from golden_util import reference_root  # noqa: E402
+
+REF = reference_root()
 SHAPES = [((64, 48), 4096), ((128, 16), 64), ((49, 40), 48), ((97, 97), 48), ((40,), 48),
           ((8, 4, 5), 4096)]
 
@@ -49,7 +51,7 @@ def _structure(d):
     return out
 
 
-@pytest.mark.skipif(not os.path.isdir(REF), reason="reference checkout not present")
+@pytest.mark.skipif(REF is None, reason="reference checkout not present")
 @pytest.mark.parametrize("int8", [True, False])
 @pytest.mark.parametrize("shape,mpd", SHAPES)
 def test_matches_reference_class(shape, mpd, int8):

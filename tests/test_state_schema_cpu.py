@@ -10,7 +10,9 @@ import torch
 from scao_b200.plan import Plan
 from scao_b200.preconditioner import PrecondView
 
-REF = "/root/reference"
+from golden_util import reference_root  # noqa: E402
+
+REF = reference_root()
 
 SHAPES = [((96, 128), 48), ((100, 30), 48), ((50, 7), 48), ((16,), 48), ((33, 200), 64),
           # width-1 remainders: diagonal sub-preconditioners inside the split
@@ -36,7 +38,7 @@ def _structure(d):
     return out
 
 
-@pytest.mark.skipif(not os.path.isdir(REF), reason="reference checkout not present")
+@pytest.mark.skipif(REF is None, reason="reference checkout not present")
 @pytest.mark.parametrize("int8", [True, False])
 @pytest.mark.parametrize("shape,mpd", SHAPES)
 def test_schema_matches_reference(shape, mpd, int8):

@@ -10,7 +10,9 @@ import torch
 import scao_b200
 from scao_b200 import utils
 
-REF = "/root/reference"
+from golden_util import reference_root  # noqa: E402
+
+REF = reference_root()
 
 
 def _spd(m, seed):
@@ -42,7 +44,7 @@ def test_exports():
         assert callable(getattr(scao_b200, name))
 
 
-@pytest.mark.skipif(not os.path.isdir(REF), reason="reference checkout not present")
+@pytest.mark.skipif(REF is None, reason="reference checkout not present")
 @pytest.mark.parametrize("ns", [False, True])
 @pytest.mark.parametrize("m", [4, 32])
 def test_neg_quarter_matches_reference(m, ns):
@@ -87,7 +89,7 @@ def test_average_norms_in_param_dtype():
         np.array([g.bfloat16().float().norm().item()], np.float32), ps[:1])[0])
 
 
-@pytest.mark.skipif(not os.path.isdir(REF), reason="reference checkout not present")
+@pytest.mark.skipif(REF is None, reason="reference checkout not present")
 def test_host_policies_match_reference_classes():
     """R1 warmup scheduler and R3 lazy trigger (optimizer.py:104-214): the
     host classes against the reference's own on random norm sequences
@@ -121,7 +123,7 @@ def test_host_policies_match_reference_classes():
         assert [c.should_update(float(v)) for v in x] == [d.should_update(float(v)) for v in x]
 
 
-@pytest.mark.skipif(not os.path.isdir(REF), reason="reference checkout not present")
+@pytest.mark.skipif(REF is None, reason="reference checkout not present")
 @pytest.mark.parametrize("name", ["scao_sub1b", "scao_1b", "scao_3b", "scao_7b", "scao_40b",
                                   "scao_125b"])
 def test_presets_configure_like_reference(name):
@@ -141,7 +143,7 @@ def test_presets_configure_like_reference(name):
         assert getattr(ref, attr) == getattr(ours, attr), attr
 
 
-@pytest.mark.skipif(not os.path.isdir(REF), reason="reference checkout not present")
+@pytest.mark.skipif(REF is None, reason="reference checkout not present")
 def test_constructor_defaults_and_errors_match_reference():
     """optimizer.py:258-304: same defaults in every param group, same
     attributes of the extensions, same ValueError cases."""
@@ -163,7 +165,7 @@ def test_constructor_defaults_and_errors_match_reference():
             scao_b200.SCAO(mk(), **bad)
 
 
-@pytest.mark.skipif(not os.path.isdir(REF), reason="reference checkout not present")
+@pytest.mark.skipif(REF is None, reason="reference checkout not present")
 def test_state_dict_top_level_schema_matches_reference():
     """optimizer.py:732-756: same top-level keys, runtime keys and group keys."""
     sys.path.insert(0, REF)
