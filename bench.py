@@ -539,7 +539,7 @@ def main():
                          "curvature steps when the cadence lands on them"}
 
     eig_slots = ("eig_prep", "eig_diag", "eig_gemm", "eig_jacobi", "eig_residual",
-                 "eig_cholinv", "eig_rank")
+                 "eig_cholinv", "eig_rank", "eig_iter")
     eig_ms = sum(prof.get(s_, (0.0, 0))[0] for s_ in eig_slots)
     diag_path = all(prof.get(s_, (0.0, 0))[1] == 0 for s_ in ("eig_gemm", "eig_jacobi"))
 
@@ -623,7 +623,8 @@ def nondegenerate_leg(a, opt, params, workload, dev, stream, L):
     torch.cuda.synchronize()
     reg, curv, eig = [], [], []
     eig_slots = ("eig_prep", "eig_diag", "eig_gemm", "eig_jacobi", "eig_residual",
-                 "eig_cholinv", "eig_rank")
+                 "eig_cholinv", "eig_rank", "eig_iter")
+    last_split = {}
     for _ in range(a.nondegenerate_steps):
         for p, g in zip(params, sets[k % 3]):
             p.grad = g
@@ -643,6 +644,13 @@ def nondegenerate_leg(a, opt, params, workload, dev, stream, L):
             curv.append(t)
             pr = _lib.prof_read()
             eig.append(sum(pr.get(s_, (0.0, 0))[0] for s_ in eig_slots))
+            last_split = {s_: round(pr[s_][0], 3) for s_ in eig_slots if s_ in pr}
+            st = getattr(opt, "_last_eig_status", None)
+            if st is not None:
+                its = st.cpu().numpy()
+                last_split["iterations_max"] = int(abs(its).max()) if its.size else 0
+                last_split["iterations_mean"] = round(float(abs(its).mean()), 2) if its.size else 0
+                last_split["capped"] = int((its < 0).sum())
         else:
             reg.append(t)
     r = statistics.mean(reg) if reg else None
@@ -651,6 +659,7 @@ def nondegenerate_leg(a, opt, params, workload, dev, stream, L):
             "regular_step_ms": round(r, 3) if r else None,
             "curvature_step_ms": [round(x, 3) for x in curv],
             "eigensolve_ms": [round(x, 3) for x in eig],
+            "eigensolve_last_split_ms": last_split,
             "amortised_ms": round(((pf - 1) * r + c) / pf, 3) if (r and c) else None,
             "note": "after the timed region: s0=1 gradients, first curvature step untimed; each "
                     "step timed alone (CUDA events, synchronised), eigensolve = eig_* kernels"}

@@ -337,14 +337,21 @@ SCAO_API int scao_plan_tensor_maps(const ScaoPlanDev* plan_host, const ScaoParam
 SCAO_API int scao_plan_grad_norms(const ScaoPlanDev* plan_host, float* out, void* stream);
 
 /* Eigen update of the listed leaves (preconditioner.py:363-451):
- * debias, Tikhonov eps = max(1e-8, 1e-4 tr/m), top-kmax eigenpairs by
- * warm-started subspace iteration with Rayleigh-Ritz (Jacobi) -- no
- * cuSOLVER -- and rank selection (utils.py:121-151 + hysteresis :437-441).
+ * debias, Tikhonov eps = max(1e-8, 1e-4 tr/m), the top eigenpairs by
+ * warm-started Chebyshev-filtered subspace iteration with Rayleigh-Ritz
+ * (Jacobi) on the tensor cores -- no cuSOLVER -- and rank selection
+ * (utils.py:121-151 + hysteresis :437-441).
  * bias_factor, eps_sparse: per leaf (device float arrays indexed by leaf).
+ * max_iters: cap on outer iterations (each: Rayleigh-Ritz + one filter).
+ * tol: a leading block of Ritz vectors that ends at a relative spectral gap
+ * of 1e-2 is accepted when its residual norm is <= tol * gap (subspace
+ * angle <~ tol rad); every usable pair also needs residual <= 1e-3 * theta_1.
  * nmax / smax: largest factor size / subspace width among the listed leaves
  * (nmax <= 4096, smax <= 160).  status (device, 2*n_ids ints, may be NULL):
  * iterations used per factor problem, negative when the cap was reached.
- * Workspaces are the plan's eig_* arenas.                                   */
+ * The iteration runs as a cached CUDA graph (conditional WHILE node): the
+ * host does not wait for the device.  Workspaces are the plan's eig_*
+ * arenas.                                                                   */
 SCAO_API int scao_plan_eigen(const ScaoPlanDev* plan_host, const int32_t* leaf_ids,
                     int n_ids, const float* bias_factor,
                     const float* eps_sparse, int max_iters, float tol,

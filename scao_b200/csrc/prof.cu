@@ -11,10 +11,11 @@ const char* kNames[SLOT_COUNT] = {
     "proj", "diag_pre", "leaf_coef", "param_pre", "apply_kron", "apply_flat", "param_post",
     "global_norm", "apply_p", "lookahead", "gram_ema", "requant", "diag_ema", "eig_prep",
     "eig_diag", "eig_gemm", "eig_jacobi", "eig_residual", "eig_cholinv", "eig_rank", "quant",
-    "seam", "gram_tc", "transpose", "filter"};
+    "seam", "gram_tc", "transpose", "filter", "eig_iter"};
 
 std::atomic<int64_t> g_launches{0};
 std::atomic<int> g_enabled{0};
+thread_local int g_suspended = 0;
 std::mutex g_mu;
 struct Pending { int slot; cudaEvent_t a, b; int dev; };
 std::vector<Pending> g_pending;
@@ -41,7 +42,12 @@ cudaEvent_t get_event() {
 
 }  // namespace
 
+void scao_prof_suspend(int on) { g_suspended = on; }
+
+void scao_prof_add_launches(int64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
 void scao_prof_begin(int slot, cudaStream_t st) {
+    if (g_suspended) return;
     g_launches.fetch_add(1, std::memory_order_relaxed);
     if (!g_enabled.load(std::memory_order_relaxed)) return;
     std::lock_guard<std::mutex> lk(g_mu);
@@ -51,7 +57,7 @@ void scao_prof_begin(int slot, cudaStream_t st) {
 }
 
 void scao_prof_end(int slot, cudaStream_t st) {
-    if (!g_enabled.load(std::memory_order_relaxed)) return;
+    if (g_suspended || !g_enabled.load(std::memory_order_relaxed)) return;
     std::lock_guard<std::mutex> lk(g_mu);
     cudaEvent_t e = get_event();
     cudaEventRecord(e, st);

@@ -314,6 +314,18 @@ class Plan:
                 ctypes.byref(self.dev), ids.data_ptr(), self.n_leaves,
                 torch.cuda.current_stream(dev).cuda_stream), "scao_plan_prep_factors")
 
+    def prep_leaves(self, leaf_ids):
+        """Rebuild the eigenvector operand tiles of the listed leaves (after
+        their U / S were written from the host, e.g. by a checkpoint load)."""
+        if not len(leaf_ids) or self.device.type != "cuda":
+            return
+        import ctypes
+        ids = torch.tensor(list(leaf_ids), dtype=torch.int32, device=self.device)
+        _lib.check(_lib.lib().scao_plan_prep_factors(
+            ctypes.byref(self.dev), ids.data_ptr(), len(leaf_ids),
+            torch.cuda.current_stream(self.device).cuda_stream), "scao_plan_prep_factors")
+        torch.cuda.current_stream(self.device).synchronize()
+
     def _init_factors(self):
         """L = R = 1e-4*I (int8: q = 127*I, absmax = float32(1e-4)), U = reversed
         identity (warm start; unused until the first eigen update), S = 1 for

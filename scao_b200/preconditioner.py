@@ -118,11 +118,37 @@ class LeafView:
             self._fac(0).copy_(st["L_ema"])
             self._fac(1).copy_(st["R_ema"])
         for side, uk, sk in ((0, "U_l", "S_l"), (1, "U_r", "S_r")):
-            U = st[uk].to(device=self.plan.device, dtype=torch.float32)
             S = st[sk].to(device=self.plan.device, dtype=torch.float32)
-            kk = U.shape[1]
-            self._u(side, kk).copy_(U)
-            self._s(side, kk).copy_(S)
+            self._u_full(side).copy_(self._complete_basis(st[uk], side))
+            self._s(side, S.shape[0]).copy_(S)
+
+    def _u_full(self, side):
+        L = self.plan.ltab[self.li]
+        n = self.m if side == 0 else self.n
+        s = int(L["sl"] if side == 0 else L["sr"])
+        o = int(L["ul_off"] if side == 0 else L["ur_off"])
+        return self.plan.u[o:o + n * s].view(n, s)
+
+    def _complete_basis(self, U, side):
+        """The stored top-k eigenvectors as the first k columns of an
+        orthonormal n x s basis (the eigensolver's warm start must be
+        orthonormal: the direct solve (s = n) and the first Rayleigh-Ritz step
+        read it as such).  Householder QR of [U, I] in float64 on the host: the
+        first k columns of Q are +-U, the rest are orthogonal to it."""
+        n = self.m if side == 0 else self.n
+        s = int(self.plan.ltab[self.li]["sl" if side == 0 else "sr"])
+        U = U.detach().to("cpu", torch.float64)
+        k = U.shape[1]
+        if k >= s:
+            return U[:, :s].to(torch.float32)
+        Q, R = torch.linalg.qr(torch.cat([U, torch.eye(n, dtype=torch.float64)], 1),
+                               mode="reduced")
+        Q = Q[:, :s].clone()
+        sg = torch.sign(torch.diagonal(R)[:k])
+        sg[sg == 0] = 1.0
+        Q[:, :k] *= sg
+        Q[:, :k] = U                   # bit-exact stored columns
+        return Q.to(torch.float32)
 
 
 class StripView:
@@ -351,5 +377,7 @@ class PrecondView:
         self.precond_step = int(st["precond_step"])
         if self.use_block_diagonal or self.use_kronecker:
             self._tree_load(self.plan.param_trees[self.pi], st, iter(self._views))
+            # the apply reads the eigenvectors through their bf16 operand tiles
+            self.plan.prep_leaves(self.plan.param_leaves[self.pi])
         else:
             self.diag_ema.copy_(st["diag_ema"])
