@@ -344,8 +344,9 @@ SCAO_API int scao_plan_grad_norms(const ScaoPlanDev* plan_host, float* out, void
  * bias_factor, eps_sparse: per leaf (device float arrays indexed by leaf).
  * max_iters: cap on outer iterations (each: Rayleigh-Ritz + one filter).
  * tol: a leading block of Ritz vectors that ends at a relative spectral gap
- * of 1e-2 is accepted when its residual norm is <= tol * gap (subspace
- * angle <~ tol rad); every usable pair also needs residual <= 1e-3 * theta_1.
+ * of 1e-2 is accepted when its largest residual norm is <= tol * gap
+ * (subspace angle <~ tol rad); every usable pair also needs residual <=
+ * 1e-3 * theta_1, except pairs in the flat bulk at the bottom of the block.
  * nmax / smax: largest factor size / subspace width among the listed leaves
  * (nmax <= 4096, smax <= 160).  status (device, 2*n_ids ints, may be NULL):
  * iterations used per factor problem, negative when the cap was reached.

@@ -53,7 +53,7 @@ constexpr float VAL_TOL = 1e-3f;    // per-pair residual bound (relative to thet
 constexpr float GAP_REL = 1e-2f;    // a spectral gap this large (relative) ends a prefix
 
 enum { AUX_SCALE = 0, AUX_BIAS, AUX_EPS, AUX_TOTAL, AUX_FLAGS, AUX_ITERS, AUX_RES,
-       AUX_CC, AUX_CE, AUX_CS, AUX_NFAIL, AUX_DEG };
+       AUX_CC, AUX_CE, AUX_CS, AUX_NFAIL, AUX_DEG, AUX_WARM };
 enum { F_DIAG = 1, F_UNIFORM = 2, F_CONV = 4, F_CHOLFAIL = 8, F_DIRECT = 16 };
 enum { BUF_U = 0, BUF_Y, BUF_X, BUF_AX, BUF_H, BUF_V, BUF_FAC };
 enum { DIM_N = 0, DIM_S = 1 };
@@ -251,6 +251,52 @@ __global__ void eig_diag_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids) 
     if (threadIdx.x == 0) {
         p.aux[AUX_FLAGS] = __int_as_float(flags_of(p) | F_CONV);
         p.aux[AUX_ITERS] = __int_as_float(0);
+        p.aux[AUX_WARM] = 0.f;      // U is a unit-vector basis: not a warm start
+    }
+}
+
+// ---------------------------------------------------------------------------
+// cold start: a problem whose U is not the result of an earlier iterative
+// solve (the initial reversed identity, or the unit-vector basis of the
+// diagonal shortcut) starts from a dense orthonormal basis instead.  Unit
+// vectors can span an exactly invariant subspace of A (rows the gradient
+// signal never reached), which subspace iteration would never leave.  The
+// basis: orthonormal DCT-II columns (frequencies 0..s-1) with the rows
+// permuted by i -> (a i + b) mod n and random signs -- still orthonormal,
+// dense, and in general position.
+// ---------------------------------------------------------------------------
+SCAO_DEV uint32_t mix32(uint32_t x) {
+    x ^= x >> 16; x *= 0x7feb352dU; x ^= x >> 15; x *= 0x846ca68bU; x ^= x >> 16;
+    return x;
+}
+
+__global__ void eig_cold_start_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids) {
+    const PInfo p = pinfo(P, ids, blockIdx.y);
+    const int fl = flags_of(p);
+    if ((fl & (F_DIAG | F_DIRECT)) || p.aux[AUX_WARM] != 0.f) return;
+    const int n = p.n, s = p.s;
+    const uint32_t key = mix32(0x9e3779b9U * (uint32_t)(2 * p.leaf + p.side + 1));
+    uint32_t a = (mix32(key) % (uint32_t)n) | 1u;
+    // a coprime to n (n >= 2): step a up until gcd(a, n) == 1
+    for (;;) {
+        uint32_t x = a, y = (uint32_t)n;
+        while (y) { const uint32_t t = x % y; x = y; y = t; }
+        if (x == 1u) break;
+        a = (a + 2u) % (uint32_t)n;
+        if (a == 0u) a = 1u;
+    }
+    const uint32_t b = mix32(key ^ 0x5bd1e995U) % (uint32_t)n;
+    float* U = P.u + p.uoff;
+    const float c0 = rsqrtf((float)n), c1 = sqrtf(2.f / (float)n);
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < (int64_t)n * s;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        const int i = (int)(e / s), f = (int)(e % s);
+        const uint32_t r = (uint32_t)(((uint64_t)a * (uint32_t)i + b) % (uint32_t)n);
+        // cos(pi (r + 1/2) f / n) = cospi(((2r + 1) f mod 4n) / 2n)
+        const uint32_t m = (uint32_t)(((uint64_t)(2u * r + 1u) * (uint32_t)f) % (4u * (uint32_t)n));
+        const float v = (f == 0 ? c0 : c1) * cospif((float)m / (float)(2 * n));
+        const float sg = (mix32(key + (uint32_t)i) & 1u) ? -1.f : 1.f;
+        U[e] = sg * v;
     }
 }
 
@@ -717,23 +763,28 @@ __global__ void eig_residual_kernel(ScaoPlanDev P, const int32_t* __restrict__ i
         if (lane == 0) rr[c] = sqrtf(r2);
     }
     __syncthreads();
-    // Convergence (pairs above the bulk only):
-    //  * every pair: r_j <= VAL_TOL * theta_1 (Ritz values accurate to ~r^2/gap)
-    //  * every prefix 0..j that ends at a gap theta_j - theta_{j+1} >= GAP_REL *
-    //    theta_1: ||r_0..j|| <= tol * gap, so the prefix subspace is within
-    //    ~tol rad of the exact one (Davis-Kahan sin(theta) bound)
+    // Convergence.  From the third outer iteration on, a pair within
+    // CLUSTER_FRAC of theta_s whose residual is below CLUSTER_FRAC * theta_s
+    // lies in the flat bulk (exempt).  Every
+    // other usable pair needs
+    //  * r_j <= VAL_TOL * theta_1 (Ritz values accurate to ~r^2 / gap), and
+    //  * for every prefix 0..j that ends at a gap theta_j - theta_{j+1} >=
+    //    GAP_REL * theta_1: max_{i<=j} r_i <= tol * gap, so the prefix subspace
+    //    is within ~tol rad of the exact one (Davis-Kahan sin(theta) bound).
     const int fl = flags_of(p);
     float rmax = 0.f;
     if (threadIdx.x == 0) {
         bool ok = true;
-        double r2 = 0.0;
         for (int j = 0; j < kc; ++j) {
-            if (ev[j] <= bulk) break;
-            r2 += (double)rr[j] * rr[j];
-            rmax = fmaxf(rmax, rr[j]);
-            if (rr[j] > VAL_TOL * scale) { ok = false; break; }
+            // (not before the third outer iteration: the Ritz values of an
+            // unfiltered block can all sit within CLUSTER_FRAC of each other)
+            const bool exempt = it >= 2 && ev[j] <= bulk && rr[j] <= CLUSTER_FRAC * fabsf(ths);
+            if (!exempt) {
+                rmax = fmaxf(rmax, rr[j]);
+                if (rr[j] > VAL_TOL * scale) { ok = false; break; }
+            }
             const float gap = (j + 1 < s) ? ev[j] - ev[j + 1] : 0.f;
-            if (gap >= GAP_REL * scale && sqrt(r2) > (double)tol * gap) { ok = false; break; }
+            if (gap >= GAP_REL * scale && rmax > tol * gap) { ok = false; break; }
         }
         sconv = ok;
         red[0] = rmax;
@@ -767,6 +818,7 @@ __global__ void eig_residual_kernel(ScaoPlanDev P, const int32_t* __restrict__ i
     if (threadIdx.x == 0) {
         int f = fl & ~F_CHOLFAIL;
         if (conv) f |= F_CONV;
+        if (conv) p.aux[AUX_WARM] = 1.f;
         p.aux[AUX_FLAGS] = __int_as_float(f);
         p.aux[AUX_ITERS] = __int_as_float(it + 1);
         p.aux[AUX_RES] = rmax / scale;
@@ -1069,6 +1121,8 @@ extern "C" int scao_plan_eigen(const ScaoPlanDev* P, const int32_t* leaf_ids, in
     SCAO_CHECK_LAUNCH();
     const size_t dsm = 4096 * 8;
     { ProfScope _ps(SLOT_EIG_DIAG, st); eig_diag_kernel<<<np, NT, dsm, st>>>(*P, leaf_ids); }
+    SCAO_CHECK_LAUNCH();
+    { ProfScope _ps(SLOT_EIG_DIAG, st); eig_cold_start_kernel<<<dim3(16, np), NT, 0, st>>>(*P, leaf_ids); }
     SCAO_CHECK_LAUNCH();
     static PerDeviceOnce attr_done;
     if (attr_done.first()) {

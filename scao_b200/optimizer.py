@@ -129,7 +129,7 @@ class SCAO(Optimizer):
         gsnr_threshold: float = 0.5,
         adaptive_rank: bool = False,
         eig_max_iters: int = 30,
-        eig_tol: float = 1e-4,
+        eig_tol: float = 5e-4,
     ) -> None:
         # optimizer.py:297-304
         if lr < 0:

@@ -27,7 +27,7 @@ from .plan import Plan
 from .preconditioner import LeafView, PrecondView, StripView
 
 _EIG_MAX_ITERS = 30      # the optimizer's defaults (SCAO(eig_max_iters, eig_tol))
-_EIG_TOL = 1e-4
+_EIG_TOL = 5e-4
 
 
 class SparsePreconditioner(PrecondView):
