@@ -256,7 +256,8 @@ __global__ void eig_diag_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids) 
 }
 
 // ---------------------------------------------------------------------------
-// cold start: a problem whose U is not the result of an earlier iterative
+// start basis.  Direct problems (s >= n) use the reversed identity.  A problem whose
+// U is not the result of an earlier iterative
 // solve (the initial reversed identity, or the unit-vector basis of the
 // diagonal shortcut) starts from a dense orthonormal basis instead.  Unit
 // vectors can span an exactly invariant subspace of A (rows the gradient
@@ -273,8 +274,21 @@ SCAO_DEV uint32_t mix32(uint32_t x) {
 __global__ void eig_cold_start_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids) {
     const PInfo p = pinfo(P, ids, blockIdx.y);
     const int fl = flags_of(p);
-    if ((fl & (F_DIAG | F_DIRECT)) || p.aux[AUX_WARM] != 0.f) return;
+    if (fl & F_DIAG) return;
     const int n = p.n, s = p.s;
+    if (fl & F_DIRECT) {
+        // direct solve (s >= n): the basis is the reversed identity, so the
+        // Rayleigh-Ritz matrix is A with its index order reversed, formed
+        // exactly (products with 1 and 0); with the Jacobi solver's tie rule
+        // (lower index first) near-degenerate eigenvalues come out in LAPACK's
+        // order (ascending index after the descending flip)
+        float* U = P.u + p.uoff;
+        for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < (int64_t)n * s;
+             e += (int64_t)gridDim.x * blockDim.x)
+            U[e] = ((int)(e / s) == n - 1 - (int)(e % s)) ? 1.f : 0.f;
+        return;
+    }
+    if (p.aux[AUX_WARM] != 0.f) return;
     const uint32_t key = mix32(0x9e3779b9U * (uint32_t)(2 * p.leaf + p.side + 1));
     uint32_t a = (mix32(key) % (uint32_t)n) | 1u;
     // a coprime to n (n >= 2): step a up until gcd(a, n) == 1
@@ -656,7 +670,9 @@ eig_jacobi_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, int max_sweeps
         }
         off = block_sum(off, red);
         fro = block_sum(fro, red);
-        if (off <= 1e-14f * fro || fro == 0.f) break;
+        // relative off-diagonal Frobenius norm <= 1e-6: Ritz values then
+        // carry errors of order 1e-12 relative, vectors 1e-6 (fp32 level)
+        if (off <= 1e-12f * fro || fro == 0.f) break;
         for (int round = 0; round < se - 1; ++round) {
             // round-robin tournament pairing of se players
             for (int t = threadIdx.x; t < half; t += blockDim.x) {
