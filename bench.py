@@ -24,6 +24,7 @@ parameter set by element count.
 from __future__ import annotations
 
 import argparse
+import re
 import json
 import os
 import statistics
@@ -40,6 +41,12 @@ import torch  # noqa: E402
 METRIC = "SCAO optimizer step ms (Llama-1B shapes)"
 UNIT = "ms"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def metric_for(workload):
+    if workload.name.startswith("llama-1b"):
+        return METRIC
+    return f"SCAO optimizer step ms ({workload.name} shapes)"
 
 
 def peaks():
@@ -119,6 +126,25 @@ class ClockSampler:
 # reference (CPU) arm
 # ---------------------------------------------------------------------------
 
+def _layer_of(name):
+    m = re.match(r"^[hl](\d+)\.", name)
+    return int(m.group(1)) if m else None
+
+
+def sample_split(workload, layers):
+    """(the non-layer parameters, the first ``layers`` transformer layers,
+    the workload's layer count) as two workloads with its settings."""
+    import copy
+    n_layers = 1 + max((_layer_of(p.name) for p in workload.params
+                        if _layer_of(p.name) is not None), default=-1)
+    w_e = copy.copy(workload)
+    w_e.params = [p for p in workload.params if _layer_of(p.name) is None]
+    w_l = copy.copy(workload)
+    w_l.params = [p for p in workload.params
+                  if _layer_of(p.name) is not None and _layer_of(p.name) < layers]
+    return w_e, w_l, n_layers
+
+
 def reference_arm(workload, steps, warmup, device="cpu", layers=1):
     """Time the reference package's own ``scao.SCAO.step()`` (the unmodified
     install under baseline/_ref; its CUDA extension is not built, so on CUDA
@@ -142,16 +168,12 @@ def reference_arm(workload, steps, warmup, device="cpu", layers=1):
     threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
     if device == "cpu":
         torch.set_num_threads(threads)
-    n_layers = sum(1 for p in workload.params if p.name.endswith(".Wq"))
-    w_l = workloads.c4(n_layers=layers)
-    w_l.params = [p for p in w_l.params if p.name not in ("embed", "final_norm")]
-    w_e = workloads.c4(n_layers=0)
+    w_e, w_l, n_layers = sample_split(workload, layers)
     samples = []
-    for w_s, groups_of in ((w_e, lambda ps: [{"params": ps, "warmup_steps": 10 ** 9}]),
-                           (w_l, lambda ps: ps)):
+    for w_s in (w_e, w_l):
         p0 = synthetic.init_params(w_s, device=device)
         params = [torch.nn.Parameter(p) for p in p0]
-        opt = scao.SCAO(groups_of(params), **w_s.scao_kwargs)
+        opt = build_opt(w_s, params, scao.SCAO)
         gen = synthetic.LowRankGradients(w_s, device=device)
         sets = [gen.next() for _ in range(3)]
         samples.append((params, opt, sets))
@@ -182,8 +204,8 @@ def reference_arm(workload, steps, warmup, device="cpu", layers=1):
         curv.append((n_prime + k + 1) % pf == 0)
     reg = [t for t, c in zip(per, curv) if not c]
     cur = [t for t, c in zip(per, curv) if c]
-    sample = (f"reference scao.SCAO.step() on {device} tensors: the embedding + final norm "
-              f"(Adam-only group) and {layers} of {n_layers} transformer layers, each its own "
+    sample = (f"reference scao.SCAO.step() on {device} tensors: the non-layer parameters "
+              f"(embedding in its Adam-only group) and {layers} of {n_layers} transformer layers, each its own "
               f"optimizer, primed {n_prime} steps, {steps} timed; per step "
               f"t(embedding part) + {scale:g} x t(layer sample)")
     return {"ms_per_step": statistics.mean(per), "cores": threads if device == "cpu" else None,
@@ -197,7 +219,8 @@ def reference_arm(workload, steps, warmup, device="cpu", layers=1):
 # ---------------------------------------------------------------------------
 
 def build_opt(workload, params, scao_cls, **extra):
-    groups = [{"params": [p for p, s in zip(params, workload.params) if not s.adam_only]}]
+    main = [p for p, s in zip(params, workload.params) if not s.adam_only]
+    groups = [{"params": main}] if main else []
     adam = [p for p, s in zip(params, workload.params) if s.adam_only]
     if adam:
         # Adam-only (Phase-1-forever) group: warmup_steps beyond any run
@@ -211,7 +234,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--layers", type=int, default=16, help="debug: fewer layers")
+    ap.add_argument("--layers", type=int, default=None, help="fewer transformer layers (small cases)")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--nondegenerate-steps", type=int, default=30,
                     help="after the timed region: steps with s0=1 gradients (factors off "
@@ -235,16 +258,24 @@ def main():
                     help="N>1: reduce-scatter / step / all-gather pipeline buckets")
     ap.add_argument("--sm-reserve", type=int, default=32,
                     help="N>1: SMs the persistent kernels leave to the collectives")
-    ap.add_argument("--workload", default="llama-1b", choices=["llama-1b", "gpt2m-train"],
-                    help="gpt2m-train: the GPT-2-medium data-parallel training step "
-                         "(benchmark configuration C3) instead of the headline optimizer step")
+    ap.add_argument("--workload", default="llama-1b",
+                    choices=["llama-1b", "qwen2.5-3b", "gpt2-small", "gpt2m-train"],
+                    help="llama-1b: the headline optimizer step (configuration C4); "
+                         "qwen2.5-3b: C5 (per-GPU peak HBM and the eigensolve step reported); "
+                         "gpt2-small: C2 (fp32 parameters); gpt2m-train: the GPT-2-medium "
+                         "data-parallel training step (C3)")
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3)
     if a.workload == "gpt2m-train":
         return gpt2_train_bench(a)
 
     from scao_b200 import workloads
-    workload = workloads.c4(n_layers=a.layers)
+    if a.workload == "qwen2.5-3b":
+        workload = workloads.c5(n_layers=a.layers or 36)
+    elif a.workload == "gpt2-small":
+        workload = workloads.c2(n_layers=a.layers or 12)
+    else:
+        workload = workloads.c4(n_layers=a.layers or 16)
     if a.grad_scale is not None:
         workload.grad_scale = a.grad_scale
     workload.scao_kwargs.update(sparsity=a.sparsity, noise_std_init=a.noise,
@@ -252,11 +283,17 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    kw = workload.scao_kwargs
+    gbytes = sum(int(np.prod(p.shape)) for p in workload.params) * \
+        (2 if workload.param_dtype != "float32" else 4)
     cfg = {"workload": workload.name, "params": workload.numel,
            "param_dtype": workload.param_dtype, "state_dtype": "float32",
-           "int8_ema": True, "max_precond_dim": 1024, "k_max": 64, "precond_freq": 10,
-           "warmup_steps": 20, "blend_steps": 50, "grad_rank": workload.grad_rank,
-           "l2": "inputs larger than L2 (2.1 GB grads, 16.6 GB fp32 state per step)",
+           "int8_ema": kw["use_int8_ema"], "max_precond_dim": kw.get("max_precond_dim", 4096),
+           "k_max": kw["k_max"], "precond_freq": kw["precond_freq"],
+           "warmup_steps": kw["warmup_steps"], "blend_steps": kw["blend_steps"],
+           "grad_rank": workload.grad_rank,
+           "l2": f"inputs larger than L2 ({gbytes / 1e9:.2f} GB of gradients, "
+                 f"{16 * workload.numel / 1e9:.1f} GB of fp32 state per step)",
            "sparsity": a.sparsity, "dynamic_sparsity": a.dynamic_sparsity,
            "noise_std_init": a.noise, "grad_scale": workload.grad_scale}
 
@@ -274,7 +311,8 @@ def main():
             kind, val = "port", amort
             sample += " (2 timed steps after 1 warm-up step; reference package not installed)"
             extra = {"regular_step_ms": reg, "curvature_step_ms": curv}
-        line = {"impl": "reference", "metric": METRIC, "value": round(val, 3), "unit": UNIT,
+        line = {"impl": "reference", "metric": metric_for(workload), "value": round(val, 3),
+                "unit": UNIT,
                 "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
                 "ms_per_step": round(val, 3), "higher_is_better": False,
                 "scaling": "strong", "vs_baseline": None, "dtype": "f32",
@@ -361,6 +399,7 @@ def main():
     if world > 1:
         torch.distributed.barrier()
     clk = clocks.stop()
+    peak_gb = torch.cuda.max_memory_allocated(dev) / 1e9   # through the timed region
     launches = L.scao_launch_count() - launches0
     L.scao_prof_enable(0)
     prof = _lib.prof_read()
@@ -547,13 +586,20 @@ def main():
     if world == 1 and a.nondegenerate_steps > 0 and workload.grad_scale < 0.5:
         nondeg = nondegenerate_leg(a, opt, params, workload, dev, stream, L)
 
+    if world > 1:
+        t = torch.tensor([peak_gb], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        peak_gb = t.item()
+    peak_gb = round(peak_gb, 2)
     if rank != 0:
         return
     line = {
-        "metric": METRIC, "value": round(ms_per_step, 3), "unit": UNIT, "n_gpus": world,
+        "metric": metric_for(workload), "value": round(ms_per_step, 3), "unit": UNIT,
+        "n_gpus": world,
         "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms_per_step, 3),
         "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
-        "dtype": "bf16", "data": "synthetic (seeded low-rank+noise gradients, N(0,0.02^2) params)",
+        "dtype": "bf16" if workload.param_dtype != "float32" else "f32",
+        "data": "synthetic (seeded low-rank+noise gradients, N(0,0.02^2) params)",
         "config": dict(cfg, parallelism=f"owner-compute x{world}" if world > 1 else "single"),
         "regular_step_ms": round(statistics.mean(reg), 3) if reg else None,
         "curvature_step_ms": round(statistics.mean(cur), 3) if cur else None,
@@ -576,6 +622,7 @@ def main():
         **({"nondegenerate": nondeg} if nondeg else {}),
         "kernels": kern,
         "gpu_launches": int(launches),
+        "peak_hbm_gb": peak_gb,
         **({"comm_compute_split": split} if split else {}),
         "clocks": clk,
     }

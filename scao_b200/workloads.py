@@ -133,11 +133,11 @@ def c1() -> Workload:
         grad_rank=8, grad_decay=0.7, steps=100)
 
 
-def c2() -> Workload:
+def c2(n_layers: int = 12) -> Workload:
     """Configuration C2: GPT-2-small shapes, embedding Adam-only."""
-    ps = [ParamSpec("wte", (50257, 768), adam_only=True)] + _gpt_layers(12, 768, 3072)
+    ps = [ParamSpec("wte", (50257, 768), adam_only=True)] + _gpt_layers(n_layers, 768, 3072)
     return Workload(
-        "c2-gpt2-small", ps,
+        "c2-gpt2-small" if n_layers == 12 else f"c2-gpt2-small-{n_layers}L", ps,
         dict(lr=1e-3, betas=(0.9, 0.999), precond_freq=10, warmup_steps=20,
              blend_steps=50, min_precond_updates=1, k_max=64,
              max_precond_dim=1024, use_int8_ema=True, **_PARITY),
@@ -163,7 +163,7 @@ def c5(n_layers: int = 36) -> Workload:
     ps += _llama_layers(n_layers, 2048, 16, 2, 128, 11008)
     ps += [ParamSpec("final_norm", (2048,))]
     return Workload(
-        "qwen2.5-3b", ps,
+        "qwen2.5-3b" if n_layers == 36 else f"qwen2.5-3b-{n_layers}L", ps,
         dict(lr=1e-3, betas=(0.9, 0.999), precond_freq=10, warmup_steps=20,
              blend_steps=50, min_precond_updates=1, k_max=64,
              max_precond_dim=1024, use_int8_ema=True, **_PARITY),
