@@ -354,15 +354,24 @@ size_t eg_smem(bool int8_a) {
     return 2 * (size_t)eg_stage(int8_a ? 1 : 3, EG_NPMAX) + 1024;
 }
 
-// x = hi + mid + lo (bf16 parts, exact for finite fp32)
+// x = hi + mid + lo exactly (finite fp32): each part keeps the top 8
+// significant bits of what remains (truncation, so every remainder is exact
+// in fp32 and the last one fits bf16).  Integer / fp32 ops only.
 SCAO_DEV void split3(float x, uint16_t& h, uint16_t& m, uint16_t& l) {
-    const __nv_bfloat16 bh = __float2bfloat16_rn(x);
-    const float r1 = x - __bfloat162float(bh);
-    const __nv_bfloat16 bm = __float2bfloat16_rn(r1);
-    const float r2 = r1 - __bfloat162float(bm);
-    h = __bfloat16_as_ushort(bh);
-    m = __bfloat16_as_ushort(bm);
-    l = __bfloat16_as_ushort(__float2bfloat16_rn(r2));
+    const uint32_t xb = __float_as_uint(x);
+    const float r1 = x - __uint_as_float(xb & 0xFFFF0000u);
+    const uint32_t rb = __float_as_uint(r1);
+    const float r2 = r1 - __uint_as_float(rb & 0xFFFF0000u);
+    h = (uint16_t)(xb >> 16);
+    m = (uint16_t)(rb >> 16);
+    l = (uint16_t)(__float_as_uint(r2) >> 16);
+}
+
+// int8 code -> its exact bf16 bit pattern (|q| <= 127): the bits of
+// 1.5 * 2^23 + q as a float, minus the bias, give (float)q exactly
+SCAO_DEV uint16_t i8_to_bf16(int q) {
+    const float f = __int_as_float(0x4B400000 + q) - 12582912.0f;
+    return (uint16_t)(__float_as_uint(f) >> 16);
 }
 
 // store 8 fp32 values as 3 x 16 bytes of bf16 parts
@@ -500,7 +509,7 @@ eig_tc_gemm_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, EgSpec g) {
                 get8(fac ? Af : A, lda, m0 + r, k0 + kg, M, K, vecA, av[it]);
             } else {
                 // A^T: element (m, k) = X[k][m]; 8 consecutive m of row k
-                const int kk = item >> 4, mg = (item & 15) * 8;
+                const int kk = (item & 7) + 8 * (item >> 7), mg = ((item >> 3) & 15) * 8;
                 get8(A, lda, k0 + kk, m0 + mg, K, M, vecA, av[it]);
             }
         }
@@ -508,7 +517,8 @@ eig_tc_gemm_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, EgSpec g) {
         for (int it = 0; it < BIT; ++it) {
             const int item = tid + it * NT;
             if (item < nbi) {
-                const int kk = item / (npad >> 3), ng = (item % (npad >> 3)) * 8;
+                const int nb8 = npad >> 3;   // 8 threads fill one 128-byte core matrix
+                const int kk = (item & 7) + 8 * ((item >> 3) / nb8), ng = ((item >> 3) % nb8) * 8;
                 get8(B, ldb, k0 + kk, ng, K, N, vecB, bv[it]);
             }
         }
@@ -527,7 +537,7 @@ eig_tc_gemm_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, EgSpec g) {
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
                     const int8_t q = (int8_t)((w[i >> 2] >> ((i & 3) * 8)) & 0xFF);
-                    h[i] = __bfloat16_as_ushort(__float2bfloat16_rn((float)q));
+                    h[i] = i8_to_bf16(q);
                 }
                 uint4 H;
                 H.x = h[0] | ((uint32_t)h[1] << 16); H.y = h[2] | ((uint32_t)h[3] << 16);
@@ -537,7 +547,7 @@ eig_tc_gemm_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, EgSpec g) {
                 const int r = item >> 3, kg = (item & 7) * 8;
                 put8(sa, EG_APART, canon_off(r, kg, EG_BK), av[it]);
             } else {
-                const int kk = item >> 4, mg = (item & 15) * 8;
+                const int kk = (item & 7) + 8 * (item >> 7), mg = ((item >> 3) & 15) * 8;
                 put8(sa, EG_APART, canon_off_mn(mg, kk, EG_BM), av[it]);
             }
         }
@@ -545,7 +555,8 @@ eig_tc_gemm_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, EgSpec g) {
         for (int it = 0; it < BIT; ++it) {
             const int item = tid + it * NT;
             if (item < nbi) {
-                const int kk = item / (npad >> 3), ng = (item % (npad >> 3)) * 8;
+                const int nb8 = npad >> 3;   // 8 threads fill one 128-byte core matrix
+                const int kk = (item & 7) + 8 * ((item >> 3) / nb8), ng = ((item >> 3) % nb8) * 8;
                 put8(sb, bpart, canon_off_mn(ng, kk, npad), bv[it]);
             }
         }
