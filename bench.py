@@ -354,6 +354,18 @@ def main():
         from scao_b200.distributed import ShardedSCAO
         opt = ShardedSCAO(params, workload, lambda ps: build_opt_list(workload, ps, SCAO),
                           buckets=a.buckets, sm_reserve=a.sm_reserve)
+        # unsharded shadow of this rank's parameters (one optimizer per bucket,
+        # as the owner runs them), replayed after the timed region on the
+        # same gradients: every rank receives the same G_t, so the averaged
+        # gradient is exactly G_t and the owned parameters must match it
+        shadow = []
+        lay = opt.layout
+        for b in range(lay.nb):
+            mine = [i for i in opt.my if lay.bucket[i] == b]
+            if mine:
+                ps = [torch.nn.Parameter(params[i].detach().clone()) for i in mine]
+                shadow.append((mine, ps, build_opt_list(
+                    workload, [(p, workload.params[i]) for p, i in zip(ps, mine)], SCAO)))
     else:
         opt = build_opt(workload, params, SCAO)
 
@@ -410,6 +422,25 @@ def main():
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         total_ms = t.item()
     ms_per_step = total_ms / a.steps
+    parity = None
+    if world > 1:
+        # the shadow runs the same n_prime + steps steps without sharding
+        for k in range(n_prime + a.steps):
+            for mine, ps, sopt in shadow:
+                for i, p in zip(mine, ps):
+                    p.grad = grad_sets[k % n_sets][i]
+                sopt.step()
+        torch.cuda.synchronize()
+        d = 0.0
+        for mine, ps, _ in shadow:
+            for i, p in zip(mine, ps):
+                d = max(d, (params[i].detach().float() - p.detach().float()).abs().max().item())
+        t = torch.tensor([d], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        parity = {"parity_max_abs": t.item(), "steps_compared": n_prime + a.steps,
+                  "note": "owned parameters after the run vs an unsharded optimizer per "
+                          "bucket fed the same gradients (every rank's G_t is identical, so "
+                          "the averaged gradient is G_t exactly); max over ranks"}
     reg = [t for t, c in zip(step_ms, curv_flags) if not c]
     cur = [t for t, c in zip(step_ms, curv_flags) if c]
 
@@ -625,6 +656,7 @@ def main():
         "peak_hbm_gb": peak_gb,
         **({"comm_compute_split": split} if split else {}),
         "clocks": clk,
+        **({"sharded_parity": parity} if parity else {}),
     }
     if e2e:
         line["e2e"] = e2e

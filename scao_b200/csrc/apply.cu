@@ -251,13 +251,13 @@ param_pre_kernel(ScaoPlanDev P) {
 
 // Adan moments + update for one element (optimizer.py:608-633).
 struct AdanOut { float u; };
-// x / c for a per-parameter constant c with r ~= 1/c: quotient from the
-// reciprocal, then one fused residual correction (Markstein); matches the
-// IEEE quotient of __fdiv_rn for normal operands.
-__device__ __forceinline__ float div_c(float x, float c, float r) {
-    const float q = x * r;
-    const float e = fmaf(-q, c, x);
-    return fmaf(e, r, q);
+// x / c for a per-parameter constant c (bias corrections): the IEEE quotient,
+// as the reference's tensor division computes it.  (A reciprocal multiply with
+// one fused correction -- Markstein's scheme -- is correctly rounded only under
+// conditions on c and the reciprocal that a per-step constant does not
+// guarantee; r is kept in the step table for the C-ABI layout only.)
+__device__ __forceinline__ float div_c(float x, float c, float /*r*/) {
+    return __fdiv_rn(x, c);
 }
 
 __device__ __forceinline__ float adan_elem(const ScaoParamStep& S, int dt, float g, float gp,

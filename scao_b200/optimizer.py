@@ -386,7 +386,7 @@ class SCAO(Optimizer):
                 row["phase"] = 1
                 row["alpha1"] = -(lr / bc1)
                 row["sqrt_bc2"] = math.sqrt(bc2)
-                row["rbc2"] = 1.0 / float(row["sqrt_bc2"])      # x / c as x * r + correction
+                row["rbc2"] = 1.0 / float(row["sqrt_bc2"])      # unused by the kernels
                 continue
             row["phase"] = 2
             if not st.get("scao_phase_started", False):
@@ -399,7 +399,7 @@ class SCAO(Optimizer):
             row["blend"] = blend
             row["one_minus_blend"] = 1.0 - blend
             row["bc1"], row["bc2"], row["bc3"] = bc1, bc2, 1.0 - b3 ** step
-            # reciprocals of the float32 constants (x / c = x * r + one FMA correction)
+            # reciprocals of the constants: table fields only (the kernels divide)
             for k in ("bc1", "bc2", "bc3"):
                 row["r" + k] = 1.0 / float(row[k])
             tau = g["tau"]
