@@ -386,7 +386,7 @@ class SCAO(Optimizer):
                 row["phase"] = 1
                 row["alpha1"] = -(lr / bc1)
                 row["sqrt_bc2"] = math.sqrt(bc2)
-                row["rbc2"] = 1.0 / float(row["sqrt_bc2"])      # unused by the kernels
+                row["rbc2"] = _recip32(row["sqrt_bc2"])   # RN(1/c) for the kernels' division
                 continue
             row["phase"] = 2
             if not st.get("scao_phase_started", False):
@@ -399,9 +399,9 @@ class SCAO(Optimizer):
             row["blend"] = blend
             row["one_minus_blend"] = 1.0 - blend
             row["bc1"], row["bc2"], row["bc3"] = bc1, bc2, 1.0 - b3 ** step
-            # reciprocals of the constants: table fields only (the kernels divide)
+            # correctly rounded float32 reciprocals for the kernels' division
             for k in ("bc1", "bc2", "bc3"):
-                row["r" + k] = 1.0 / float(row[k])
+                row["r" + k] = _recip32(row[k])
             tau = g["tau"]
             row["clip"] = 0 if tau is None else 1
             row["tau"] = 0.0 if tau is None else tau
@@ -655,6 +655,11 @@ class SCAO(Optimizer):
             ws._stable_count = int(runtime.get("warmup_stable_count", ws._stable_count))
             ws._early_exit_step = runtime.get("warmup_early_exit_step", ws._early_exit_step)
         self._lookahead_init = False
+
+
+def _recip32(c):
+    """RN(1/c) in float32 (c rounded to float32 first, as the kernels see it)."""
+    return float(np.float32(1.0) / np.float32(c))
 
 
 def _in_param_dtypes(norms, params):
