@@ -279,42 +279,43 @@ size_t gram_tc_smem() {
 }
 
 // ---------------------------------------------------------------------------
-// Persistent, warp-specialised tensor-core gram + EMA (bf16 gradients whose
-// leaf block allows whole 64-deep K blocks).  Operands arrive by TMA tensor
-// copies (cp.async.bulk.tensor, 128-byte swizzle, no multicast) from one 2-D
-// tensor map per parameter gradient; the leaf block is selected by the copy
-// coordinates.  Roles per CTA (one CTA per SM, 192 threads):
-//   warp 0      TMA producer over a GST-stage shared-memory ring
-//   warp 1      TMEM owner and MMA issuer (one thread), 2 accumulators
-//   warps 2-5   epilogue: TMEM -> dequant*rho + alpha*gram -> fp32 staging
-// The epilogue of tile t overlaps the main loop of tile t+1 (double-buffered
-// TMEM accumulators).  L = G G^T uses K-major operands (gradient rows);
-// R = G^T G uses MN-major operands (gradient columns) -- no transpose.
-// Every wait is bounded; on a timeout the CTA records an error and stops.
+// Persistent, warp-specialised tensor-core gram + EMA on SM pairs (bf16
+// gradients whose leaf block allows whole 64-deep K blocks).  The grid is made
+// of clusters of 2 CTAs (one CTA per SM); a cluster computes 256 x 256 output
+// tiles of the lower triangle with tcgen05.mma.cta_group::2 (M = 256): each CTA
+// holds its 128 rows of A and 128 of the 256 columns of B in its own shared
+// memory and its 128 accumulator rows in its own TMEM, so per SM the operand
+// traffic of a 128 x 256 tile is A + B/2 instead of A + B (the 1-SM tile was
+// bound by shared-memory bandwidth).  Operands arrive by TMA tensor copies
+// (cp.async.bulk.tensor, 128-byte swizzle, no multicast) from one 2-D tensor
+// map per parameter gradient; each CTA copies its own halves and the copies
+// complete on the pair leader's barrier.  Roles per CTA (320 threads):
+//   warp 0      TMA producer over a GST-stage ring (both CTAs)
+//   warp 1      TMEM owner (both); MMA issuer (leader, one thread)
+//   warps 2-9   epilogue: own TMEM rows -> dequant*rho + alpha*gram -> staging
+// The epilogue of tile t overlaps the main loop of tile t+1 (two TMEM
+// accumulators).  L = G G^T uses K-major operands (gradient rows); R = G^T G
+// uses MN-major operands (gradient columns) -- no transpose.  Every wait is
+// bounded; on a timeout the CTA records an error, stops issuing, and both CTAs
+// still meet at the final cluster barrier.
 // ---------------------------------------------------------------------------
-constexpr int GN = 256;                 // output tile: 128 rows x GN columns
-constexpr int GST = 4;                  // pipeline stages
+constexpr int GN = 256;                 // output tile: 256 rows x GN columns per pair
+constexpr int GST = 6;                  // pipeline stages
 constexpr uint32_t GOPB = 128 * 64 * 2; // one 128 x 64 operand block, 16 KB
-constexpr uint32_t GSTAGE = GOPB + (GN / 128) * GOPB;
+constexpr uint32_t GSTAGE = 2 * GOPB;   // per CTA: A half + B half
 constexpr int GEPI = 256;                // epilogue threads (8 warps)
 constexpr int GTHREADS = 64 + GEPI;
 constexpr int GTRI = GT * GT;           // floats per staged 128 x 128 sub-tile
 
-
-
-
-// work tiles of one factor problem: row block ti (128 rows), column block
-// tc (GN columns) for every tc * GN <= 128 ti + 127 (lower triangle)
-__device__ __forceinline__ int gram_row_tiles(int ti) { return (128 * ti + 127) / GN + 1; }
+// work tiles of one factor problem: row block ti2 (256 rows), column block tc
+// (256 columns) for every tc <= ti2 (lower triangle)
 __host__ __device__ inline int gram_work_tiles(int n) {
-    const int nt = (n + 127) / 128;
-    int c = 0;
-    for (int ti = 0; ti < nt; ++ti) c += (128 * ti + 127) / GN + 1;
-    return c;
+    const int nt2 = (n + 255) / 256;
+    return nt2 * (nt2 + 1) / 2;
 }
 
 struct GTile {
-    int j, leaf, side, n, K, ti, tc, param;
+    int j, leaf, side, n, K, ti2, tc, param;
     int64_t row0, col0;
 };
 
@@ -330,22 +331,21 @@ __device__ __forceinline__ bool gram_tile(const ScaoPlanDev& P, const int32_t* i
     if (!gram_tma_use(P.params, P.step, L, w.side)) return false;
     w.n = w.side ? L.b : L.a;
     w.K = w.side ? L.a : L.b;
-    const int nt = (w.n + 127) / 128;
-    int ti = 0;
-    for (; ti < nt; ++ti) {
-        const int c = gram_row_tiles(ti);
-        if (t < c) break;
-        t -= c;
+    const int nt2 = (w.n + 255) / 256;
+    int ti2 = 0;
+    for (; ti2 < nt2; ++ti2) {
+        if (t < ti2 + 1) break;
+        t -= ti2 + 1;
     }
-    if (ti >= nt) return false;
-    w.ti = ti;
+    if (ti2 >= nt2) return false;
+    w.ti2 = ti2;
     w.tc = t;
     w.row0 = L.row0;
     w.col0 = L.col0;
     return true;
 }
 
-__global__ void __launch_bounds__(GTHREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GTHREADS, 1)
 gram_tma_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, int nprob, int tpp,
                 float* xbuf, int64_t xstride, float* amnew, float rho_f, float alpha_f, int* err) {
     extern __shared__ unsigned char gsm_raw[];
@@ -354,73 +354,79 @@ gram_tma_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, int nprob, int t
     __shared__ uint32_t tslot;
     __shared__ volatile int abort_flag;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
     if (tid == 0) {
-        for (int i = 0; i < GST; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
-        for (int i = 0; i < 2; ++i) { mbar_init(&accf[i], 1); mbar_init(&acce[i], GEPI); }
+        // the leader's full barrier counts both CTAs' producers; its acce
+        // counts both CTAs' epilogue warps
+        for (int i = 0; i < GST; ++i) { mbar_init(&full[i], 2); mbar_init(&empty[i], 1); }
+        for (int i = 0; i < 2; ++i) { mbar_init(&accf[i], 1); mbar_init(&acce[i], 2 * (GEPI / 32)); }
         mbar_init(&fin, 1);
         abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 1) tc_alloc(&tslot, 2 * GN);
+    if (warp == 1) tc_alloc_pair(&tslot, 2 * GN);
     tc_fence_before();
-    __syncthreads();
+    cluster_sync_all();        // barriers initialised and TMEM allocated in both CTAs
     tc_fence_after();
     const uint32_t tmem = tslot;
     const int total = nprob * tpp;
+    const int cid = blockIdx.x >> 1, ncl = gridDim.x >> 1;
     const unsigned char* maps = P.tmaps;
     if (warp == 0) {
         if (lane == 0) {
-            // ---------------- TMA producer ----------------
+            // ---------------- TMA producer (both CTAs) ----------------
             int stage = 0;
             uint32_t ph = 0, issued = 0, last_ph = 0;
             GTile w;
-            for (int T = blockIdx.x; T < total && !abort_flag; T += gridDim.x) {
+            for (int T = cid; T < total && !abort_flag; T += ncl) {
                 if (!gram_tile(P, ids, tpp, T, w)) continue;
                 const void* map = scao_tmap(maps, w.param, w.side ? TM_G64 : TM_G128);
-                const int i0 = w.ti * 128, j0 = w.tc * GN;
+                // this CTA's 128 rows of A and 128 columns of B
+                const int i0 = w.ti2 * 256 + 128 * (int)rank, j0 = w.tc * GN + 128 * (int)rank;
                 const int x0 = (int)w.col0, y0 = (int)w.row0;
                 for (int kb = 0; kb < w.K / 64; ++kb) {
                     if (!mbar_wait(&empty[stage], ph ^ 1)) { abort_flag = 1; atomicExch(err, 2); break; }
-                    mbar_expect_tx(&full[stage], GSTAGE);
+                    const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
+                    mbar_arrive_expect_tx_cl(fb, GSTAGE);
                     const uint32_t a = smem_u32(gsm + (size_t)stage * GSTAGE), b = a + GOPB;
                     const int k0 = kb * 64;
                     if (w.side == 0) {
                         // K-major: x = K (gradient column), y = output index (row)
-                        tma_load_2d(a, map, x0 + k0, y0 + i0, &full[stage]);
-#pragma unroll
-                        for (int h = 0; h < GN / 128; ++h)
-                            tma_load_2d(b + h * GOPB, map, x0 + k0, y0 + j0 + 128 * h, &full[stage]);
+                        tma_load_2d_pair(a, map, x0 + k0, y0 + i0, fb);
+                        tma_load_2d_pair(b, map, x0 + k0, y0 + j0, fb);
                     } else {
                         // MN-major: x = output index (gradient column), y = K (row)
 #pragma unroll
-                        for (int h = 0; h < 2; ++h)
-                            tma_load_2d(a + h * (GOPB / 2), map, x0 + i0 + 64 * h, y0 + k0, &full[stage]);
-#pragma unroll
-                        for (int h = 0; h < GN / 64; ++h)
-                            tma_load_2d(b + h * (GOPB / 2), map, x0 + j0 + 64 * h, y0 + k0, &full[stage]);
+                        for (int h = 0; h < 2; ++h) {
+                            tma_load_2d_pair(a + h * (GOPB / 2), map, x0 + i0 + 64 * h, y0 + k0, fb);
+                            tma_load_2d_pair(b + h * (GOPB / 2), map, x0 + j0 + 64 * h, y0 + k0, fb);
+                        }
                     }
                     issued |= 1u << stage;
                     last_ph = (last_ph & ~(1u << stage)) | (ph << stage);
                     if (++stage == GST) { stage = 0; ph ^= 1; }
                 }
             }
-            // no copy may still be landing when the CTA exits
-            for (int s2 = 0; s2 < GST; ++s2)
-                if ((issued >> s2) & 1u)
-                    if (!mbar_wait(&full[s2], (last_ph >> s2) & 1u)) atomicExch(err, 2);
+            // the leader waits until no copy of either CTA is still landing
+            // (both CTAs' copies complete on the leader's barriers)
+            if (leader)
+                for (int s2 = 0; s2 < GST; ++s2)
+                    if ((issued >> s2) & 1u)
+                        if (!mbar_wait(&full[s2], (last_ph >> s2) & 1u)) atomicExch(err, 2);
         }
     } else if (warp == 1) {
-        if (lane == 0) {
-            // ---------------- MMA issuer ----------------
+        if (lane == 0 && leader) {
+            // ---------------- MMA issuer (leader) ----------------
             int stage = 0, acc = 0;
             uint32_t ph = 0, aph = 0;
             GTile w;
-            for (int T = blockIdx.x; T < total && !abort_flag; T += gridDim.x) {
+            for (int T = cid; T < total && !abort_flag; T += ncl) {
                 if (!gram_tile(P, ids, tpp, T, w)) continue;
                 if (!mbar_wait(&acce[acc], aph ^ 1)) { abort_flag = 1; atomicExch(err, 2); break; }
                 tc_fence_after();
                 const uint32_t d = tmem + acc * GN;
-                const uint32_t idesc = idesc_bf16(128, GN, w.side, w.side);
+                const uint32_t idesc = idesc_bf16(256, GN, w.side, w.side);
                 bool ok = true;
                 for (int kb = 0; kb < w.K / 64; ++kb) {
                     if (!mbar_wait(&full[stage], ph)) { ok = false; break; }
@@ -436,29 +442,32 @@ gram_tma_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, int nprob, int t
                             ad = smem_desc_sw128(a + s * 2048, GOPB / 2, 1024);
                             bd = smem_desc_sw128(b + s * 2048, GOPB / 2, 1024);
                         }
-                        tc_mma_bf16(d, ad, bd, idesc, (kb > 0 || s > 0) ? 1u : 0u);
+                        tc_mma_bf16_pair(d, ad, bd, idesc, (kb > 0 || s > 0) ? 1u : 0u);
                     }
-                    tc_commit(&empty[stage]);
+                    tc_commit_pair(&empty[stage], 0x3);
                     if (++stage == GST) { stage = 0; ph ^= 1; }
                 }
                 if (!ok) { abort_flag = 1; atomicExch(err, 2); break; }
-                tc_commit(&accf[acc]);
+                tc_commit_pair(&accf[acc], 0x3);
                 acc ^= 1;
                 if (acc == 0) aph ^= 1;
             }
-            // every issued MMA has completed before TMEM is released
-            tc_commit(&fin);
-            if (!mbar_wait(&fin, 0)) atomicExch(err, 2);
+            // every issued MMA has completed before either CTA releases TMEM
+            tc_commit_pair(&fin, 0x3);
         }
+        __syncwarp();
+        if (!mbar_wait(&fin, 0)) atomicExch(err, 2);
     } else {
-        // ---------------- epilogue (warps 2..9) ----------------
+        // ---------------- epilogue (warps 2..9, both CTAs) ----------------
         const int q = warp & 3;                 // TMEM lane quarter of this warp
         const int h = (warp - 2) >> 2;          // column half of the tile
-        const int r = q * 32 + lane;            // tile row
+        const int r = q * 32 + lane;            // row within this CTA's 128 rows
+        const uint32_t acce_cl[2] = {mapa_shared(smem_u32(&acce[0]), 0),
+                                     mapa_shared(smem_u32(&acce[1]), 0)};
         int acc = 0;
         uint32_t aph = 0;
         GTile w;
-        for (int T = blockIdx.x; T < total; T += gridDim.x) {
+        for (int T = cid; T < total; T += ncl) {
             if (__any_sync(0xffffffffu, abort_flag)) break;
             if (!gram_tile(P, ids, tpp, T, w)) continue;
             // warp-uniform: the TMEM loads below are warp-collective
@@ -469,7 +478,8 @@ gram_tma_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, int nprob, int t
             }
             tc_fence_after();
             const int n = w.n;
-            const int i0 = w.ti * 128, j0 = w.tc * GN + h * (GN / 2);
+            const int ti = 2 * w.ti2 + (int)rank;           // 128-row block of this CTA
+            const int i0 = ti * 128, j0 = w.tc * GN + h * (GN / 2);
             const int i = i0 + r;
             const int pid = 2 * w.leaf + w.side;
             const ScaoLeaf& L = P.leaves[w.leaf];
@@ -478,7 +488,7 @@ gram_tma_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, int nprob, int t
             const uint32_t tbase = tmem + acc * GN + h * (GN / 2) + ((uint32_t)(q * 32) << 16);
             int cend = min(GN / 2, n - j0);
             // columns above the diagonal sub-tile are not needed
-            cend = min(cend, ((w.ti + 1) << 7) - j0);
+            cend = min(cend, ((ti + 1) << 7) - j0);
             if (P.int8_ema) {
                 const int8_t* qo = (const int8_t*)P.fac + fo;
                 const float s_old = quant_scale_f(P.absmax[pid]);
@@ -493,7 +503,7 @@ gram_tma_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, int nprob, int t
                     const int c0 = u * 16;
                     if (c0 >= cend) break;
                     const int tj = (j0 + c0) >> 7;          // 128-sub-tile of these columns
-                    const bool diag = tj == w.ti;
+                    const bool diag = tj == ti;
                     float v[16];
                     tc_ld16(tbase + c0, v);
                     const int8_t* qv = (const int8_t*)&q4[u];
@@ -510,7 +520,7 @@ gram_tma_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, int nprob, int t
                         xo[c] = x;
                     }
                     float* xt = xbuf + (int64_t)w.j * xstride +
-                                (int64_t)(w.ti * (w.ti + 1) / 2 + tj) * GTRI + r * GT + ((j0 + c0) & 127);
+                                (int64_t)(ti * (ti + 1) / 2 + tj) * GTRI + r * GT + ((j0 + c0) & 127);
 #pragma unroll
                     for (int c = 0; c < 16; c += 4)
                         __stcs((float4*)(xt + c), make_float4(xo[c], xo[c + 1], xo[c + 2], xo[c + 3]));
@@ -533,7 +543,8 @@ gram_tma_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, int nprob, int t
                 }
             }
             tc_fence_before();
-            mbar_arrive(&acce[acc]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cl(acce_cl[acc]);   // the leader's accumulator is free
             acc ^= 1;
             if (acc == 0) aph ^= 1;
             if (P.int8_ema) {
@@ -544,8 +555,10 @@ gram_tma_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, int nprob, int t
     }
     tc_fence_before();
     __syncthreads();
+    // neither CTA leaves while the other may still touch its barriers
+    cluster_sync_all();
     tc_fence_after();
-    if (warp == 1) tc_dealloc(tmem, 2 * GN);
+    if (warp == 1) tc_dealloc_pair(tmem, 2 * GN);
 }
 
 size_t gram_tma_smem() { return (size_t)GST * GSTAGE + 1024; }
@@ -846,7 +859,9 @@ extern "C" int scao_plan_curvature(const ScaoPlanDev* P, const int32_t* leaf_ids
                                      (int)gram_tma_smem());
             }
             const int64_t work = (int64_t)np * tpp;
-            const int g = scao_persistent_grid(P, work);
+            // clusters of 2 CTAs: an even grid of at most one CTA per SM
+            int g = scao_persistent_grid(P, 2 * work) & ~1;
+            if (g < 2) g = 2;
             ProfScope _ps(SLOT_GRAM_TC, st);
             gram_tma_kernel<<<g, GTHREADS, gram_tma_smem(), st>>>(*P, ids, np, tpp, xbuf, xstride,
                                                                   amnew, rho_f, alpha_f, P->err);

@@ -216,3 +216,66 @@ TC_DEV void tma_store_2d_hint(const void* map, int x, int y, uint32_t src, uint6
         "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%1, %2}], [%3], %4;"
         :: "l"(map), "r"(x), "r"(y), "r"(src), "l"(policy) : "memory");
 }
+
+// ---------------------------------------------------------------------------
+// CTA-pair (cta_group::2) helpers: one tcgen05.mma spans the tensor cores of
+// two SMs of a cluster of 2; each CTA holds half of A (its 128 rows) and half
+// of B in its own shared memory, and its 128 accumulator rows in its own TMEM.
+// ---------------------------------------------------------------------------
+TC_DEV uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// shared::cluster address of a shared::cta location in CTA `rank` of the cluster
+TC_DEV uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+TC_DEV void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+                 ::: "memory");
+}
+// arrive (with transaction bytes expected) on an mbarrier given by its cluster address
+TC_DEV void mbar_arrive_expect_tx_cl(uint32_t cl_addr, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cluster.b64 _, [%0], %1;"
+                 :: "r"(cl_addr), "r"(bytes) : "memory");
+}
+TC_DEV void mbar_arrive_cl(uint32_t cl_addr) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" :: "r"(cl_addr) : "memory");
+}
+// TMA tensor load into this CTA's shared memory whose completion is counted
+// on the pair leader's mbarrier (cluster address).  No multicast.
+TC_DEV void tma_load_2d_pair(uint32_t dst, const void* map, int x, int y, uint32_t mbar_cl) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3}], [%4];"
+        :: "r"(dst), "l"(map), "r"(x), "r"(y), "r"(mbar_cl) : "memory");
+}
+TC_DEV void tc_mma_bf16_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                             uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n"
+        :
+        : "r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+// arrive on the mbarrier at this shared offset in every CTA of cta_mask when
+// the pair's issued MMAs have completed
+TC_DEV void tc_commit_pair(uint64_t* mbar, uint16_t cta_mask) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+        :: "r"(smem_u32(mbar)), "h"(cta_mask) : "memory");
+}
+// one warp in each CTA of the pair (same warp index): TMEM for both
+TC_DEV void tc_alloc_pair(uint32_t* slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
+                 :: "r"(smem_u32(slot)), "r"(ncols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+TC_DEV void tc_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;"
+                 :: "r"(taddr), "r"(ncols) : "memory");
+}
