@@ -234,6 +234,10 @@ typedef struct {
     float* strip_part;           /* per strip: |u|^2, |g|^2, |p_dec|^2, nat^2 */
     int32_t n_strips;
     int32_t pad6_;
+    uint8_t* eig_img;            /* eigensolver operand images (bf16 hi/mid/lo
+                                    tiles of an n x s block), eig_img_stride
+                                    bytes per factor problem 2*leaf+side     */
+    int64_t eig_img_stride;
 } ScaoPlanDev;
 
 /* ---------------------------------------------------------------------- */

@@ -93,6 +93,7 @@ class PlanDev(C.Structure):
         ("tmaps", _P), ("tmaps_ok", C.c_int32), ("gnorm_host", C.c_int32),
         ("filt", FilterDev),
         ("strips", _P), ("strip_part", _P), ("n_strips", C.c_int32), ("pad6_", C.c_int32),
+        ("eig_img", _P), ("eig_img_stride", C.c_int64),
     ]
 
 

@@ -344,6 +344,7 @@ struct EgSpec {
     int cheb_i;         // EPI_CHEB: recurrence index i >= 2
     int fail_x;         // where F_CHOLFAIL is set, store X instead
     int skip_direct;    // skip problems solved directly (s == n)
+    int b_img;          // B from its pre-split image (eig_presplit_kernel), not converted here
 };
 
 __host__ __device__ constexpr uint32_t eg_bpart(int npad) { return (uint32_t)EG_BK * npad * 2; }
@@ -419,6 +420,31 @@ SCAO_DEV void cheb_coef(const float* aux, int i, float& al, float& be, float& ga
     ga = -sp * s;
 }
 
+// Pre-split an n x s operand of the factor products (subspace problems) into
+// its image: per 64-row chunk the three bf16 parts in the MN-major canonical
+// layout the GEMM stages, so the GEMM copies each chunk with one bulk copy
+// instead of converting it in every 128-row tile of the product.
+__global__ void __launch_bounds__(NT)
+eig_presplit_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, int buf) {
+    const PInfo p = pinfo(P, ids, blockIdx.y);
+    if (skip_iter(p) || (flags_of(p) & F_DIRECT)) return;
+    const int n = p.n, N = p.s, npad = (N + 15) & ~15;
+    const int k0 = blockIdx.x * EG_BK;
+    if (k0 >= n) return;
+    int ld;
+    const float* X = buf_ptr(P, p, buf, &ld);
+    const uint32_t bpart = eg_bpart(npad);
+    unsigned char* img = P.eig_img + (int64_t)(2 * p.leaf + p.side) * P.eig_img_stride + (size_t)blockIdx.x * 3 * bpart;
+    const int nb8 = npad >> 3, nbi = EG_BK * nb8;
+    const bool vec = (ld & 3) == 0;
+    for (int item = threadIdx.x; item < nbi; item += blockDim.x) {
+        const int kk = (item & 7) + 8 * ((item >> 3) / nb8), ng = ((item >> 3) % nb8) * 8;
+        float v[8];
+        get8(X, ld, k0 + kk, ng, n, N, vec, v);
+        put8(img, bpart, canon_off_mn(ng, kk, npad), v);
+    }
+}
+
 __global__ void __launch_bounds__(NT, 1)
 eig_tc_gemm_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, EgSpec g) {
     const PInfo p = pinfo(P, ids, blockIdx.y);
@@ -457,15 +483,25 @@ eig_tc_gemm_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, EgSpec g) {
     unsigned char* sm = (unsigned char*)(((uintptr_t)eg_smem_raw + 1023) & ~(uintptr_t)1023);
     const uint32_t bpart = eg_bpart(npad);
     const uint32_t stage = (uint32_t)na * EG_APART + 3 * bpart;
-    __shared__ uint64_t mbar[2];
+    __shared__ uint64_t mbar[2], fullb[2];
     __shared__ uint32_t tslot;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t tcols = npad <= 32 ? 32 : npad <= 64 ? 64 : npad <= 128 ? 128 : 256;
+    // B staged by bulk copies of its pre-split image (subspace problems)
+    const bool bimg = g.b_img && !(flags_of(p) & F_DIRECT);
+    const unsigned char* img = P.eig_img + (int64_t)(2 * p.leaf + p.side) * P.eig_img_stride;
+    const uint32_t bbytes = 3 * bpart;
     if (warp == 0) tc_alloc(&tslot, tcols);
     if (tid == 0) {
         mbar_init(&mbar[0], 1);
         mbar_init(&mbar[1], 1);
+        mbar_init(&fullb[0], 1);
+        mbar_init(&fullb[1], 1);
         fence_async_smem();
+        if (bimg) {
+            mbar_expect_tx(&fullb[0], bbytes);
+            bulk_g2s(sm + na * EG_APART, img, bbytes, &fullb[0]);
+        }
     }
     tc_fence_before();
     __syncthreads();
@@ -484,9 +520,9 @@ eig_tc_gemm_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, EgSpec g) {
     uint2 aq[AIT];
     float bv[BIT][8];
     bool ok = true;
-    for (int kb = 0; kb < nkb; ++kb) {
+    // global -> registers for chunk kb (issued one chunk ahead of its use)
+    auto load_regs = [&](int kb) {
         const int k0 = kb * EG_BK;
-        // ---- global -> registers ----
 #pragma unroll
         for (int it = 0; it < AIT; ++it) {
             const int item = tid + it * NT;
@@ -516,12 +552,15 @@ eig_tc_gemm_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, EgSpec g) {
 #pragma unroll
         for (int it = 0; it < BIT; ++it) {
             const int item = tid + it * NT;
-            if (item < nbi) {
+            if (!bimg && item < nbi) {
                 const int nb8 = npad >> 3;   // 8 threads fill one 128-byte core matrix
                 const int kk = (item & 7) + 8 * ((item >> 3) / nb8), ng = ((item >> 3) % nb8) * 8;
                 get8(B, ldb, k0 + kk, ng, K, N, vecB, bv[it]);
             }
         }
+    };
+    load_regs(0);
+    for (int kb = 0; kb < nkb; ++kb) {
         // ---- wait until the MMAs of chunk kb-2 released this stage ----
         const int st = kb & 1;
         if (kb >= 2) ok = mbar_wait(&mbar[st], ((kb - 2) >> 1) & 1) && ok;
@@ -554,12 +593,15 @@ eig_tc_gemm_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, EgSpec g) {
 #pragma unroll
         for (int it = 0; it < BIT; ++it) {
             const int item = tid + it * NT;
-            if (item < nbi) {
+            if (!bimg && item < nbi) {
                 const int nb8 = npad >> 3;   // 8 threads fill one 128-byte core matrix
                 const int kk = (item & 7) + 8 * ((item >> 3) / nb8), ng = ((item >> 3) % nb8) * 8;
                 put8(sb, bpart, canon_off_mn(ng, kk, npad), bv[it]);
             }
         }
+        // the registers are free again: start the next chunk's loads
+        if (kb + 1 < nkb) load_regs(kb + 1);
+        if (bimg) ok = mbar_wait(&fullb[st], (kb >> 1) & 1) && ok;
         fence_async_smem();
         tc_fence_before();
         __syncthreads();
@@ -592,6 +634,15 @@ eig_tc_gemm_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, EgSpec g) {
                 }
             }
             tc_commit(&mbar[st]);
+            // prefetch chunk kb+1 of B into the other stage once the MMAs of
+            // chunk kb-1 have released it
+            if (bimg && kb + 1 < nkb) {
+                const int s1 = (kb + 1) & 1;
+                if (kb >= 1) ok = mbar_wait(&mbar[s1], ((kb - 1) >> 1) & 1) && ok;
+                mbar_expect_tx(&fullb[s1], bbytes);
+                bulk_g2s(sm + s1 * stage + na * EG_APART, img + (size_t)(kb + 1) * bbytes, bbytes,
+                         &fullb[s1]);
+            }
         }
     }
     ok = mbar_wait(&mbar[(nkb - 1) & 1], ((nkb - 1) >> 1) & 1) && ok;
@@ -1052,8 +1103,14 @@ int64_t launch_iteration(const ScaoPlanDev& P, const int32_t* ids, int np, int n
         ++n;
     };
     //            a        b      c       m      k      tA  epi        prev    i  fail skipD
+    auto presplit = [&](int buf) {
+        ProfScope _ps(SLOT_EIG_GEMM, st);
+        eig_presplit_kernel<<<dim3((nmax + EG_BK - 1) / EG_BK, np), NT, 0, st>>>(P, ids, buf);
+        ++n;
+    };
     // Rayleigh-Ritz: Y = A U, H = U^T Y, Jacobi, X = U V, AX = Y V
-    gemm({BUF_FAC, BUF_U, BUF_Y, DIM_N, DIM_N, 0, EPI_FAC, 0, 0, 0, 0}, tiles_n, sm_big);
+    presplit(BUF_U);
+    gemm({BUF_FAC, BUF_U, BUF_Y, DIM_N, DIM_N, 0, EPI_FAC, 0, 0, 0, 0, 1}, tiles_n, sm_big);
     gemm({BUF_U, BUF_Y, BUF_H, DIM_S, DIM_N, 1, EPI_STORE, 0, 0, 0, 0}, tiles_s, sm_small);
     { ProfScope _ps(SLOT_EIG_JACOBI, st); eig_jacobi_kernel<<<np, NT, jsm, st>>>(P, ids, 30); ++n; }
     gemm({BUF_U, BUF_V, BUF_X, DIM_N, DIM_S, 0, EPI_STORE, 0, 0, 0, 0}, tiles_n, sm_small);
@@ -1065,7 +1122,8 @@ int64_t launch_iteration(const ScaoPlanDev& P, const int32_t* ids, int np, int n
     int cur = BUF_Y, prv = BUF_X;
     for (int i = 2; i <= CHEB_M; ++i) {
         const int out = (prv == BUF_X) ? BUF_AX : prv;
-        gemm({BUF_FAC, cur, out, DIM_N, DIM_N, 0, EPI_CHEB, prv, i, 0, 0}, tiles_n, sm_big);
+        presplit(cur);
+        gemm({BUF_FAC, cur, out, DIM_N, DIM_N, 0, EPI_CHEB, prv, i, 0, 0, 1}, tiles_n, sm_big);
         prv = cur;
         cur = out;
     }

@@ -250,6 +250,17 @@ class Plan:
         self.k = z(self.n_leaves, torch.int32)
         self.eig_y, self.eig_x, self.eig_ax = z(u_n), z(u_n), z(u_n)
         self.eig_h, self.eig_v = z(h_n), z(h_n)
+        # split-bf16 images of the eigensolver's n x s operands (subspace
+        # problems): 64-row chunks x 16-padded width x 3 bf16 parts
+        stride = 16
+        for li in range(self.n_leaves):
+            for side in (0, 1):
+                n = int(self.ltab["b" if side else "a"][li])
+                sw = int(self.ltab["sr" if side else "sl"][li])
+                if sw < n:
+                    stride = max(stride, _round_up(n, 64) * _round_up(sw, 16) * 6)
+        self.eig_img_stride = stride
+        self.eig_img = z(stride * 2 * self.n_leaves if stride > 16 else 16, torch.uint8)
         self.eig_aux = z(2 * self.n_leaves * 16)
         self.eig_status = z(2 * self.n_leaves, torch.int32)
         self.w = z(w_n)
@@ -541,4 +552,6 @@ def PlanDev_from(plan):
     d.diag_list, d.flat_list, d.p_list = ptr(plan.t_diag_list), ptr(plan.t_flat_list), ptr(plan.t_p_list)
     d.n_diag = plan.n_diag
     d.strips, d.strip_part, d.n_strips = ptr(plan.t_strips), ptr(plan.strip_part), plan.n_strips
+    d.eig_img = ptr(plan.eig_img)
+    d.eig_img_stride = plan.eig_img_stride
     return d
