@@ -623,6 +623,7 @@ def main():
         peak_gb = t.item()
     peak_gb = round(peak_gb, 2)
     if rank != 0:
+        torch.distributed.destroy_process_group()
         return
     line = {
         "metric": metric_for(workload), "value": round(ms_per_step, 3), "unit": UNIT,
@@ -678,6 +679,8 @@ def main():
     if a.json_out:
         with open(a.json_out, "w") as f:
             json.dump(line, f, indent=1)
+    if world > 1:
+        torch.distributed.destroy_process_group()
 
 
 def nondegenerate_leg(a, opt, params, workload, dev, stream, L):
