@@ -34,6 +34,7 @@
 //   control kernel at the end of each outer iteration clears the loop
 //   condition once every problem has converged (or the iteration cap is
 //   reached), so the host never waits for the device.
+#include <algorithm>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
@@ -351,8 +352,18 @@ __host__ __device__ constexpr uint32_t eg_bpart(int npad) { return (uint32_t)EG_
 __host__ __device__ constexpr uint32_t eg_stage(int na, int npad) {
     return na * EG_APART + 3 * eg_bpart(npad);
 }
+// int8 factor products whose factor rows are 16-byte aligned stream both
+// operands through a ring of up to EG_MAXST stages (A as raw int8 rows by
+// 16-byte asynchronous copies, converted to bf16 in shared memory; B by bulk
+// copies of its image): EG_SMEM_STREAM bytes.
+constexpr int EG_MAXST = 4;
+constexpr size_t EG_SMEM_STREAM = 224 * 1024;
+// int8 rows staged 80 bytes apart: the 8-byte reads of 8 rows x 2 column
+// groups by a half-warp hit 32 distinct banks
+constexpr int EG_SROW = EG_BK + 16;
 size_t eg_smem(bool int8_a) {
-    return 2 * (size_t)eg_stage(int8_a ? 1 : 3, EG_NPMAX) + 1024;
+    const size_t two = 2 * (size_t)eg_stage(int8_a ? 1 : 3, EG_NPMAX) + 1024;
+    return int8_a ? (two > EG_SMEM_STREAM ? two : EG_SMEM_STREAM) : two;
 }
 
 // x = hi + mid + lo exactly (finite fp32): each part keeps the top 8
@@ -420,6 +431,15 @@ SCAO_DEV void cheb_coef(const float* aux, int i, float& al, float& be, float& ga
     ga = -sp * s;
 }
 
+// A tile item (8 consecutive K values of one row) -> (row r, first column
+// kg): 8 consecutive items take rows 8j..8j+7 at one kg, so their 16-byte
+// stores into the canonical K-major tile fill one 128-byte core matrix
+// (no shared-memory bank conflicts); a warp covers 8 rows x 32 columns.
+SCAO_DEV void a_item(int item, int& r, int& kg) {
+    r = (item & 7) + ((item >> 6) << 3);
+    kg = ((item >> 3) & 7) * 8;
+}
+
 // Pre-split an n x s operand of the factor products (subspace problems) into
 // its image: per 64-row chunk the three bf16 parts in the MN-major canonical
 // layout the GEMM stages, so the GEMM copies each chunk with one bulk copy
@@ -483,7 +503,7 @@ eig_tc_gemm_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, EgSpec g) {
     unsigned char* sm = (unsigned char*)(((uintptr_t)eg_smem_raw + 1023) & ~(uintptr_t)1023);
     const uint32_t bpart = eg_bpart(npad);
     const uint32_t stage = (uint32_t)na * EG_APART + 3 * bpart;
-    __shared__ uint64_t mbar[2], fullb[2];
+    __shared__ uint64_t mbar[EG_MAXST], fullb[EG_MAXST];
     __shared__ uint32_t tslot;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t tcols = npad <= 32 ? 32 : npad <= 64 ? 64 : npad <= 128 ? 128 : 256;
@@ -491,14 +511,16 @@ eig_tc_gemm_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, EgSpec g) {
     const bool bimg = g.b_img && !(flags_of(p) & F_DIRECT);
     const unsigned char* img = P.eig_img + (int64_t)(2 * p.leaf + p.side) * P.eig_img_stride;
     const uint32_t bbytes = 3 * bpart;
+    // both operands by bulk copies (int8 factor, rows 16-byte aligned)
+    const bool stream = i8 && bimg && !g.trans_a && (p.n & 15) == 0 && (p.facoff & 15) == 0;
     if (warp == 0) tc_alloc(&tslot, tcols);
     if (tid == 0) {
-        mbar_init(&mbar[0], 1);
-        mbar_init(&mbar[1], 1);
-        mbar_init(&fullb[0], 1);
-        mbar_init(&fullb[1], 1);
+        for (int i = 0; i < EG_MAXST; ++i) {
+            mbar_init(&mbar[i], 1);
+            mbar_init(&fullb[i], stream ? NT + 1 : 1);
+        }
         fence_async_smem();
-        if (bimg) {
+        if (bimg && !stream) {
             mbar_expect_tx(&fullb[0], bbytes);
             bulk_g2s(sm + na * EG_APART, img, bbytes, &fullb[0]);
         }
@@ -527,7 +549,8 @@ eig_tc_gemm_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, EgSpec g) {
         for (int it = 0; it < AIT; ++it) {
             const int item = tid + it * NT;
             if (i8) {
-                const int r = item >> 3, kg = (item & 7) * 8;
+                int r, kg;
+                a_item(item, r, kg);
                 const int row = m0 + r, col = k0 + kg;
                 if (row < M && vecQ && col + 8 <= K) {
                     aq[it] = *(const uint2*)(Aq + (int64_t)row * p.n + col);
@@ -541,7 +564,8 @@ eig_tc_gemm_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, EgSpec g) {
                     aq[it] = make_uint2(w[0], w[1]);
                 }
             } else if (!g.trans_a) {
-                const int r = item >> 3, kg = (item & 7) * 8;
+                int r, kg;
+                a_item(item, r, kg);
                 get8(fac ? Af : A, lda, m0 + r, k0 + kg, M, K, vecA, av[it]);
             } else {
                 // A^T: element (m, k) = X[k][m]; 8 consecutive m of row k
@@ -559,100 +583,190 @@ eig_tc_gemm_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, EgSpec g) {
             }
         }
     };
-    load_regs(0);
-    for (int kb = 0; kb < nkb; ++kb) {
-        // ---- wait until the MMAs of chunk kb-2 released this stage ----
-        const int st = kb & 1;
-        if (kb >= 2) ok = mbar_wait(&mbar[st], ((kb - 2) >> 1) & 1) && ok;
-        unsigned char* sa = sm + st * stage;
-        unsigned char* sb = sa + na * EG_APART;
+    if (stream) {
+        // two bf16 A tiles, then a ring of nst stages [B image chunk | A int8
+        // rows]; nst - 1 chunks in flight, all threads convert A into the A
+        // tile of the chunk's parity, one thread issues the MMAs and commits
+        // them to the stage's empty barrier
+        unsigned char* ring = sm + 2 * EG_APART;
+        const uint32_t a8 = bbytes;
+        const uint32_t stage2 = a8 + EG_BM * EG_SROW;
+        int nst = (int)((EG_SMEM_STREAM - 1024 - 2 * EG_APART) / stage2);
+        nst = nst > EG_MAXST ? EG_MAXST : nst;
+        const int rows_a = min(EG_BM, M - m0);
+        // A: 16-byte asynchronous copies by every thread, whose completion
+        // arrives on the stage's full barrier (NT arrivals); B: one bulk copy
+        // of its image chunk (one arrival with its byte count)
+        auto produce_a = [&](int kb) {            // every thread
+            const int s_ = kb % nst;
+            unsigned char* dst = ring + s_ * stage2 + a8;
+            const int k0 = kb * EG_BK;
+            // columns past K keep stale int8 codes: finite, and the B image
+            // rows past K are zero; rows past M are never stored
+            for (int c = tid; c < EG_BM * (EG_BK / 16); c += NT) {
+                const int r = c >> 2, seg = (c & 3) * 16;
+                if (r < rows_a && k0 + seg < K)
+                    cp_async16(dst + r * EG_SROW + seg, Aq + (int64_t)(m0 + r) * p.n + k0 + seg);
+            }
+            cp_async_arrive_noinc(&fullb[s_]);
+        };
+        auto produce_b = [&](int kb) {            // thread 0
+            const int s_ = kb % nst;
+            mbar_expect_tx(&fullb[s_], bbytes);
+            bulk_g2s(ring + s_ * stage2, img + (size_t)kb * bbytes, bbytes, &fullb[s_]);
+        };
+        for (int j = 0; j < nst - 1 && j < nkb; ++j) {
+            produce_a(j);
+            if (tid == 0) produce_b(j);
+        }
+        for (int kb = 0; kb < nkb; ++kb) {
+            const int st = kb % nst;
+            unsigned char* base = ring + st * stage2;
+            unsigned char* sa = sm + (kb & 1) * EG_APART;
+            ok = mbar_wait(&fullb[st], (kb / nst) & 1) && ok;
+            // the A tile of this parity was read by the MMAs of chunk kb - 2
+            if (kb >= 2) ok = mbar_wait(&mbar[(kb - 2) % nst], ((kb - 2) / nst) & 1) && ok;
 #pragma unroll
-        for (int it = 0; it < AIT; ++it) {
-            const int item = tid + it * NT;
-            if (i8) {
-                const int r = item >> 3, kg = (item & 7) * 8;
+            for (int it = 0; it < AIT; ++it) {
+                const int item = tid + it * NT;
+                int r, kg;
+                a_item(item, r, kg);
+                const uint2 wq = *(const uint2*)(base + a8 + r * EG_SROW + kg);
+                const uint32_t w[2] = {wq.x, wq.y};
                 uint16_t h[8];
-                const uint32_t w[2] = {aq[it].x, aq[it].y};
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const int8_t q = (int8_t)((w[i >> 2] >> ((i & 3) * 8)) & 0xFF);
-                    h[i] = i8_to_bf16(q);
-                }
+                for (int i = 0; i < 8; ++i)
+                    h[i] = i8_to_bf16((int8_t)((w[i >> 2] >> ((i & 3) * 8)) & 0xFF));
                 uint4 H;
                 H.x = h[0] | ((uint32_t)h[1] << 16); H.y = h[2] | ((uint32_t)h[3] << 16);
                 H.z = h[4] | ((uint32_t)h[5] << 16); H.w = h[6] | ((uint32_t)h[7] << 16);
                 *(uint4*)(sa + canon_off(r, kg, EG_BK)) = H;
-            } else if (!g.trans_a) {
-                const int r = item >> 3, kg = (item & 7) * 8;
-                put8(sa, EG_APART, canon_off(r, kg, EG_BK), av[it]);
-            } else {
-                const int kk = (item & 7) + 8 * (item >> 7), mg = ((item >> 3) & 15) * 8;
-                put8(sa, EG_APART, canon_off_mn(mg, kk, EG_BM), av[it]);
             }
-        }
+            fence_async_smem();
+            tc_fence_before();
+            __syncthreads();
+            tc_fence_after();
+            if (tid == 0) {
+                const uint32_t a0 = smem_u32(sa), b0 = smem_u32(base);
 #pragma unroll
-        for (int it = 0; it < BIT; ++it) {
-            const int item = tid + it * NT;
-            if (!bimg && item < nbi) {
-                const int nb8 = npad >> 3;   // 8 threads fill one 128-byte core matrix
-                const int kk = (item & 7) + 8 * ((item >> 3) / nb8), ng = ((item >> 3) % nb8) * 8;
-                put8(sb, bpart, canon_off_mn(ng, kk, npad), bv[it]);
+                for (int ks = 0; ks < EG_BK / 16; ++ks) {
+                    const uint64_t ad = smem_desc(a0 + ks * 256, 128, 16 * EG_BK);
+                    const uint32_t boff = (uint32_t)ks * 2 * 16 * npad;
+                    const uint32_t acc0 = (kb > 0 || ks > 0) ? 1u : 0u;
+                    tc_mma_bf16(tmem, ad, smem_desc(b0 + boff, 16 * npad, 128), idesc, acc0);
+                    tc_mma_bf16(tmem, ad, smem_desc(b0 + bpart + boff, 16 * npad, 128), idesc, 1u);
+                    tc_mma_bf16(tmem, ad, smem_desc(b0 + 2 * bpart + boff, 16 * npad, 128), idesc, 1u);
+                }
+                tc_commit(&mbar[st]);
             }
-        }
-        // the registers are free again: start the next chunk's loads
-        if (kb + 1 < nkb) load_regs(kb + 1);
-        if (bimg) ok = mbar_wait(&fullb[st], (kb >> 1) & 1) && ok;
-        fence_async_smem();
-        tc_fence_before();
-        __syncthreads();
-        tc_fence_after();
-        if (tid == 0) {
-            const uint32_t a0 = smem_u32(sa), b0 = smem_u32(sb);
-#pragma unroll
-            for (int ks = 0; ks < EG_BK / 16; ++ks) {
-                const uint32_t aoff = g.trans_a ? (uint32_t)ks * 2 * 16 * EG_BM : (uint32_t)ks * 256;
-                const uint32_t boff = (uint32_t)ks * 2 * 16 * npad;
-                auto adesc = [&](int part) {
-                    const uint32_t a = a0 + part * EG_APART + aoff;
-                    return g.trans_a ? smem_desc(a, 16 * EG_BM, 128) : smem_desc(a, 128, 16 * EG_BK);
-                };
-                auto bdesc = [&](int part) {
-                    return smem_desc(b0 + part * bpart + boff, 16 * npad, 128);
-                };
-                const uint32_t acc0 = (kb > 0 || ks > 0) ? 1u : 0u;
-                if (i8) {
-                    tc_mma_bf16(tmem, adesc(0), bdesc(0), idesc, acc0);
-                    tc_mma_bf16(tmem, adesc(0), bdesc(1), idesc, 1u);
-                    tc_mma_bf16(tmem, adesc(0), bdesc(2), idesc, 1u);
-                } else {
-                    tc_mma_bf16(tmem, adesc(0), bdesc(0), idesc, acc0);
-                    tc_mma_bf16(tmem, adesc(0), bdesc(1), idesc, 1u);
-                    tc_mma_bf16(tmem, adesc(1), bdesc(0), idesc, 1u);
-                    tc_mma_bf16(tmem, adesc(0), bdesc(2), idesc, 1u);
-                    tc_mma_bf16(tmem, adesc(1), bdesc(1), idesc, 1u);
-                    tc_mma_bf16(tmem, adesc(2), bdesc(0), idesc, 1u);
+            // refill the stage of chunk kb - 1: its int8 rows were converted
+            // before this iteration's barrier; its B part once its MMAs completed
+            if (kb + nst - 1 < nkb) {
+                produce_a(kb + nst - 1);
+                if (tid == 0) {
+                    if (kb >= 1) ok = mbar_wait(&mbar[(kb - 1) % nst], ((kb - 1) / nst) & 1) && ok;
+                    produce_b(kb + nst - 1);
                 }
             }
-            tc_commit(&mbar[st]);
-            // prefetch chunk kb+1 of B into the other stage once the MMAs of
-            // chunk kb-1 have released it
-            if (bimg && kb + 1 < nkb) {
-                const int s1 = (kb + 1) & 1;
-                if (kb >= 1) ok = mbar_wait(&mbar[s1], ((kb - 1) >> 1) & 1) && ok;
-                mbar_expect_tx(&fullb[s1], bbytes);
-                bulk_g2s(sm + s1 * stage + na * EG_APART, img + (size_t)(kb + 1) * bbytes, bbytes,
-                         &fullb[s1]);
+        }
+        ok = mbar_wait(&mbar[(nkb - 1) % nst], ((nkb - 1) / nst) & 1) && ok;
+    } else {
+        load_regs(0);
+        for (int kb = 0; kb < nkb; ++kb) {
+            // ---- wait until the MMAs of chunk kb-2 released this stage ----
+            const int st = kb & 1;
+            if (kb >= 2) ok = mbar_wait(&mbar[st], ((kb - 2) >> 1) & 1) && ok;
+            unsigned char* sa = sm + st * stage;
+            unsigned char* sb = sa + na * EG_APART;
+    #pragma unroll
+            for (int it = 0; it < AIT; ++it) {
+                const int item = tid + it * NT;
+                if (i8) {
+                    int r, kg;
+                    a_item(item, r, kg);
+                    uint16_t h[8];
+                    const uint32_t w[2] = {aq[it].x, aq[it].y};
+    #pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const int8_t q = (int8_t)((w[i >> 2] >> ((i & 3) * 8)) & 0xFF);
+                        h[i] = i8_to_bf16(q);
+                    }
+                    uint4 H;
+                    H.x = h[0] | ((uint32_t)h[1] << 16); H.y = h[2] | ((uint32_t)h[3] << 16);
+                    H.z = h[4] | ((uint32_t)h[5] << 16); H.w = h[6] | ((uint32_t)h[7] << 16);
+                    *(uint4*)(sa + canon_off(r, kg, EG_BK)) = H;
+                } else if (!g.trans_a) {
+                    int r, kg;
+                    a_item(item, r, kg);
+                    put8(sa, EG_APART, canon_off(r, kg, EG_BK), av[it]);
+                } else {
+                    const int kk = (item & 7) + 8 * (item >> 7), mg = ((item >> 3) & 15) * 8;
+                    put8(sa, EG_APART, canon_off_mn(mg, kk, EG_BM), av[it]);
+                }
+            }
+    #pragma unroll
+            for (int it = 0; it < BIT; ++it) {
+                const int item = tid + it * NT;
+                if (!bimg && item < nbi) {
+                    const int nb8 = npad >> 3;   // 8 threads fill one 128-byte core matrix
+                    const int kk = (item & 7) + 8 * ((item >> 3) / nb8), ng = ((item >> 3) % nb8) * 8;
+                    put8(sb, bpart, canon_off_mn(ng, kk, npad), bv[it]);
+                }
+            }
+            // the registers are free again: start the next chunk's loads
+            if (kb + 1 < nkb) load_regs(kb + 1);
+            if (bimg) ok = mbar_wait(&fullb[st], (kb >> 1) & 1) && ok;
+            fence_async_smem();
+            tc_fence_before();
+            __syncthreads();
+            tc_fence_after();
+            if (tid == 0) {
+                const uint32_t a0 = smem_u32(sa), b0 = smem_u32(sb);
+    #pragma unroll
+                for (int ks = 0; ks < EG_BK / 16; ++ks) {
+                    const uint32_t aoff = g.trans_a ? (uint32_t)ks * 2 * 16 * EG_BM : (uint32_t)ks * 256;
+                    const uint32_t boff = (uint32_t)ks * 2 * 16 * npad;
+                    auto adesc = [&](int part) {
+                        const uint32_t a = a0 + part * EG_APART + aoff;
+                        return g.trans_a ? smem_desc(a, 16 * EG_BM, 128) : smem_desc(a, 128, 16 * EG_BK);
+                    };
+                    auto bdesc = [&](int part) {
+                        return smem_desc(b0 + part * bpart + boff, 16 * npad, 128);
+                    };
+                    const uint32_t acc0 = (kb > 0 || ks > 0) ? 1u : 0u;
+                    if (i8) {
+                        tc_mma_bf16(tmem, adesc(0), bdesc(0), idesc, acc0);
+                        tc_mma_bf16(tmem, adesc(0), bdesc(1), idesc, 1u);
+                        tc_mma_bf16(tmem, adesc(0), bdesc(2), idesc, 1u);
+                    } else {
+                        tc_mma_bf16(tmem, adesc(0), bdesc(0), idesc, acc0);
+                        tc_mma_bf16(tmem, adesc(0), bdesc(1), idesc, 1u);
+                        tc_mma_bf16(tmem, adesc(1), bdesc(0), idesc, 1u);
+                        tc_mma_bf16(tmem, adesc(0), bdesc(2), idesc, 1u);
+                        tc_mma_bf16(tmem, adesc(1), bdesc(1), idesc, 1u);
+                        tc_mma_bf16(tmem, adesc(2), bdesc(0), idesc, 1u);
+                    }
+                }
+                tc_commit(&mbar[st]);
+                // prefetch chunk kb+1 of B into the other stage once the MMAs of
+                // chunk kb-1 have released it
+                if (bimg && kb + 1 < nkb) {
+                    const int s1 = (kb + 1) & 1;
+                    if (kb >= 1) ok = mbar_wait(&mbar[s1], ((kb - 1) >> 1) & 1) && ok;
+                    mbar_expect_tx(&fullb[s1], bbytes);
+                    bulk_g2s(sm + s1 * stage + na * EG_APART, img + (size_t)(kb + 1) * bbytes, bbytes,
+                             &fullb[s1]);
+                }
             }
         }
+        ok = mbar_wait(&mbar[(nkb - 1) & 1], ((nkb - 1) >> 1) & 1) && ok;
     }
-    ok = mbar_wait(&mbar[(nkb - 1) & 1], ((nkb - 1) >> 1) & 1) && ok;
     if (!ok && P.err) atomicExch(P.err, 1);
     tc_fence_after();
     __syncthreads();
 
     // ---- epilogue: TMEM lane = row of the tile ----
     const int q = warp & 3, half = warp >> 2;
-    const int r = m0 + q * 32 + lane;
     const bool fail = g.fail_x && (flags_of(p) & F_CHOLFAIL);
     const float* X = P.eig_x + p.uoff;
     float dscale = 1.f, eps = 0.f;
@@ -667,25 +781,36 @@ eig_tc_gemm_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, EgSpec g) {
         cheb_coef(p.aux, g.cheb_i, al, be, ga);
         Prev = buf_ptr(P, p, g.prev, &ldp);
     }
+    // TMEM -> shared tile (row stride npad + 4 floats: the float4 stores of
+    // 8 consecutive lanes fall in distinct banks), then row-contiguous,
+    // coalesced reads of B / Prev and stores of C by all warps.  Every MMA and
+    // bulk copy has completed, so the stage memory is free (after a timed-out
+    // wait the tile is not read: the output is zero and the error flag set).
+    float* T = (float*)sm;
+    const int ts = npad + 4;
     const int cw = npad >> 1;                           // columns per warp half (multiple of 8)
     for (int c0 = half * cw; c0 < half * cw + cw; c0 += 8) {
         float v[8];
         tc_ld8(tmem + ((uint32_t)(q * 32) << 16) + c0, v);
-        if (r < M) {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int c = c0 + j;
-                if (c >= N) continue;
-                float out = ok ? v[j] : 0.f;
-                if (g.epi != EPI_STORE) {
-                    const float bcur = B[(int64_t)r * ldb + c];
-                    out = fmaf(out, dscale, eps * bcur);
-                    if (g.epi == EPI_CHEB)
-                        out = fmaf(al, out, fmaf(be, bcur, ga * Prev[(int64_t)r * ldp + c]));
-                }
-                if (fail) out = X[(int64_t)r * p.s + c];
-                C[(int64_t)r * ldc + c] = out;
+        float* t = T + (q * 32 + lane) * ts + c0;
+        *(float4*)t = make_float4(v[0], v[1], v[2], v[3]);
+        *(float4*)(t + 4) = make_float4(v[4], v[5], v[6], v[7]);
+    }
+    tc_fence_before();
+    __syncthreads();
+    const int rows = min(EG_BM, M - m0);
+    for (int rr = warp; rr < rows; rr += NT / 32) {
+        const int r = m0 + rr;
+        for (int c = lane; c < N; c += 32) {
+            float out = ok ? T[rr * ts + c] : 0.f;
+            if (g.epi != EPI_STORE) {
+                const float bcur = B[(int64_t)r * ldb + c];
+                out = fmaf(out, dscale, eps * bcur);
+                if (g.epi == EPI_CHEB)
+                    out = fmaf(al, out, fmaf(be, bcur, ga * Prev[(int64_t)r * ldp + c]));
             }
+            if (fail) out = X[(int64_t)r * p.s + c];
+            C[(int64_t)r * ldc + c] = out;
         }
     }
     tc_fence_before();
@@ -760,27 +885,35 @@ eig_jacobi_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, int max_sweeps
                 cs[t] = c; sn[t] = sv;
             }
             __syncthreads();
-            // rows: H <- J^T H
-            for (int e = threadIdx.x; e < half * se; e += blockDim.x) {
-                const int t = e / se, k = e % se;
-                const int P0 = pp[t], Q0 = qq[t];
-                const float c = cs[t], sv = sn[t];
-                const float hp = H[P0 * ld + k], hq = H[Q0 * ld + k];
-                H[P0 * ld + k] = c * hp - sv * hq;
-                H[Q0 * ld + k] = sv * hp + c * hq;
+            // H <- J^T H J and V <- V J in one pass: the rotations of a round
+            // act on disjoint index pairs, so each 2 x 2 block (rows p1,q1 of
+            // pair t1; cols p2,q2 of pair t2) is updated from its own four
+            // entries, rows first, then columns
+            const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+            for (int t1 = warp; t1 < half; t1 += blockDim.x >> 5) {
+                const int P1 = pp[t1], Q1 = qq[t1];
+                const float c1 = cs[t1], s1 = sn[t1];
+                for (int t2 = lane; t2 < half; t2 += 32) {
+                    const int P2 = pp[t2], Q2 = qq[t2];
+                    const float c2 = cs[t2], s2 = sn[t2];
+                    const float hpp = H[P1 * ld + P2], hpq = H[P1 * ld + Q2];
+                    const float hqp = H[Q1 * ld + P2], hqq = H[Q1 * ld + Q2];
+                    const float rpp = c1 * hpp - s1 * hqp, rqp = s1 * hpp + c1 * hqp;
+                    const float rpq = c1 * hpq - s1 * hqq, rqq = s1 * hpq + c1 * hqq;
+                    H[P1 * ld + P2] = c2 * rpp - s2 * rpq;
+                    H[P1 * ld + Q2] = s2 * rpp + c2 * rpq;
+                    H[Q1 * ld + P2] = c2 * rqp - s2 * rqq;
+                    H[Q1 * ld + Q2] = s2 * rqp + c2 * rqq;
+                }
             }
-            __syncthreads();
-            // cols: H <- H J, V <- V J
-            for (int e = threadIdx.x; e < half * se; e += blockDim.x) {
-                const int t = e / se, k = e % se;
-                const int P0 = pp[t], Q0 = qq[t];
-                const float c = cs[t], sv = sn[t];
-                const float hp = H[k * ld + P0], hq = H[k * ld + Q0];
-                H[k * ld + P0] = c * hp - sv * hq;
-                H[k * ld + Q0] = sv * hp + c * hq;
-                const float vp = V[k * ld + P0], vq = V[k * ld + Q0];
-                V[k * ld + P0] = c * vp - sv * vq;
-                V[k * ld + Q0] = sv * vp + c * vq;
+            for (int k = warp; k < se; k += blockDim.x >> 5) {
+                for (int t = lane; t < half; t += 32) {
+                    const int P0 = pp[t], Q0 = qq[t];
+                    const float c = cs[t], sv = sn[t];
+                    const float vp = V[k * ld + P0], vq = V[k * ld + Q0];
+                    V[k * ld + P0] = c * vp - sv * vq;
+                    V[k * ld + Q0] = sv * vp + c * vq;
+                }
             }
             __syncthreads();
         }
@@ -1216,7 +1349,7 @@ extern "C" int scao_plan_eigen(const ScaoPlanDev* P, const int32_t* leaf_ids, in
         cudaFuncSetAttribute(eig_cholinv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)cholinv_smem(SMAX));
         cudaFuncSetAttribute(eig_tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)eg_smem(false));
+                             (int)std::max(eg_smem(false), eg_smem(true)));
     }
     if (max_iters > 0 && getenv("SCAO_EIG_NOGRAPH")) {
         // diagnostic: the same kernels launched directly, every iteration up

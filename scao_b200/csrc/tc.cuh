@@ -137,6 +137,18 @@ TC_DEV void bulk_g2s(void* dst_smem, const void* src_gmem, uint32_t bytes, uint6
         :: "r"(smem_u32(dst_smem)), "l"(src_gmem), "r"(bytes), "r"(smem_u32(mbar)) : "memory");
 }
 
+// 16-byte asynchronous global -> shared copy (L2 only), and an arrival on an
+// mbarrier once all of this thread's earlier asynchronous copies completed
+// (noinc: the arrival counts toward the barrier's initial count)
+TC_DEV void cp_async16(void* dst_smem, const void* src_gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+                 :: "r"(smem_u32(dst_smem)), "l"(src_gmem) : "memory");
+}
+TC_DEV void cp_async_arrive_noinc(uint64_t* mbar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];"
+                 :: "r"(smem_u32(mbar)) : "memory");
+}
+
 // TMA tensor copy of one 2-D box (coordinates x = innermost) into shared
 // memory, completion counted on an mbarrier.  No multicast.
 TC_DEV void tma_load_2d(uint32_t dst, const void* map, int x, int y, uint64_t* mbar) {
