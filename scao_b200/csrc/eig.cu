@@ -798,19 +798,37 @@ eig_tc_gemm_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, EgSpec g) {
     }
     tc_fence_before();
     __syncthreads();
+    // 4 rows per warp step, up to EP_C columns per lane: every load of a
+    // step (B, Prev) is issued before its stores, so a warp waits one memory
+    // latency per step instead of one per element
+    constexpr int EP_R = 4, EP_C = (EG_NPMAX + 31) / 32;
     const int rows = min(EG_BM, M - m0);
-    for (int rr = warp; rr < rows; rr += NT / 32) {
-        const int r = m0 + rr;
-        for (int c = lane; c < N; c += 32) {
-            float out = ok ? T[rr * ts + c] : 0.f;
-            if (g.epi != EPI_STORE) {
-                const float bcur = B[(int64_t)r * ldb + c];
-                out = fmaf(out, dscale, eps * bcur);
-                if (g.epi == EPI_CHEB)
-                    out = fmaf(al, out, fmaf(be, bcur, ga * Prev[(int64_t)r * ldp + c]));
+    for (int rr0 = warp * EP_R; rr0 < rows; rr0 += EP_R * (NT / 32)) {
+        float bc[EP_R][EP_C], pv[EP_R][EP_C];
+#pragma unroll
+        for (int i = 0; i < EP_R; ++i) {
+#pragma unroll
+            for (int j = 0; j < EP_C; ++j) {
+                const int r = m0 + rr0 + i, c = lane + 32 * j;
+                const bool in = rr0 + i < rows && c < N;
+                bc[i][j] = (g.epi != EPI_STORE && in) ? B[(int64_t)r * ldb + c] : 0.f;
+                pv[i][j] = (g.epi == EPI_CHEB && in) ? Prev[(int64_t)r * ldp + c] : 0.f;
             }
-            if (fail) out = X[(int64_t)r * p.s + c];
-            C[(int64_t)r * ldc + c] = out;
+        }
+#pragma unroll
+        for (int i = 0; i < EP_R; ++i) {
+#pragma unroll
+            for (int j = 0; j < EP_C; ++j) {
+                const int rr = rr0 + i, r = m0 + rr, c = lane + 32 * j;
+                if (rr >= rows || c >= N) continue;
+                float out = ok ? T[rr * ts + c] : 0.f;
+                if (g.epi != EPI_STORE) {
+                    out = fmaf(out, dscale, eps * bc[i][j]);
+                    if (g.epi == EPI_CHEB) out = fmaf(al, out, fmaf(be, bc[i][j], ga * pv[i][j]));
+                }
+                if (fail) out = X[(int64_t)r * p.s + c];
+                C[(int64_t)r * ldc + c] = out;
+            }
         }
     }
     tc_fence_before();
@@ -961,17 +979,38 @@ __global__ void eig_residual_kernel(ScaoPlanDev P, const int32_t* __restrict__ i
     const float bulk = ths >= 0.f ? (1.f + CLUSTER_FRAC) * ths : ths;
     __shared__ float rr[SMAX];
     __shared__ int sconv;
-    // one warp per column
+    // rows over warps, columns over lanes (row-contiguous, coalesced reads);
+    // per-warp partial sums reduced in shared memory
+    __shared__ float part[NT / 32][SMAX];
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    for (int c = wid; c < kc; c += nw) {
-        const float th = ev[c];
-        float r2 = 0.f;
-        for (int i = lane; i < p.n; i += 32) {
-            const float d = AX[(int64_t)i * s + c] - th * X[(int64_t)i * s + c];
-            r2 += d * d;
+    constexpr int RC = (SMAX + 31) / 32;
+    float thc[RC], acc[RC];
+#pragma unroll
+    for (int j = 0; j < RC; ++j) {
+        const int c = lane + 32 * j;
+        thc[j] = c < kc ? ev[c] : 0.f;
+        acc[j] = 0.f;
+    }
+    for (int i = wid; i < p.n; i += nw) {
+#pragma unroll
+        for (int j = 0; j < RC; ++j) {
+            const int c = lane + 32 * j;
+            if (c < kc) {
+                const float d = AX[(int64_t)i * s + c] - thc[j] * X[(int64_t)i * s + c];
+                acc[j] = fmaf(d, d, acc[j]);
+            }
         }
-        r2 = warp_sum(r2);
-        if (lane == 0) rr[c] = sqrtf(r2);
+    }
+#pragma unroll
+    for (int j = 0; j < RC; ++j) {
+        const int c = lane + 32 * j;
+        if (c < kc) part[wid][c] = acc[j];
+    }
+    __syncthreads();
+    for (int c = threadIdx.x; c < kc; c += blockDim.x) {
+        float r2 = 0.f;
+        for (int w = 0; w < nw; ++w) r2 += part[w][c];
+        rr[c] = sqrtf(r2);
     }
     __syncthreads();
     // Convergence.  From the third outer iteration on, a pair within
