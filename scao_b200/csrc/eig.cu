@@ -798,10 +798,10 @@ eig_tc_gemm_kernel(ScaoPlanDev P, const int32_t* __restrict__ ids, EgSpec g) {
     }
     tc_fence_before();
     __syncthreads();
-    // 4 rows per warp step, up to EP_C columns per lane: every load of a
+    // EP_R rows per warp step, up to EP_C columns per lane: every load of a
     // step (B, Prev) is issued before its stores, so a warp waits one memory
     // latency per step instead of one per element
-    constexpr int EP_R = 4, EP_C = (EG_NPMAX + 31) / 32;
+    constexpr int EP_R = 8, EP_C = (EG_NPMAX + 31) / 32;
     const int rows = min(EG_BM, M - m0);
     for (int rr0 = warp * EP_R; rr0 < rows; rr0 += EP_R * (NT / 32)) {
         float bc[EP_R][EP_C], pv[EP_R][EP_C];
