@@ -154,7 +154,8 @@ def reference_arm(workload, steps, warmup, device="cpu", layers=1):
     are primed through the 20 Adam-warmup steps + ``warmup`` steps untimed,
     then ``steps`` steps are timed (same global steps, hence the same
     curvature cadence, as the GPU arm); a step of the full set is
-    t(embedding part) + (16 / layers) * t(layer sample)."""
+    t(non-layer part) + (layer count / layers) * t(layer sample), the first
+    term absent when every parameter belongs to a layer."""
     ref = os.path.join(ROOT, "baseline", "_ref")
     if not os.path.isfile(os.path.join(ref, "scao", "__init__.py")):
         return None
@@ -169,20 +170,23 @@ def reference_arm(workload, steps, warmup, device="cpu", layers=1):
     if device == "cpu":
         torch.set_num_threads(threads)
     w_e, w_l, n_layers = sample_split(workload, layers)
+    scale = n_layers / layers
     samples = []
-    for w_s in (w_e, w_l):
+    for w_s, weight in ((w_e, 1.0), (w_l, scale)):
+        if not w_s.params:                  # e.g. no parameters outside the layers
+            continue
         p0 = synthetic.init_params(w_s, device=device)
         params = [torch.nn.Parameter(p) for p in p0]
         opt = build_opt(w_s, params, scao.SCAO)
         gen = synthetic.LowRankGradients(w_s, device=device)
         sets = [gen.next() for _ in range(3)]
-        samples.append((params, opt, sets))
+        samples.append((params, opt, sets, weight))
     pf = workload.scao_kwargs["precond_freq"]
     n_prime = workload.scao_kwargs["warmup_steps"] + warmup
 
     def one(k):
-        out = []
-        for params, opt, sets in samples:
+        t = 0.0
+        for params, opt, sets, weight in samples:
             for p, g in zip(params, sets[k % 3]):
                 p.grad = g
             if device != "cpu":
@@ -191,16 +195,14 @@ def reference_arm(workload, steps, warmup, device="cpu", layers=1):
             opt.step()
             if device != "cpu":
                 torch.cuda.synchronize()
-            out.append((time.perf_counter() - t0) * 1e3)
-        return out
+            t += weight * (time.perf_counter() - t0) * 1e3
+        return t
 
     for k in range(n_prime):
         one(k)
     per, curv = [], []
-    scale = n_layers / layers
     for k in range(steps):
-        te, tl = one(n_prime + k)
-        per.append(te + scale * tl)
+        per.append(one(n_prime + k))
         curv.append((n_prime + k + 1) % pf == 0)
     reg = [t for t, c in zip(per, curv) if not c]
     cur = [t for t, c in zip(per, curv) if c]
